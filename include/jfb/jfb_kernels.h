@@ -1,0 +1,164 @@
+/*
+ * jfb kernel library: the hand-written sm_100a kernels of the native Qwen2
+ * stage engine behind a thin C ABI.
+ *
+ * Conventions: every pointer argument is a device pointer unless its name ends
+ * in _host; sizes are element counts; `stream` is a cudaStream_t passed as
+ * void* (NULL = the legacy default stream); every call validates its shapes on
+ * the host and returns a jfb_status instead of throwing. Nothing here
+ * allocates device memory: scratch buffers are caller-owned, and their
+ * required sizes are returned by the *_scratch_bytes queries.
+ *
+ * Each entry point replaces one GGML op (or a chain of them) of the reference
+ * graph runtime/engines/native/src/qwen2_architecture.cpp; the op it replaces
+ * is cited on its declaration. The reference has no C ABI at this level (it
+ * calls into GGML), so these signatures are new; the engine ABI in
+ * jfb_engine.h is the drop-in boundary.
+ */
+#ifndef JFB_KERNELS_H
+#define JFB_KERNELS_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include "jfb/jfb_status.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* A weight matrix resident in HBM in the engine's planar layout.
+ * rows = output features (GGML ne1), cols = input features (GGML ne0).
+ *   F32, F16 : plane[0] = [rows][cols] values (GGML layout, unchanged)
+ *   Q4_K     : plane[0] = [rows][cols/256][128] 4-bit codes,
+ *              plane[1] = [rows][cols/256][16]  f16 d, f16 dmin, 12 scale bytes
+ *   Q6_K     : plane[0] = [rows][cols/256][192] ql (128 B) then qh (64 B),
+ *              plane[1] = [rows][cols/256][16]  int8 scales,
+ *              plane[2] = [rows][cols/256]      f16 d
+ *   Q2_K     : plane[0] = [rows][cols/256][64]  2-bit codes,
+ *              plane[1] = [rows][cols/256][16]  scale | min << 4 bytes,
+ *              plane[2] = [rows][cols/256][2]   f16 d, f16 dmin
+ * The bytes inside each plane are the GGML block bytes, only regrouped, so
+ * dequantized values are bit-identical to GGML's. */
+typedef struct jfb_weight {
+    uint32_t type;      /* JF_TENSOR_* id */
+    uint32_t rows;
+    uint32_t cols;
+    uint32_t reserved;
+    const void * plane[3];
+} jfb_weight;
+
+/* Activations quantized to GGML's Q8_K (per 256 values: f32 d, 256 int8,
+ * 16 int16 partial sums), stored as three planes for [rows][cols]. */
+typedef struct jfb_q8k {
+    int8_t * qs;        /* [rows][cols] */
+    float * d;          /* [rows][cols/256] */
+    int16_t * bsums;    /* [rows][cols/16] */
+} jfb_q8k;
+
+/* Per-sequence KV cache: token-major F16 rows for every resident layer,
+ * K and V in separate buffers laid out [layers][capacity][kv_dim]. The
+ * reference keeps K token-major and V transposed
+ * (qwen2_architecture.cpp:1072-1079); here both are token-major so decode
+ * never re-transposes V. */
+typedef struct jfb_kv_slot {
+    uint16_t * k;
+    uint16_t * v;
+    uint32_t capacity;
+    uint32_t reserved;
+} jfb_kv_slot;
+
+/* Bytes of device memory a weight of this type and shape occupies (all
+ * planes, each plane 256-byte aligned). */
+uint64_t jfb_weight_device_bytes(uint32_t type, uint32_t rows, uint32_t cols);
+
+/* Regroups GGML block bytes (src, device) into the planar layout at dst
+ * (device, jfb_weight_device_bytes long) and fills *weight. */
+jfb_status jfb_weight_repack(uint32_t type, uint32_t rows, uint32_t cols, const void * src, void * dst,
+                             jfb_weight * weight, void * stream);
+
+/* out[rows][cols] = dequantized weight, bit-exact with GGML's dequantize_row_*
+ * (used by get_rows on token_embd, qwen2_architecture.cpp:564-568). */
+jfb_status jfb_dequantize(const jfb_weight * weight, float * out, void * stream);
+
+/* hidden[r][:] = dequantized row tokens[r] of the embedding table
+ * (ggml_get_rows(token_embd, ids), qwen2_architecture.cpp:564-568).
+ * Tokens outside [0, rows) are rejected on the device: the row is zeroed and
+ * *error_flag (may be NULL) is set to 1. */
+jfb_status jfb_embed_rows(const jfb_weight * embd, const int32_t * tokens, uint32_t n, float * hidden,
+                          int32_t * error_flag, void * stream);
+
+/* RMSNorm times weight (ggml_rms_norm + ggml_mul, qwen2_architecture.cpp:373-376)
+ * of rows [n][cols] of x, optionally gathered by row_index (NULL = identity).
+ * Writes the f32 result to out_f32 (may be NULL) and its Q8_K quantization
+ * to out_q8 (may be NULL; cols % 256 == 0). */
+jfb_status jfb_rmsnorm_quant(const float * x, const int32_t * row_index, const float * norm_weight,
+                             uint32_t n, uint32_t cols, float eps, float * out_f32, const jfb_q8k * out_q8,
+                             void * stream);
+
+/* Q8_K quantization of f32 rows (GGML quantize_row_q8_K semantics). */
+jfb_status jfb_quantize_q8k(const float * x, uint32_t n, uint32_t cols, const jfb_q8k * out, void * stream);
+
+/* out[r][i] = silu(gate[r][i]) * up[r][i] (ggml_swiglu_split or silu+mul,
+ * qwen2_architecture.cpp:508-520); also quantizes the result to Q8_K when
+ * out_q8 != NULL. */
+jfb_status jfb_swiglu_quant(const float * gate, const float * up, uint32_t n, uint32_t cols, float * out_f32,
+                            const jfb_q8k * out_q8, void * stream);
+
+/* Epilogue applied to y = W x by jfb_matmul. */
+typedef enum jfb_epilogue {
+    JFB_EPILOGUE_STORE = 0,        /* out = Wx */
+    JFB_EPILOGUE_BIAS = 1,         /* out = Wx + bias */
+    JFB_EPILOGUE_RESIDUAL = 2,     /* out = Wx + residual (out may alias residual) */
+} jfb_epilogue;
+
+/* ggml_mul_mat(W, x) for n activation rows (qwen2_architecture.cpp:361-371):
+ * K-quant weights consume the Q8_K activations (exact integer sub-block dot
+ * products, one float scale per 256-block); F32/F16 weights consume x_f32.
+ * out[r][rows] row-major. */
+jfb_status jfb_matmul(const jfb_weight * weight, const jfb_q8k * x_q8, const float * x_f32, uint32_t n,
+                      uint32_t epilogue, const float * bias, const float * residual, float * out,
+                      void * stream);
+
+/* NEOX rotary embedding of q and k plus the F16 KV-cache append
+ * (ggml_rope_ext NEOX + ggml_set_rows, qwen2_architecture.cpp:400-424,
+ * 499-506). Row r belongs to slots[seq[r]] at absolute position pos[r]; its K
+ * and V rows are written at [layer][pos[r]] of that slot. q is rotated in
+ * place. theta_scale = powf(freq_base, -2/rope_dims), computed by the caller
+ * on the host; the angle of pair i is pos * theta_scale^i built by repeated
+ * float multiplication, as GGML's rope cache does. */
+jfb_status jfb_rope_kv_append(float * q, const float * k, const float * v, uint32_t n, const int32_t * seq,
+                              const int32_t * pos, uint32_t heads, uint32_t kv_heads, uint32_t head_dim,
+                              uint32_t rope_dims, float theta_scale, const jfb_kv_slot * slots,
+                              uint32_t layer, void * stream);
+
+/* Scratch bytes jfb_attention needs for n query rows with at most max_keys
+ * keys each. */
+uint64_t jfb_attention_scratch_bytes(uint32_t n, uint32_t heads, uint32_t head_dim, uint32_t max_keys);
+
+/* Causal GQA attention of query rows over the F16 caches
+ * (qwen2_architecture.cpp:425-470): row r attends keys [0, pos[r]] of
+ * slots[seq[r]] at `layer`; query head h reads kv head h / (heads / kv_heads);
+ * scores are K . f16(q) accumulated in f32, scaled by 1/sqrt(head_dim),
+ * softmax in f32 (online, split over key chunks), output accumulated in f32.
+ * Writes out[r][heads*head_dim] and, when out_q8 != NULL, its Q8_K
+ * quantization. */
+jfb_status jfb_attention(const float * q, uint32_t n, const int32_t * seq, const int32_t * pos, uint32_t heads,
+                         uint32_t kv_heads, uint32_t head_dim, uint32_t max_keys, const jfb_kv_slot * slots,
+                         uint32_t layer, void * scratch, uint64_t scratch_bytes, float * out,
+                         const jfb_q8k * out_q8, void * stream);
+
+/* First index of the maximum of each row (ggml_argmax, qwen2_architecture.cpp:594). */
+jfb_status jfb_argmax(const float * logits, uint32_t n, uint32_t cols, int32_t * out, void * stream);
+
+/* The reference F16 activation codec on the device, bit-exact with
+ * runtime/activation/builtin_activation_codecs.cpp:51-137 (round to nearest
+ * even, NaN payload kept and made quiet). */
+jfb_status jfb_codec_f32_to_f16(const float * in, uint16_t * out, uint64_t count, void * stream);
+jfb_status jfb_codec_f16_to_f32(const uint16_t * in, float * out, uint64_t count, void * stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

@@ -1,0 +1,207 @@
+// Device-resident Qwen2 stage: weight arena (the TensorStore of the
+// reference), per-session KV caches and the batched stage forward pass.
+#pragma once
+
+#include "jetsonfabric/native_inference.hpp"
+#include "jfb/jfb_kernels.h"
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <memory>
+#include <span>
+#include <string>
+#include <vector>
+
+namespace jfb::engine {
+
+using jetsonfabric::native::ModelInfo;
+
+// Qwen2 hyper-parameters (reference qwen2_metadata.hpp / Qwen2HParams).
+struct Qwen2HParams {
+    ModelInfo info;
+    std::uint32_t feed_forward_length = 0;
+    std::uint32_t head_count = 0;
+    std::uint32_t kv_head_count = 0;
+    std::uint32_t rope_dimension_count = 0;
+    float rope_frequency_base = 0.0f;
+    float rms_epsilon = 0.0f;
+
+    std::uint32_t head_dim() const { return info.embedding_length / head_count; }
+    std::uint32_t kv_dim() const { return head_dim() * kv_head_count; }
+};
+
+struct LayerWeights {
+    jfb_weight q{}, k{}, v{}, o{}, gate{}, up{}, down{};
+    const float * attn_norm = nullptr;
+    const float * q_bias = nullptr;
+    const float * k_bias = nullptr;
+    const float * v_bias = nullptr;
+    const float * ffn_norm = nullptr;
+};
+
+// Throws std::runtime_error with `what` and the CUDA error string.
+void cuda_check(cudaError_t e, const char * what);
+// Throws std::runtime_error for a failing jfb_status.
+void jfb_check(const jfb_status & s);
+
+class DeviceModel {
+public:
+    DeviceModel(const std::string & package_path, std::uint32_t layer_start, std::uint32_t layer_end);
+    ~DeviceModel();
+    DeviceModel(const DeviceModel &) = delete;
+    DeviceModel & operator=(const DeviceModel &) = delete;
+
+    const Qwen2HParams & hparams() const { return hp_; }
+    bool first_stage() const { return layer_start_ == 0; }
+    bool last_stage() const { return layer_end_ == hp_.info.layer_count; }
+    std::uint32_t layer_start() const { return layer_start_; }
+    std::uint32_t layer_end() const { return layer_end_; }
+    std::uint32_t layers() const { return layer_end_ - layer_start_; }
+    std::uint32_t vocabulary() const { return vocab_; }
+    int device() const { return device_; }
+    cudaStream_t stream() const { return stream_; }
+
+    const jfb_weight & token_embd() const { return token_embd_; }
+    const jfb_weight & output() const { return output_; }
+    const float * output_norm() const { return output_norm_; }
+    const float * output_bias() const { return output_bias_; }
+    const LayerWeights & layer(std::uint32_t i) const { return layer_weights_[i]; }
+
+    const std::string & source_sha256() const { return source_sha256_; }
+    const std::string & device_name() const { return device_name_; }
+    std::uint64_t weight_bytes() const { return weight_bytes_; }
+    std::uint64_t total_weight_bytes() const { return total_weight_bytes_; }
+    std::uint64_t tensor_count() const { return tensor_count_; }
+    std::uint64_t arena_bytes() const { return arena_bytes_; }
+
+private:
+    Qwen2HParams hp_;
+    std::uint32_t layer_start_ = 0, layer_end_ = 0, vocab_ = 0;
+    int device_ = 0;
+    cudaStream_t stream_ = nullptr;
+    void * arena_ = nullptr;
+    std::uint64_t arena_bytes_ = 0;
+    jfb_weight token_embd_{}, output_{};
+    const float * output_norm_ = nullptr;
+    const float * output_bias_ = nullptr;
+    std::vector<LayerWeights> layer_weights_;
+    std::string source_sha256_, device_name_;
+    std::uint64_t weight_bytes_ = 0, total_weight_bytes_ = 0, tensor_count_ = 0;
+};
+
+// Per-session F16 KV cache: K and V, each [layers][capacity][kv_dim].
+class KvCache {
+public:
+    KvCache(const DeviceModel & model, std::uint32_t capacity);
+    ~KvCache();
+    KvCache(const KvCache &) = delete;
+    KvCache & operator=(const KvCache &) = delete;
+    jfb_kv_slot slot() const { return jfb_kv_slot{k_, v_, capacity_, 0}; }
+    std::uint32_t capacity() const { return capacity_; }
+    std::uint64_t bytes() const { return bytes_; }
+
+private:
+    std::uint16_t * k_ = nullptr;
+    std::uint16_t * v_ = nullptr;
+    std::uint32_t capacity_ = 0;
+    std::uint64_t bytes_ = 0;
+};
+
+// One sequence's slice of a batched forward call: `rows` consecutive rows
+// starting at absolute position `start`.
+struct SequenceRows {
+    const KvCache * cache = nullptr;
+    std::uint32_t start = 0;
+    std::uint32_t rows = 0;
+};
+
+// Where the inputs come from and where the outputs go.
+struct ForwardIo {
+    // inputs (exactly one): token ids of every row, or f32 activations [R][h]
+    const std::int32_t * tokens = nullptr;
+    const float * activations = nullptr;
+    bool inputs_on_device = false;
+    // outputs of a final stage: one greedy token per sequence (host or
+    // device), optionally the last row's logits per sequence [S][V] (host)
+    std::int32_t * tokens_out = nullptr;
+    bool tokens_out_on_device = false;
+    float * logits_out = nullptr;
+    // output of an intermediate stage: activations [R][h] (host or device)
+    float * activations_out = nullptr;
+    bool activations_out_on_device = false;
+    // synchronise the stream before returning (needed for host outputs)
+    bool synchronize = true;
+};
+
+// Per-kernel-family device time and algorithmic bytes of the last forward
+// call made with timing enabled (CUDA events around each launch).
+struct KernelTiming {
+    std::uint64_t matmul_launches = 0;
+    double matmul_ms = 0.0;
+    double matmul_bytes = 0.0;
+    std::uint64_t attention_launches = 0;
+    double attention_ms = 0.0;
+    double attention_bytes = 0.0;
+};
+
+class Qwen2Stage {
+public:
+    explicit Qwen2Stage(DeviceModel & model);
+    ~Qwen2Stage();
+    Qwen2Stage(const Qwen2Stage &) = delete;
+    Qwen2Stage & operator=(const Qwen2Stage &) = delete;
+
+    // Runs the stage over the rows of every sequence (positions must already
+    // be validated by the caller). Launches on model.stream().
+    void forward(std::span<const SequenceRows> seqs, const ForwardIo & io);
+
+    std::uint64_t scratch_bytes() const { return scratch_bytes_; }
+    std::uint64_t kernel_launches() const { return launches_; }
+    void set_timing(bool enabled) { timing_ = enabled; }
+    // Waits for the timed launches of the last forward and sums them up.
+    KernelTiming collect_timing();
+
+private:
+    void ensure_scratch(std::uint32_t rows, std::uint32_t seqs, std::uint32_t max_keys);
+    void free_scratch();
+
+    DeviceModel & m_;
+    // scratch (device)
+    float * hidden_ = nullptr;
+    float * xf_ = nullptr;
+    float * q_ = nullptr;
+    float * k_ = nullptr;
+    float * v_ = nullptr;
+    float * attn_ = nullptr;
+    float * gate_ = nullptr;
+    float * up_ = nullptr;
+    jfb_q8k q8_{};
+    void * attn_scratch_ = nullptr;
+    std::uint64_t attn_scratch_bytes_ = 0;
+    float * logits_ = nullptr;
+    std::int32_t * tokens_dev_ = nullptr;
+    std::int32_t * error_flag_ = nullptr;
+    // per-call metadata: seq[R], pos[R], last_row[S], tokens[R], slots[S]
+    void * meta_dev_ = nullptr;
+    void * meta_host_ = nullptr;
+    std::uint64_t meta_bytes_ = 0;
+    cudaEvent_t meta_uploaded_ = nullptr;  // the pinned staging buffer is free again
+    std::uint32_t cap_rows_ = 0, cap_seqs_ = 0, cap_keys_ = 0;
+    std::uint64_t scratch_bytes_ = 0;
+    std::uint64_t launches_ = 0;
+    // kernel timing
+    struct TimedLaunch {
+        int family;  // 0 matmul, 1 attention
+        double bytes;
+        cudaEvent_t start, stop;
+    };
+    bool timing_ = false;
+    std::vector<TimedLaunch> timed_;
+    std::vector<cudaEvent_t> event_pool_;
+    cudaEvent_t take_event();
+};
+
+Qwen2HParams load_qwen2_hparams(std::span<const std::byte> gguf_metadata);
+
+}  // namespace jfb::engine

@@ -1,0 +1,142 @@
+// Shared helpers of the sm_100a kernel library: status construction, launch
+// checks and the small device-side building blocks (binary16 conversion,
+// Q8_K quantization of one 256-value block, block reductions).
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdint>
+#include <cstdio>
+
+#include "jetsonfabric/engine.h"
+#include "jfb/jfb_kernels.h"
+
+namespace jfb {
+
+constexpr int kQK = 256;  // K-quant / Q8_K super-block length
+
+inline jfb_status status_ok() {
+    jfb_status s;
+    s.code = JFB_STATUS_OK;
+    s.message[0] = '\0';
+    return s;
+}
+
+inline jfb_status status_error(jfb_status_code code, const char * format, ...) {
+    jfb_status s;
+    s.code = code;
+    va_list args;
+    va_start(args, format);
+    std::vsnprintf(s.message, sizeof(s.message), format, args);
+    va_end(args);
+    return s;
+}
+
+inline jfb_status launch_status(const char * what) {
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return status_error(JFB_STATUS_CUDA_ERROR, "%s: %s", what, cudaGetErrorString(e));
+    return status_ok();
+}
+
+inline cudaStream_t as_stream(void * s) { return static_cast<cudaStream_t>(s); }
+
+inline bool is_kquant(uint32_t type) {
+    return type == JF_TENSOR_Q4_K || type == JF_TENSOR_Q6_K || type == JF_TENSOR_Q2_K;
+}
+
+// ---- device helpers --------------------------------------------------------
+
+__device__ __forceinline__ float half_bits_to_float(uint16_t h) {
+    return __half2float(__ushort_as_half(h));
+}
+
+__device__ __forceinline__ uint16_t float_to_half_bits(float f) {
+    return __half_as_ushort(__float2half_rn(f));
+}
+
+// Warp-wide sum.
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ double warp_sum(double v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// (|value| max, first index on ties) reduction key packed for a shuffle: the
+// magnitude's bits (non-negative floats order like their bit patterns) in the
+// high word and the complement of the index in the low word, so a plain
+// unsigned max picks the largest magnitude and, among equals, the smallest
+// index.
+__device__ __forceinline__ unsigned long long amax_key(float magnitude, int index) {
+    return (static_cast<unsigned long long>(__float_as_uint(magnitude)) << 32) |
+           static_cast<unsigned long long>(0xffffffffu - static_cast<unsigned>(index));
+}
+
+__device__ __forceinline__ unsigned long long warp_max_u64(unsigned long long v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long other = __shfl_xor_sync(0xffffffffu, v, o);
+        v = other > v ? other : v;
+    }
+    return v;
+}
+
+// Quantizes one 256-value block held one value per thread by a 256-thread
+// block (thread t holds element t) with GGML's quantize_row_q8_K rule:
+// max = signed value of largest magnitude (first on ties), iscale = -127/max,
+// q = round-half-even(iscale * x) capped at 127, d = 1/iscale, bsums over 16.
+// `shared` must hold 8 unsigned long long + 16 int. Every thread of the block
+// must call it.
+__device__ __forceinline__ void q8k_block_256(float x, int8_t * qs, float * d, int16_t * bsums,
+                                              unsigned long long * shared_keys) {
+    const int t = threadIdx.x;
+    unsigned long long key = warp_max_u64(amax_key(fabsf(x), t));
+    if ((t & 31) == 0) shared_keys[t >> 5] = key;
+    __syncthreads();
+    if (t < 32) {
+        unsigned long long k2 = t < 8 ? shared_keys[t] : 0ull;
+        k2 = warp_max_u64(k2);
+        if (t == 0) shared_keys[0] = k2;
+    }
+    __syncthreads();
+    const unsigned long long best = shared_keys[0];
+    const float amax = __uint_as_float(static_cast<unsigned>(best >> 32));
+    int q = 0;
+    float dval = 0.0f;
+    // All threads read the winner's value by broadcast through a shuffle-free
+    // path: the winner writes it.
+    __shared__ float winner_value;
+    const int winner = static_cast<int>(0xffffffffu - static_cast<unsigned>(best & 0xffffffffull));
+    if (t == winner) winner_value = x;
+    __syncthreads();
+    if (amax != 0.0f) {
+        const float mx = winner_value;
+        const float iscale = __fdiv_rn(-127.0f, mx);
+        const int v = __float2int_rn(__fmul_rn(iscale, x));
+        q = v < 127 ? v : 127;
+        dval = __fdiv_rn(1.0f, iscale);
+    }
+    qs[t] = static_cast<int8_t>(q);
+    // bsums: 16 consecutive values -> half-warp segments
+    int s = q;
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if ((t & 15) == 0) bsums[t >> 4] = static_cast<int16_t>(s);
+    if (t == 0) *d = dval;
+    __syncthreads();  // shared_keys / winner_value reuse safety
+}
+
+}  // namespace jfb

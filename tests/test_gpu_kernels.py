@@ -1,0 +1,273 @@
+"""Kernel-level parity of the sm_100a library against the CPU oracle.
+
+Bit-exact: K-quant dequantization (also against gguf-py), Q8_K activation
+quantization, RMSNorm, the F16 activation codec, argmax.
+Tolerance-based: matmul (integer sub-block sums are exact; only the order of
+the float additions across 256-blocks differs), RoPE + KV append, attention.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import struct
+
+import numpy as np
+import pytest
+
+from jetsonfabric_b200 import jfm
+from oracle import binding as ob
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+KQ = [jfm.JF_TENSOR_Q4_K, jfm.JF_TENSOR_Q6_K, jfm.JF_TENSOR_Q2_K]
+
+
+@pytest.fixture(scope="module")
+def K():
+    if not torch.cuda.is_available():
+        pytest.fail("a CUDA device is required for the gpu tests")
+    from jetsonfabric_b200 import kernels
+    return kernels
+
+
+def make_weight(K, jf_type, rows, cols, seed, std=0.02):
+    rng = np.random.default_rng(seed)
+    values = rng.normal(0, std, rows * cols).astype(np.float32)
+    if jf_type == jfm.JF_TENSOR_F32:
+        raw = values.tobytes()
+    elif jf_type == jfm.JF_TENSOR_F16:
+        raw = values.astype(np.float16).tobytes()
+    else:
+        raw = jfm.quantize_blocks(jf_type, values)
+    return K.DeviceWeight(jf_type, rows, cols, raw), raw
+
+
+@pytest.mark.parametrize("jf_type", KQ + [jfm.JF_TENSOR_F32, jfm.JF_TENSOR_F16])
+def test_dequantize_bit_exact(K, jf_type):
+    rows, cols = 48, 1024
+    w, raw = make_weight(K, jf_type, rows, cols, 1)
+    gpu = w.dequantize().cpu().numpy().ravel()
+    ref = ob.dequantize(jf_type, raw, rows * cols)
+    assert np.array_equal(gpu.view(np.uint32), ref.view(np.uint32))
+    if jf_type in KQ:
+        from gguf.quants import dequantize as gd
+        import gguf
+        gt = {jfm.JF_TENSOR_Q4_K: gguf.GGMLQuantizationType.Q4_K, jfm.JF_TENSOR_Q6_K: gguf.GGMLQuantizationType.Q6_K,
+              jfm.JF_TENSOR_Q2_K: gguf.GGMLQuantizationType.Q2_K}[jf_type]
+        assert np.array_equal(gpu.view(np.uint32), gd(np.frombuffer(raw, np.uint8), gt).ravel().view(np.uint32))
+
+
+def q8_reference(x: np.ndarray):
+    raw = ob.quantize_q8_k(x)
+    return ob.split_q8_k(raw, x.size)
+
+
+def test_quantize_q8k_bit_exact(K):
+    rng = np.random.default_rng(2)
+    rows, cols = 37, 2048
+    x = rng.normal(0, 1, (rows, cols)).astype(np.float32)
+    x[3, :256] = 0.0                                   # zero block
+    x[5, 10], x[5, 20] = 4.0, -4.0                      # magnitude tie
+    x[7] *= 1e-30                                      # tiny values
+    x[9, 300] = 1e6                                    # extreme
+    xt = torch.from_numpy(x).cuda()
+    out = K.Q8Buffer(rows, cols)
+    K.quantize_q8k(xt, out)
+    torch.cuda.synchronize()
+    for r in range(rows):
+        d, qs, bs = q8_reference(x[r])
+        assert np.array_equal(out.qs[r].cpu().numpy(), qs), r
+        assert np.array_equal(out.d[r].cpu().numpy().view(np.uint32), d.view(np.uint32)), r
+        assert np.array_equal(out.bsums[r].cpu().numpy(), bs), r
+
+
+@pytest.mark.parametrize("cols", [4, 1536, 2048, 5120])
+def test_rmsnorm_quant_bit_exact(K, cols):
+    rng = np.random.default_rng(cols)
+    rows = 9
+    x = rng.normal(0, 2, (rows, cols)).astype(np.float32)
+    w = (1 + rng.normal(0, 0.1, cols)).astype(np.float32)
+    xt, wt = torch.from_numpy(x).cuda(), torch.from_numpy(w).cuda()
+    out = torch.empty_like(xt)
+    q8 = K.Q8Buffer(rows, cols) if cols % 256 == 0 else None
+    K.rmsnorm_quant(xt, wt, 1e-6, out_f32=out, out_q8=q8)
+    torch.cuda.synchronize()
+    got = out.cpu().numpy()
+    for r in range(rows):
+        ref = np.empty(cols, np.float32)
+        ob.lib().orc_rms_norm(x[r].ctypes.data, w.ctypes.data, cols, C.c_float(1e-6), ref.ctypes.data)
+        assert np.array_equal(got[r].view(np.uint32), ref.view(np.uint32)), r
+        if q8 is not None:
+            d, qs, bs = q8_reference(ref)
+            assert np.array_equal(q8.qs[r].cpu().numpy(), qs)
+            assert np.array_equal(q8.d[r].cpu().numpy().view(np.uint32), d.view(np.uint32))
+
+
+def test_rmsnorm_row_gather(K):
+    rng = np.random.default_rng(4)
+    x = rng.normal(0, 1, (6, 512)).astype(np.float32)
+    w = np.ones(512, np.float32)
+    idx = torch.tensor([5, 0, 3], dtype=torch.int32, device="cuda")
+    out = torch.empty((3, 512), dtype=torch.float32, device="cuda")
+    K.rmsnorm_quant(torch.from_numpy(x).cuda(), torch.from_numpy(w).cuda(), 1e-6, out_f32=out, row_index=idx, rows=3)
+    torch.cuda.synchronize()
+    for i, r in enumerate([5, 0, 3]):
+        ref = np.empty(512, np.float32)
+        ob.lib().orc_rms_norm(x[r].ctypes.data, w.ctypes.data, 512, C.c_float(1e-6), ref.ctypes.data)
+        assert np.array_equal(out[i].cpu().numpy(), ref)
+
+
+@pytest.mark.parametrize("jf_type", KQ)
+@pytest.mark.parametrize("rows_in", [1, 3, 8, 13, 32])
+def test_matmul_matches_oracle(K, jf_type, rows_in):
+    N, Kdim = 96, 2048
+    w, raw = make_weight(K, jf_type, N, Kdim, 10 + jf_type)
+    rng = np.random.default_rng(rows_in)
+    x = rng.normal(0, 1, (rows_in, Kdim)).astype(np.float32)
+    q8 = K.Q8Buffer(rows_in, Kdim)
+    K.quantize_q8k(torch.from_numpy(x).cuda(), q8)
+    bias = torch.from_numpy(rng.normal(0, 0.1, N).astype(np.float32)).cuda()
+    out = torch.empty((rows_in, N), dtype=torch.float32, device="cuda")
+    K.matmul(w, rows_in, out, x_q8=q8, epilogue=K.EPILOGUE_BIAS, bias=bias)
+    torch.cuda.synchronize()
+    raw_np = np.frombuffer(raw, np.uint8)
+    t = ob.OrcTensor(jf_type, 0, Kdim, N, raw_np.ctypes.data)
+    ref = np.empty((rows_in, N), np.float32)
+    ob.lib().orc_matmul(C.byref(t), x.ctypes.data, rows_in, ref.ctypes.data)
+    ref += bias.cpu().numpy()
+    got = out.cpu().numpy()
+    scale = np.abs(ref).max()
+    np.testing.assert_allclose(got, ref, rtol=1e-5, atol=1e-6 * scale)
+
+
+@pytest.mark.parametrize("jf_type", [jfm.JF_TENSOR_F32, jfm.JF_TENSOR_F16])
+def test_float_matmul_residual(K, jf_type):
+    N, Kdim, rows_in = 40, 96, 5
+    w, raw = make_weight(K, jf_type, N, Kdim, 3)
+    rng = np.random.default_rng(6)
+    x = rng.normal(0, 1, (rows_in, Kdim)).astype(np.float32)
+    res = rng.normal(0, 1, (rows_in, N)).astype(np.float32)
+    out = torch.from_numpy(res.copy()).cuda()
+    K.matmul(w, rows_in, out, x_f32=torch.from_numpy(x).cuda(), epilogue=K.EPILOGUE_RESIDUAL, residual=out)
+    torch.cuda.synchronize()
+    t = ob.OrcTensor(jf_type, 0, Kdim, N, np.frombuffer(raw, np.uint8).ctypes.data)
+    ref = np.empty((rows_in, N), np.float32)
+    ob.lib().orc_matmul(C.byref(t), x.ctypes.data, rows_in, ref.ctypes.data)
+    np.testing.assert_allclose(out.cpu().numpy(), ref + res, rtol=1e-5, atol=1e-5)
+
+
+def test_swiglu_quant(K):
+    rng = np.random.default_rng(8)
+    g = rng.normal(0, 2, (4, 1024)).astype(np.float32)
+    u = rng.normal(0, 2, (4, 1024)).astype(np.float32)
+    out = torch.empty((4, 1024), dtype=torch.float32, device="cuda")
+    q8 = K.Q8Buffer(4, 1024)
+    K.swiglu_quant(torch.from_numpy(g).cuda(), torch.from_numpy(u).cuda(), out_f32=out, out_q8=q8)
+    torch.cuda.synchronize()
+    ref = (g / (np.float32(1) + np.exp(-g))) * u
+    np.testing.assert_allclose(out.cpu().numpy(), ref, rtol=2e-6, atol=1e-7)
+    d, qs, bs = q8_reference(out[1].cpu().numpy())
+    assert np.array_equal(q8.qs[1].cpu().numpy(), qs)
+
+
+def test_argmax_first_max(K):
+    x = np.random.default_rng(1).normal(0, 1, (4, 151936)).astype(np.float32)
+    x[0, 17] = x[0, 99999] = 50.0          # tie: first index wins
+    x[1, :] = -np.inf
+    x[2, 5] = np.nan
+    x[2, 6] = 30.0
+    out = torch.empty(4, dtype=torch.int32, device="cuda")
+    K.argmax(torch.from_numpy(x).cuda(), out)
+    torch.cuda.synchronize()
+    got = out.cpu().numpy().tolist()
+    assert got[0] == 17 and got[1] == 0 and got[2] == 6
+    assert got[3] == ob.lib().orc_argmax(x[3].ctypes.data, x.shape[1])
+
+
+def test_codec_bit_exact(K):
+    rng = np.random.default_rng(5)
+    specials = [0.0, -0.0, 1.0, 65504.0, 65519.99, 65520.0, 1e-8, 5.96e-8, 6.1e-5, 6.0e-5, np.inf, -np.inf]
+    vals = np.concatenate([rng.normal(0, 100, 20000), rng.normal(0, 1e-5, 5000), specials]).astype(np.float32)
+    nan_bits = np.array([0x7F800001, 0x7FC00000, 0xFFBFFFFF, 0x7F801000 | (0x2AA << 13)], dtype=np.uint32)
+    vals = np.concatenate([vals, nan_bits.view(np.float32)])
+    x = torch.from_numpy(vals).cuda()
+    h = torch.empty(vals.size, dtype=torch.int16, device="cuda")
+    K.codec_f32_to_f16(x, h)
+    back = torch.empty(vals.size, dtype=torch.float32, device="cuda")
+    K.codec_f16_to_f32(h, back)
+    torch.cuda.synchronize()
+    got = h.cpu().numpy().view(np.uint16)
+    ref = np.array([ob.lib().orc_codec_float_to_half(float(v)) for v in vals], dtype=np.uint16)
+    # ctypes passes floats through a double: NaN payloads must be checked bitwise separately
+    finite = np.isfinite(vals) | np.isinf(vals)
+    assert np.array_equal(got[finite], ref[finite])
+    for bits, g in zip(nan_bits, got[-4:]):
+        mant = int(bits) & 0x7FFFFF
+        assert g == (((int(bits) >> 16) & 0x8000) | 0x7C00 | (mant >> 13) | 0x200)
+    widened = back.cpu().numpy().view(np.uint32)
+    for g, w in zip(got[:50], widened[:50]):
+        assert struct.unpack("<I", struct.pack("<f", ob.lib().orc_codec_half_to_float(int(g))))[0] == w
+
+
+def _attention_reference(q, kc, vc, pos, heads, kv_heads, hd):
+    group = heads // kv_heads
+    out = np.zeros(heads * hd, np.float32)
+    qh = q.astype(np.float16).astype(np.float32).reshape(heads, hd)
+    keys = pos + 1
+    for h in range(heads):
+        g = h // group
+        k = kc[:keys, g * hd:(g + 1) * hd].astype(np.float32)
+        v = vc[:keys, g * hd:(g + 1) * hd].astype(np.float32)
+        s = (k @ qh[h].astype(np.float64)) * (1.0 / np.sqrt(np.float32(hd)))
+        p = np.exp(s - s.max())
+        p = p / p.sum()
+        out[h * hd:(h + 1) * hd] = (p @ v.astype(np.float64)).astype(np.float32)
+    return out
+
+
+@pytest.mark.parametrize("heads,kv_heads,hd", [(16, 2, 128), (12, 2, 128), (1, 1, 4), (40, 8, 128)])
+def test_rope_kv_and_attention(K, heads, kv_heads, hd):
+    rng = np.random.default_rng(heads)
+    cap, layers, layer = 300, 2, 1
+    kvd = kv_heads * hd
+    n_seq = 3
+    positions = [0, 77, 299]  # one row per sequence (decode-like), covering 1..5 key chunks
+    kbuf = [torch.zeros((layers, cap, kvd), dtype=torch.float16, device="cuda") for _ in range(n_seq)]
+    vbuf = [torch.zeros((layers, cap, kvd), dtype=torch.float16, device="cuda") for _ in range(n_seq)]
+    hist_k = [rng.normal(0, 1, (cap, kvd)).astype(np.float16) for _ in range(n_seq)]
+    hist_v = [rng.normal(0, 1, (cap, kvd)).astype(np.float16) for _ in range(n_seq)]
+    for i in range(n_seq):
+        kbuf[i][layer] = torch.from_numpy(hist_k[i]).cuda()
+        vbuf[i][layer] = torch.from_numpy(hist_v[i]).cuda()
+    slots = (K.KvSlot * n_seq)()
+    for i in range(n_seq):
+        slots[i] = K.KvSlot(kbuf[i].data_ptr(), vbuf[i].data_ptr(), cap, 0)
+    slots_dev = torch.frombuffer(bytearray(bytes(slots)), dtype=torch.uint8).cuda()
+    q = rng.normal(0, 1, (n_seq, heads * hd)).astype(np.float32)
+    k = rng.normal(0, 1, (n_seq, kvd)).astype(np.float32)
+    v = rng.normal(0, 1, (n_seq, kvd)).astype(np.float32)
+    seq = torch.arange(n_seq, dtype=torch.int32, device="cuda")
+    pos = torch.tensor(positions, dtype=torch.int32, device="cuda")
+    qt = torch.from_numpy(q.copy()).cuda()
+    libm = C.CDLL("libm.so.6")
+    libm.powf.argtypes, libm.powf.restype = [C.c_float, C.c_float], C.c_float
+    theta_scale = libm.powf(1e6, -2.0 / hd)  # the host-side powf the engine uses
+    K.rope_kv_append(qt, torch.from_numpy(k).cuda(), torch.from_numpy(v).cuda(), seq, pos, heads, kv_heads, hd, hd,
+                     theta_scale, slots_dev, layer)
+    scratch = torch.empty(K.attention_scratch_bytes(n_seq, heads, hd, cap), dtype=torch.uint8, device="cuda")
+    out = torch.empty((n_seq, heads * hd), dtype=torch.float32, device="cuda")
+    K.attention(qt, seq, pos, heads, kv_heads, hd, cap, slots_dev, layer, scratch, out)
+    torch.cuda.synchronize()
+    for i, p in enumerate(positions):
+        # RoPE of q and k through the oracle, then the cache row written at p
+        qr, kr = q[i].copy(), k[i].copy()
+        ob.lib().orc_rope_neox(qr.ctypes.data, heads, hd, hd, p, C.c_float(1e6))
+        ob.lib().orc_rope_neox(kr.ctypes.data, kv_heads, hd, hd, p, C.c_float(1e6))
+        np.testing.assert_allclose(qt[i].cpu().numpy(), qr, rtol=1e-5, atol=1e-5)
+        kc = kbuf[i][layer].cpu().numpy()
+        vc = vbuf[i][layer].cpu().numpy()
+        assert np.array_equal(kc[p], kr.astype(np.float16)) or np.abs(kc[p].astype(np.float32) - kr).max() < 2e-3
+        assert np.array_equal(vc[p], v[i].astype(np.float16))
+        assert np.array_equal(kc[p + 1:], hist_k[i][p + 1:])  # nothing else touched
+        ref = _attention_reference(qt[i].cpu().numpy(), kc, vc, p, heads, kv_heads, hd)
+        np.testing.assert_allclose(out[i].cpu().numpy(), ref, rtol=1e-4, atol=1e-5)
