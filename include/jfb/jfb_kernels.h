@@ -124,25 +124,34 @@ jfb_status jfb_matmul(const jfb_weight * weight, const jfb_q8k * x_q8, const flo
  * (ggml_rope_ext NEOX + ggml_set_rows, qwen2_architecture.cpp:400-424,
  * 499-506). Row r belongs to slots[seq[r]] at absolute position pos[r]; its K
  * and V rows are written at [layer][pos[r]] of that slot. q is rotated in
- * place. theta_scale = powf(freq_base, -2/rope_dims), computed by the caller
- * on the host; the angle of pair i is pos * theta_scale^i built by repeated
- * float multiplication, as GGML's rope cache does. */
+ * place. rope_table holds (cos, sin) pairs [table_positions][rope_dims/2]:
+ * GGML's rope cache values, angle_i = pos * theta_scale^i built by repeated
+ * float multiplication, theta_scale = powf(freq_base, -2/rope_dims), computed
+ * once on the host with the C library's cosf/sinf (the functions GGML-CPU
+ * calls), so device and CPU rotate with identical coefficients. */
 jfb_status jfb_rope_kv_append(float * q, const float * k, const float * v, uint32_t n, const int32_t * seq,
                               const int32_t * pos, uint32_t heads, uint32_t kv_heads, uint32_t head_dim,
-                              uint32_t rope_dims, float theta_scale, const jfb_kv_slot * slots,
-                              uint32_t layer, void * stream);
+                              uint32_t rope_dims, const float * rope_table, uint32_t table_positions,
+                              const jfb_kv_slot * slots, uint32_t layer, void * stream);
+
+/* Host helper: fills table[positions][rope_dims/2][2] with GGML's rope cache
+ * (cosf/sinf of pos * theta_scale^i, angles by repeated multiplication). */
+void jfb_rope_table_host(float * table, uint32_t positions, uint32_t rope_dims, float freq_base);
 
 /* Scratch bytes jfb_attention needs for n query rows with at most max_keys
  * keys each. */
 uint64_t jfb_attention_scratch_bytes(uint32_t n, uint32_t heads, uint32_t head_dim, uint32_t max_keys);
 
 /* Causal GQA attention of query rows over the F16 caches
- * (qwen2_architecture.cpp:425-470): row r attends keys [0, pos[r]] of
- * slots[seq[r]] at `layer`; query head h reads kv head h / (heads / kv_heads);
- * scores are K . f16(q) accumulated in f32, scaled by 1/sqrt(head_dim),
- * softmax in f32 (online, split over key chunks), output accumulated in f32.
- * Writes out[r][heads*head_dim] and, when out_q8 != NULL, its Q8_K
- * quantization. */
+ * (qwen2_architecture.cpp:425-470, GGML-CPU semantics of the unfused path):
+ * row r attends keys [0, pos[r]] of slots[seq[r]] at `layer`; query head h
+ * reads kv head h / (heads / kv_heads); scores are K . f16(q) with the exact
+ * f16 products summed in double and rounded to f32 once; x = score *
+ * 1/sqrt(head_dim); softmax with exp(x - max) summed in double over all keys,
+ * p = e * (float)(1/sum) rounded to f16; output = exact p*v products summed
+ * in double, rounded once. Four launches: scores (+chunk maxima), row
+ * statistics, P V partials, combine (+Q8_K quantization of the result when
+ * out_q8 != NULL). */
 jfb_status jfb_attention(const float * q, uint32_t n, const int32_t * seq, const int32_t * pos, uint32_t heads,
                          uint32_t kv_heads, uint32_t head_dim, uint32_t max_keys, const jfb_kv_slot * slots,
                          uint32_t layer, void * scratch, uint64_t scratch_bytes, float * out,

@@ -286,6 +286,17 @@ DeviceModel::DeviceModel(const std::string & package_path, std::uint32_t layer_s
     cuda_check(cudaStreamSynchronize(stream_), "upload native weights");
     if (staging != nullptr) cudaFree(staging);
 
+    // RoPE coefficients, computed once on the host with the C library's
+    // cosf/sinf exactly as GGML's rope cache does, then kept on the device.
+    {
+        const std::uint32_t positions = hp_.info.context_length, pairs = hp_.rope_dimension_count / 2;
+        std::vector<float> table(std::size_t(positions) * pairs * 2);
+        jfb_rope_table_host(table.data(), positions, hp_.rope_dimension_count, hp_.rope_frequency_base);
+        cuda_check(cudaMalloc(&rope_table_, table.size() * sizeof(float)), "allocate rope table");
+        cuda_check(cudaMemcpy(rope_table_, table.data(), table.size() * sizeof(float), cudaMemcpyHostToDevice),
+                   "upload rope table");
+    }
+
     auto vec = [&](const std::string & n) -> const float * {
         const auto it = index.find(n);
         if (it == index.end()) return nullptr;
@@ -323,6 +334,7 @@ DeviceModel::DeviceModel(const std::string & package_path, std::uint32_t layer_s
 
 DeviceModel::~DeviceModel() {
     if (arena_ != nullptr) cudaFree(arena_);
+    if (rope_table_ != nullptr) cudaFree(rope_table_);
     if (stream_ != nullptr) cudaStreamDestroy(stream_);
 }
 
@@ -518,7 +530,6 @@ void Qwen2Stage::forward(std::span<const SequenceRows> seqs, const ForwardIo & i
                    "upload stage activations");
     }
 
-    const float theta_scale = ::powf(hp.rope_frequency_base, -2.0f / float(hp.rope_dimension_count));
     for (const TimedLaunch & t : timed_) {  // results of an uncollected earlier pass are dropped
         event_pool_.push_back(t.start);
         event_pool_.push_back(t.stop);
@@ -555,7 +566,7 @@ void Qwen2Stage::forward(std::span<const SequenceRows> seqs, const ForwardIo & i
         mm(w.k, xf_, R, JFB_EPILOGUE_BIAS, w.k_bias, nullptr, k_);
         mm(w.v, xf_, R, JFB_EPILOGUE_BIAS, w.v_bias, nullptr, v_);
         jfb_check(jfb_rope_kv_append(q_, k_, v_, R, seq_d, pos_d, hp.head_count, hp.kv_head_count, hp.head_dim(),
-                                     hp.rope_dimension_count, theta_scale, slots_d, li, st));
+                                     hp.rope_dimension_count, m_.rope_table(), hp.info.context_length, slots_d, li, st));
         const bool o_q8 = needs_q8(w.o);
         timed(1, attention_bytes, [&] {
             jfb_check(jfb_attention(q_, R, seq_d, pos_d, hp.head_count, hp.kv_head_count, hp.head_dim(), max_keys,

@@ -67,6 +67,8 @@ public:
     const float * output_norm() const { return output_norm_; }
     const float * output_bias() const { return output_bias_; }
     const LayerWeights & layer(std::uint32_t i) const { return layer_weights_[i]; }
+    // GGML rope cache (cos, sin) for positions [0, context_length), device
+    const float * rope_table() const { return rope_table_; }
 
     const std::string & source_sha256() const { return source_sha256_; }
     const std::string & device_name() const { return device_name_; }
@@ -82,6 +84,7 @@ private:
     cudaStream_t stream_ = nullptr;
     void * arena_ = nullptr;
     std::uint64_t arena_bytes_ = 0;
+    float * rope_table_ = nullptr;
     jfb_weight token_embd_{}, output_{};
     const float * output_norm_ = nullptr;
     const float * output_bias_ = nullptr;

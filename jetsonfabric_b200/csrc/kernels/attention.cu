@@ -1,20 +1,25 @@
-// Causal GQA attention over the F16 KV cache, split over key chunks, plus the
-// combine step (fused with the Q8_K quantization of the result, which the
-// O-projection consumes).
+// Causal GQA attention over the F16 KV cache with GGML-CPU semantics,
+// computed exactly enough to reproduce the CPU result bit for bit.
 //
-// Semantics follow the reference graph's unfused path, which is what GGML-CPU
-// executes (qwen2_architecture.cpp:425-470): scores = K . q with q rounded to
-// f16 and f32 accumulation; x = score * (1/sqrt(head_dim)); keys after the
-// query's position are masked out (697-708); softmax in f32; output = P V
-// accumulated in f32. One deliberate difference: GGML rounds the normalized
-// probabilities to f16 before the V product; this kernel keeps them in f32
-// (online softmax across chunks), a relative difference below 2^-11 per
-// probability.
+// The reference graph's unfused path, which GGML-CPU executes
+// (qwen2_architecture.cpp:425-470, mask 697-708), is: scores = K . q with q
+// converted to f16 and an f32 result; soft_max_ext: x = score * scale + mask,
+// e = exp(x - max), p = e / sum; P converted to f16; out = V . P with an f32
+// result. Here:
+//   - every product of two f16 values is exact in f32 and the products are
+//     summed in double, then rounded to f32 once, so the order of the
+//     additions (and the split of a row over CTAs) does not change the result;
+//   - the softmax normaliser is the double sum of exp(x - max) over all keys
+//     of the row, and p is rounded to f16 exactly as GGML does before P V;
+//   - exp is exp_cw (common.cuh), the same method the CPU oracle implements.
 //
-// Grid: (query row, kv head, key chunk). A CTA owns the G = heads/kv_heads
-// query heads that share one kv head, so every K and V row it reads serves G
-// heads. Two threads per key compute the scores (half of head_dim each); one
-// thread per output dimension accumulates P V.
+// Four launches over a (row, kv head, 64-key chunk) grid:
+//   1. scores x_j (and each chunk's maximum) -> scratch
+//   2. per (row, head): max over chunks, sum_j exp(x_j - max) in double
+//   3. P V partial sums per chunk in double -> scratch
+//   4. per row: sum of the chunk partials, f32 output (+ Q8_K quantization)
+// A CTA of launches 1 and 3 serves the G = heads/kv_heads query heads that
+// share its kv head, so each K and V row is read once for G heads.
 #include "common.cuh"
 
 namespace jfb {
@@ -25,157 +30,220 @@ constexpr int kChunk = 64;      // keys per CTA
 constexpr int kMaxGroup = 16;   // query heads per kv head
 constexpr int kMaxHeadDim = 256;
 
-__global__ void __launch_bounds__(kThreads) attention_chunk_kernel(
-    const float * __restrict__ q, const int32_t * __restrict__ seq, const int32_t * __restrict__ pos, uint32_t heads,
-    uint32_t kv_heads, uint32_t head_dim, const jfb_kv_slot * __restrict__ slots, uint32_t layer, float scale,
-    uint32_t max_splits, float * __restrict__ partial) {
+struct Scratch {
+    float * scores;      // [n][heads][keys_cap]
+    float * chunk_max;   // [n][heads][splits]
+    float2 * stats;      // [n][heads] (max, 1/sum)
+    double * partial;    // [n][heads][splits][head_dim]
+};
+
+__host__ __device__ inline uint64_t align_up(uint64_t v) { return (v + 255) / 256 * 256; }
+
+__host__ __device__ inline Scratch carve(void * base, uint32_t n, uint32_t heads, uint32_t head_dim, uint32_t splits) {
+    uint8_t * p = static_cast<uint8_t *>(base);
+    const uint64_t keys_cap = uint64_t(splits) * kChunk;
+    Scratch s;
+    s.scores = reinterpret_cast<float *>(p);
+    p += align_up(uint64_t(n) * heads * keys_cap * sizeof(float));
+    s.chunk_max = reinterpret_cast<float *>(p);
+    p += align_up(uint64_t(n) * heads * splits * sizeof(float));
+    s.stats = reinterpret_cast<float2 *>(p);
+    p += align_up(uint64_t(n) * heads * sizeof(float2));
+    s.partial = reinterpret_cast<double *>(p);
+    return s;
+}
+
+uint64_t scratch_size(uint32_t n, uint32_t heads, uint32_t head_dim, uint32_t splits) {
+    const uint64_t keys_cap = uint64_t(splits) * kChunk;
+    return align_up(uint64_t(n) * heads * keys_cap * sizeof(float)) + align_up(uint64_t(n) * heads * splits * sizeof(float)) +
+           align_up(uint64_t(n) * heads * sizeof(float2)) + uint64_t(n) * heads * splits * head_dim * sizeof(double);
+}
+
+// Launch 1: x_j = f32(sum_d k_jd * f16(q_d)) * scale for the chunk's keys.
+__global__ void __launch_bounds__(kThreads) scores_kernel(const float * __restrict__ q, const int32_t * __restrict__ seq,
+                                                        const int32_t * __restrict__ pos, uint32_t heads, uint32_t kv_heads,
+                                                        uint32_t head_dim, const jfb_kv_slot * __restrict__ slots,
+                                                        uint32_t layer, float scale, uint32_t splits, Scratch sc) {
     __shared__ float q_s[kMaxGroup * kMaxHeadDim];
-    __shared__ float p_s[kMaxGroup][kChunk];
-    __shared__ float m_s[kMaxGroup], l_s[kMaxGroup];
+    __shared__ float x_s[kMaxGroup][kChunk];
     const uint32_t r = blockIdx.x, kvh = blockIdx.y, split = blockIdx.z;
-    const int32_t p = pos[r];
-    const uint32_t keys = uint32_t(p) + 1u;
+    const uint32_t keys = uint32_t(pos[r]) + 1u;
     const uint32_t j0 = split * kChunk;
     if (j0 >= keys) return;
     const uint32_t j1 = min(keys, j0 + kChunk);
-    const uint32_t G = heads / kv_heads;
-    const uint32_t D = head_dim;
+    const uint32_t G = heads / kv_heads, D = head_dim, kvd = kv_heads * D;
     const jfb_kv_slot slot = slots[seq[r]];
-    const uint32_t kvd = kv_heads * D;
-    const uint16_t * kbase = slot.k + (uint64_t(layer) * slot.capacity) * kvd + kvh * D;
-    const uint16_t * vbase = slot.v + (uint64_t(layer) * slot.capacity) * kvd + kvh * D;
-
-    // q rounded to f16 (GGML converts src1 of the F16 mul_mat to F16)
+    const uint16_t * kbase = slot.k + uint64_t(layer) * slot.capacity * kvd + kvh * D;
     for (uint32_t i = threadIdx.x; i < G * D; i += kThreads) {
         const uint32_t g = i / D, d = i % D;
         q_s[i] = __half2float(__float2half_rn(q[uint64_t(r) * heads * D + (kvh * G + g) * D + d]));
     }
     __syncthreads();
-
-    // scores: thread pair (2k, 2k+1) handles key j0 + k, each over half of D
-    {
-        const uint32_t kk = threadIdx.x >> 1, half = threadIdx.x & 1;
-        const uint32_t j = j0 + kk;
-        float acc[kMaxGroup];
+    const uint32_t kk = threadIdx.x >> 1, half = threadIdx.x & 1;
+    const uint32_t j = j0 + kk;
+    double acc[kMaxGroup];
 #pragma unroll
-        for (int g = 0; g < kMaxGroup; ++g) acc[g] = 0.0f;
-        if (j < j1) {
-            const uint16_t * krow = kbase + uint64_t(j) * kvd;
-            const uint32_t d_begin = half * (D / 2), d_end = half ? D : D / 2;
-            if ((D % 16) == 0) {
-                for (uint32_t d = d_begin; d < d_end; d += 8) {
-                    const uint4 raw = __ldg(reinterpret_cast<const uint4 *>(krow + d));
-                    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+    for (int g = 0; g < kMaxGroup; ++g) acc[g] = 0.0;
+    if (j < j1) {
+        const uint16_t * krow = kbase + uint64_t(j) * kvd;
+        const uint32_t d_begin = half * (D / 2), d_end = half ? D : D / 2;
+        if ((D % 16) == 0) {
+            for (uint32_t d = d_begin; d < d_end; d += 8) {
+                const uint4 raw = __ldg(reinterpret_cast<const uint4 *>(krow + d));
+                const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const float k0 = half_bits_to_float(uint16_t(w[e] & 0xffffu));
-                        const float k1 = half_bits_to_float(uint16_t(w[e] >> 16));
+                for (int e = 0; e < 4; ++e) {
+                    const float k0 = half_bits_to_float(uint16_t(w[e] & 0xffffu));
+                    const float k1 = half_bits_to_float(uint16_t(w[e] >> 16));
 #pragma unroll
-                        for (int g = 0; g < kMaxGroup; ++g) {
-                            if (uint32_t(g) < G) {
-                                acc[g] = fmaf(k0, q_s[g * D + d + 2 * e], acc[g]);
-                                acc[g] = fmaf(k1, q_s[g * D + d + 2 * e + 1], acc[g]);
-                            }
+                    for (int g = 0; g < kMaxGroup; ++g) {
+                        if (uint32_t(g) < G) {
+                            acc[g] += double(__fmul_rn(k0, q_s[g * D + d + 2 * e]));
+                            acc[g] += double(__fmul_rn(k1, q_s[g * D + d + 2 * e + 1]));
                         }
                     }
                 }
-            } else {
-                for (uint32_t d = d_begin; d < d_end; ++d) {
-                    const float kv = half_bits_to_float(krow[d]);
+            }
+        } else {
+            for (uint32_t d = d_begin; d < d_end; ++d) {
+                const float kv = half_bits_to_float(krow[d]);
 #pragma unroll
-                    for (int g = 0; g < kMaxGroup; ++g) {
-                        if (uint32_t(g) < G) acc[g] = fmaf(kv, q_s[g * D + d], acc[g]);
-                    }
+                for (int g = 0; g < kMaxGroup; ++g) {
+                    if (uint32_t(g) < G) acc[g] += double(__fmul_rn(kv, q_s[g * D + d]));
                 }
             }
         }
+    }
 #pragma unroll
-        for (int g = 0; g < kMaxGroup; ++g) {
-            const float total = acc[g] + __shfl_xor_sync(0xffffffffu, acc[g], 1);
-            if (uint32_t(g) < G && half == 0 && kk < uint32_t(kChunk)) {
-                p_s[g][kk] = j < j1 ? __fmul_rn(total, scale) : -INFINITY;
-            }
+    for (int g = 0; g < kMaxGroup; ++g) {
+        const double total = acc[g] + __shfl_xor_sync(0xffffffffu, acc[g], 1);
+        if (uint32_t(g) < G && half == 0) {
+            x_s[g][kk] = j < j1 ? __fmul_rn(__double2float_rn(total), scale) : -INFINITY;
         }
     }
     __syncthreads();
-
-    // per-head chunk max and exponentials: warp w handles heads w, w+4, ...
+    const uint32_t keys_cap = splits * kChunk;
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (uint32_t g = warp; g < G; g += kThreads / 32) {
+        const uint32_t h = kvh * G + g;
+        float * dst = sc.scores + (uint64_t(r) * heads + h) * keys_cap + j0;
         float mx = -INFINITY;
-        for (uint32_t k = lane; k < uint32_t(kChunk); k += 32) mx = fmaxf(mx, p_s[g][k]);
-        mx = warp_max(mx);
-        float sum = 0.0f;
         for (uint32_t k = lane; k < uint32_t(kChunk); k += 32) {
-            const float e = (j0 + k < j1) ? expf(p_s[g][k] - mx) : 0.0f;
-            p_s[g][k] = e;
-            sum += e;
+            const float x = x_s[g][k];
+            if (j0 + k < j1) dst[k] = x;
+            mx = fmaxf(mx, x);
         }
-        sum = warp_sum(sum);
-        if (lane == 0) {
-            m_s[g] = mx;
-            l_s[g] = sum;
-        }
+        mx = warp_max(mx);
+        if (lane == 0) sc.chunk_max[(uint64_t(r) * heads + h) * splits + split] = mx;
+    }
+}
+
+__device__ __forceinline__ double block_sum(double v, double * shared) {
+    v = warp_sum(v);
+    if ((threadIdx.x & 31) == 0) shared[threadIdx.x >> 5] = v;
+    __syncthreads();
+    double t = 0.0;
+    if (threadIdx.x < 32) {
+        t = threadIdx.x < kThreads / 32 ? shared[threadIdx.x] : 0.0;
+        t = warp_sum(t);
+        if (threadIdx.x == 0) shared[0] = t;
     }
     __syncthreads();
+    return shared[0];
+}
 
-    // P V: thread d (and d + 128 for head_dim 256)
-    const uint64_t part_row = (uint64_t(r) * heads + kvh * G) * max_splits;  // head (kvh*G + g) at + g*max_splits
+// Launch 2: per (row, head) maximum and 1 / sum_j exp(x_j - max).
+__global__ void __launch_bounds__(kThreads) stats_kernel(const int32_t * __restrict__ pos, uint32_t heads, uint32_t splits,
+                                                       Scratch sc) {
+    __shared__ double red[kThreads / 32];
+    const uint32_t r = blockIdx.x, h = blockIdx.y;
+    const uint32_t keys = uint32_t(pos[r]) + 1u;
+    const uint32_t used = (keys + kChunk - 1) / kChunk;
+    const uint64_t rh = uint64_t(r) * heads + h;
+    float mx = -INFINITY;
+    for (uint32_t c = threadIdx.x; c < used; c += kThreads) mx = fmaxf(mx, sc.chunk_max[rh * splits + c]);
+    mx = warp_max(mx);
+    __shared__ float mx_s[kThreads / 32];
+    if ((threadIdx.x & 31) == 0) mx_s[threadIdx.x >> 5] = mx;
+    __syncthreads();
+    mx = -INFINITY;
+    for (int w = 0; w < kThreads / 32; ++w) mx = fmaxf(mx, mx_s[w]);
+    const float * x = sc.scores + rh * (uint64_t(splits) * kChunk);
+    double sum = 0.0;
+    for (uint32_t j = threadIdx.x; j < keys; j += kThreads) sum += double(exp_cw(__fsub_rn(x[j], mx)));
+    sum = block_sum(sum, red);
+    if (threadIdx.x == 0) sc.stats[rh] = make_float2(mx, __double2float_rn(__ddiv_rn(1.0, sum)));  // sum >= 1
+}
+
+// Launch 3: P V over the chunk, p = f16(exp(x - max) * inv), sums in double.
+__global__ void __launch_bounds__(kThreads) pv_kernel(const int32_t * __restrict__ seq, const int32_t * __restrict__ pos,
+                                                    uint32_t heads, uint32_t kv_heads, uint32_t head_dim,
+                                                    const jfb_kv_slot * __restrict__ slots, uint32_t layer,
+                                                    uint32_t splits, Scratch sc) {
+    __shared__ float p_s[kMaxGroup][kChunk];
+    const uint32_t r = blockIdx.x, kvh = blockIdx.y, split = blockIdx.z;
+    const uint32_t keys = uint32_t(pos[r]) + 1u;
+    const uint32_t j0 = split * kChunk;
+    if (j0 >= keys) return;
+    const uint32_t j1 = min(keys, j0 + kChunk);
+    const uint32_t G = heads / kv_heads, D = head_dim, kvd = kv_heads * D;
+    const uint32_t keys_cap = splits * kChunk;
+    for (uint32_t i = threadIdx.x; i < G * kChunk; i += kThreads) {
+        const uint32_t g = i / kChunk, k = i % kChunk;
+        const uint64_t rh = uint64_t(r) * heads + kvh * G + g;
+        float p = 0.0f;
+        if (j0 + k < j1) {
+            const float2 st = sc.stats[rh];
+            const float e = exp_cw(__fsub_rn(sc.scores[rh * keys_cap + j0 + k], st.x));
+            p = __half2float(__float2half_rn(__fmul_rn(e, st.y)));
+        }
+        p_s[g][k] = p;
+    }
+    __syncthreads();
+    const jfb_kv_slot slot = slots[seq[r]];
+    const uint16_t * vbase = slot.v + uint64_t(layer) * slot.capacity * kvd + kvh * D;
     for (uint32_t d = threadIdx.x; d < D; d += kThreads) {
-        float acc[kMaxGroup];
+        double acc[kMaxGroup];
 #pragma unroll
-        for (int g = 0; g < kMaxGroup; ++g) acc[g] = 0.0f;
+        for (int g = 0; g < kMaxGroup; ++g) acc[g] = 0.0;
         for (uint32_t j = j0; j < j1; ++j) {
             const float vv = half_bits_to_float(vbase[uint64_t(j) * kvd + d]);
 #pragma unroll
             for (int g = 0; g < kMaxGroup; ++g) {
-                if (uint32_t(g) < G) acc[g] = fmaf(p_s[g][j - j0], vv, acc[g]);
+                if (uint32_t(g) < G) acc[g] += double(__fmul_rn(p_s[g][j - j0], vv));
             }
         }
 #pragma unroll
         for (int g = 0; g < kMaxGroup; ++g) {
             if (uint32_t(g) < G) {
-                float * rec = partial + ((part_row + uint64_t(g) * max_splits + split) * (D + 2));
-                rec[2 + d] = acc[g];
+                const uint64_t rh = uint64_t(r) * heads + kvh * G + g;
+                sc.partial[(rh * splits + split) * D + d] = acc[g];
             }
         }
     }
-    if (threadIdx.x < G) {
-        float * rec = partial + ((part_row + uint64_t(threadIdx.x) * max_splits + split) * (D + 2));
-        rec[0] = m_s[threadIdx.x];
-        rec[1] = l_s[threadIdx.x];
-    }
 }
 
-// Merges the chunk partials of one query row, writes out[r][heads*D] and
-// optionally its Q8_K quantization (then heads*D % 256 == 0).
-__global__ void __launch_bounds__(256) attention_combine_kernel(const int32_t * __restrict__ pos, uint32_t heads,
-                                                              uint32_t head_dim, uint32_t max_splits,
-                                                              const float * __restrict__ partial,
-                                                              float * __restrict__ out, jfb_q8k q8, int quantize) {
-    __shared__ unsigned long long keys[8];
+// Launch 4: out[r][h*D + d] = f32(sum of the chunk partials); Q8_K of the row.
+__global__ void __launch_bounds__(256) combine_kernel(const int32_t * __restrict__ pos, uint32_t heads, uint32_t head_dim,
+                                                    uint32_t splits, Scratch sc, float * __restrict__ out, jfb_q8k q8,
+                                                    int quantize) {
+    __shared__ unsigned long long keys_s[8];
     const uint32_t r = blockIdx.x;
     const uint32_t D = head_dim, width = heads * D;
-    const uint32_t splits = (uint32_t(pos[r]) + kChunk) / kChunk;  // ceil((pos + 1) / chunk)
+    const uint32_t used = (uint32_t(pos[r]) + kChunk) / kChunk;
     for (uint32_t i = threadIdx.x; i < width; i += blockDim.x) {
         const uint32_t h = i / D, d = i % D;
-        const float * base = partial + (uint64_t(r) * heads + h) * max_splits * (D + 2);
-        float M = -INFINITY;
-        for (uint32_t c = 0; c < splits; ++c) M = fmaxf(M, base[c * (D + 2)]);
-        float L = 0.0f, O = 0.0f;
-        for (uint32_t c = 0; c < splits; ++c) {
-            const float w = expf(base[c * (D + 2)] - M);
-            L = fmaf(w, base[c * (D + 2) + 1], L);
-            O = fmaf(w, base[c * (D + 2) + 2 + d], O);
-        }
-        out[uint64_t(r) * width + i] = __fdiv_rn(O, L);
+        const double * base = sc.partial + ((uint64_t(r) * heads + h) * splits) * D + d;
+        double acc = 0.0;
+        for (uint32_t c = 0; c < used; ++c) acc += base[uint64_t(c) * D];
+        out[uint64_t(r) * width + i] = __double2float_rn(acc);
     }
     if (!quantize) return;
     __syncthreads();
     for (uint32_t c = 0; c < width / kQK; ++c) {
         const float y = out[uint64_t(r) * width + c * kQK + threadIdx.x];
         const uint64_t block = uint64_t(r) * (width / kQK) + c;
-        q8k_block_256(y, q8.qs + block * kQK, q8.d + block, q8.bsums + block * 16, keys);
+        q8k_block_256(y, q8.qs + block * kQK, q8.d + block, q8.bsums + block * 16, keys_s);
     }
 }
 
@@ -185,8 +253,8 @@ __global__ void __launch_bounds__(256) attention_combine_kernel(const int32_t * 
 using namespace jfb;
 
 extern "C" uint64_t jfb_attention_scratch_bytes(uint32_t n, uint32_t heads, uint32_t head_dim, uint32_t max_keys) {
-    const uint64_t splits = (uint64_t(max_keys) + kChunk - 1) / kChunk;
-    return uint64_t(n) * heads * splits * (uint64_t(head_dim) + 2) * sizeof(float);
+    const uint32_t splits = (max_keys + kChunk - 1) / kChunk;
+    return scratch_size(n, heads, head_dim, splits);
 }
 
 extern "C" jfb_status jfb_attention(const float * q, uint32_t n, const int32_t * seq, const int32_t * pos,
@@ -208,16 +276,17 @@ extern "C" jfb_status jfb_attention(const float * q, uint32_t n, const int32_t *
     }
     if (n == 0) return status_ok();
     const uint32_t splits = (max_keys + kChunk - 1) / kChunk;
-    if (splits > 65535u || kv_heads > 65535u) return status_error(JFB_STATUS_INVALID_ARGUMENT, "attention grid too large");
+    if (splits > 65535u || kv_heads > 65535u || heads > 65535u) {
+        return status_error(JFB_STATUS_INVALID_ARGUMENT, "attention grid too large");
+    }
     cudaStream_t s = as_stream(stream);
+    const Scratch sc = carve(scratch, n, heads, head_dim, splits);
     const float scale = 1.0f / sqrtf(float(head_dim));
-    attention_chunk_kernel<<<dim3(n, kv_heads, splits), kThreads, 0, s>>>(q, seq, pos, heads, kv_heads, head_dim, slots,
-                                                                          layer, scale, splits,
-                                                                          static_cast<float *>(scratch));
-    jfb_status st = launch_status("jfb_attention(chunks)");
-    if (st.code != JFB_STATUS_OK) return st;
+    scores_kernel<<<dim3(n, kv_heads, splits), kThreads, 0, s>>>(q, seq, pos, heads, kv_heads, head_dim, slots, layer,
+                                                                  scale, splits, sc);
+    stats_kernel<<<dim3(n, heads), kThreads, 0, s>>>(pos, heads, splits, sc);
+    pv_kernel<<<dim3(n, kv_heads, splits), kThreads, 0, s>>>(seq, pos, heads, kv_heads, head_dim, slots, layer, splits, sc);
     const jfb_q8k q8 = out_q8 != nullptr ? *out_q8 : jfb_q8k{nullptr, nullptr, nullptr};
-    attention_combine_kernel<<<n, 256, 0, s>>>(pos, heads, head_dim, splits, static_cast<const float *>(scratch), out,
-                                               q8, out_q8 != nullptr);
-    return launch_status("jfb_attention(combine)");
+    combine_kernel<<<n, 256, 0, s>>>(pos, heads, head_dim, splits, sc, out, q8, out_q8 != nullptr);
+    return launch_status("jfb_attention");
 }

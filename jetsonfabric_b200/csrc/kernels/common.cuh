@@ -56,6 +56,34 @@ __device__ __forceinline__ uint16_t float_to_half_bits(float f) {
     return __half_as_ushort(__float2half_rn(f));
 }
 
+// exp(x) by Cody-Waite argument reduction (x = n ln2 + r with ln2 split into
+// a short high part and a correction) and the degree-7 Taylor polynomial of
+// e^r evaluated in Horner form with fused multiply-adds, then an exact
+// two-step scaling by 2^n (max error below 1 ulp over the normal range). Every
+// step is a correctly rounded IEEE operation, so the CPU oracle's
+// implementation of the same method gives identical bits.
+__device__ __forceinline__ float pow2i(int e) { return __uint_as_float(static_cast<unsigned>(e + 127) << 23); }
+
+__device__ __forceinline__ float exp_cw(float x) {
+    if (x != x) return x;
+    if (x > 88.72283935546875f) return __int_as_float(0x7f800000);
+    if (x < -103.972084045410156f) return 0.0f;
+    const float n = rintf(__fmul_rn(x, 1.44269502162933349609375f));
+    float r = fmaf(-n, 0.693145751953125f, x);
+    r = fmaf(-n, 1.4286068203094172e-06f, r);
+    float p = 1.98412701138295233e-04f;
+    p = fmaf(p, r, 1.38888892251998186e-03f);
+    p = fmaf(p, r, 8.33333376795053482e-03f);
+    p = fmaf(p, r, 4.16666679084300995e-02f);
+    p = fmaf(p, r, 1.66666671633720398e-01f);
+    p = fmaf(p, r, 0.5f);
+    p = fmaf(p, r, 1.0f);
+    p = fmaf(p, r, 1.0f);
+    const int e = static_cast<int>(n);
+    const int e1 = e / 2, e2 = e - e1;
+    return __fmul_rn(__fmul_rn(p, pow2i(e1)), pow2i(e2));
+}
+
 // Warp-wide sum.
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll

@@ -4,9 +4,11 @@
 // 256-value block, exact integer dot products of the weight codes with the
 // Q8_K activation bytes inside each 16- or 32-value sub-block, multiplies them
 // by the integer sub-block scales, and applies one float scale per block:
-//     sum += (d_w * d_a) * isum - (dmin_w * d_a) * msum
-// This kernel computes the same integers with dp4a, so the only difference
-// from the CPU result is the order of the float additions across blocks.
+//     c_b = (d_w * d_a) * isum - (dmin_w * d_a) * msum
+// This kernel computes the same integers with dp4a and each c_b with the same
+// rounded float operations; the c_b of a row are summed in double and
+// rounded to float once, which makes the result independent of the order in
+// which lanes add blocks, so it equals the CPU oracle bit for bit.
 //
 // Work split: one warp per weight row, four lanes per 256-block (each lane
 // owns 64 values: 32 bytes of Q4_K codes, 64 bytes of Q6_K ql/qh, or the
@@ -66,17 +68,30 @@ struct ActView {
     uint32_t cols;
 };
 
+// Sums an integer over the four lanes that share one 256-block (lanes 4k..4k+3).
+__device__ __forceinline__ int block_lanes_sum(int v) {
+    v += __shfl_xor_sync(0xffffffffu, v, 1);
+    v += __shfl_xor_sync(0xffffffffu, v, 2);
+    return v;
+}
+
+// One 256-block of one weight row against up to kGroup activation rows. The
+// four lanes of a block each own 64 values; their integer partial sums are
+// combined first so the block's float term is formed once, as on the CPU.
+// Every lane of the warp must call this (the shuffles are warp-wide);
+// `valid` is false for lanes whose block index is past the row end.
 template <uint32_t TYPE>
 __device__ __forceinline__ void lane_block(const jfb_weight & w, uint64_t block, int c, const ActView & a,
-                                           uint32_t b, uint32_t t0, int nt, float * acc) {
+                                           uint32_t b, uint32_t t0, int nt, bool valid, double * acc) {
     const uint8_t * p0 = static_cast<const uint8_t *>(w.plane[0]);
     const uint8_t * p1 = static_cast<const uint8_t *>(w.plane[1]);
     const uint8_t * p2 = static_cast<const uint8_t *>(w.plane[2]);
     const uint32_t nb = a.cols / kQK;
     if constexpr (TYPE == JF_TENSOR_Q4_K) {
-        const uint4 q0 = ldg16(p0 + block * 128 + 32 * c);
-        const uint4 q1 = ldg16(p0 + block * 128 + 32 * c + 16);
-        const uint4 hdr = ldg16(p1 + block * 16);
+        const uint4 zero = make_uint4(0, 0, 0, 0);
+        const uint4 q0 = valid ? ldg16(p0 + block * 128 + 32 * c) : zero;
+        const uint4 q1 = valid ? ldg16(p0 + block * 128 + 32 * c + 16) : zero;
+        const uint4 hdr = valid ? ldg16(p1 + block * 16) : zero;
         const float d = half_bits_to_float(uint16_t(hdr.x & 0xffffu));
         const float dmin = half_bits_to_float(uint16_t(hdr.x >> 16));
         int sc_lo, m_lo, sc_hi, m_hi;
@@ -87,36 +102,47 @@ __device__ __forceinline__ void lane_block(const jfb_weight & w, uint64_t block,
         for (int t = 0; t < kGroup; ++t) {
             if (t >= nt) break;
             const uint64_t row = uint64_t(t0 + t);
-            const int8_t * aq = a.qs + row * a.cols + uint64_t(b) * kQK + 64 * c;
-            const int4 a0 = __ldg(reinterpret_cast<const int4 *>(aq));
-            const int4 a1 = __ldg(reinterpret_cast<const int4 *>(aq + 16));
-            const int4 a2 = __ldg(reinterpret_cast<const int4 *>(aq + 32));
-            const int4 a3 = __ldg(reinterpret_cast<const int4 *>(aq + 48));
-            const int av[16] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w,
-                                a2.x, a2.y, a2.z, a2.w, a3.x, a3.y, a3.z, a3.w};
-            int s_lo = 0, s_hi = 0;
+            int isum = 0, msum = 0;
+            float da = 0.0f;
+            if (valid) {
+                const int8_t * aq = a.qs + row * a.cols + uint64_t(b) * kQK + 64 * c;
+                const int4 a0 = __ldg(reinterpret_cast<const int4 *>(aq));
+                const int4 a1 = __ldg(reinterpret_cast<const int4 *>(aq + 16));
+                const int4 a2 = __ldg(reinterpret_cast<const int4 *>(aq + 32));
+                const int4 a3 = __ldg(reinterpret_cast<const int4 *>(aq + 48));
+                const int av[16] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w,
+                                    a2.x, a2.y, a2.z, a2.w, a3.x, a3.y, a3.z, a3.w};
+                int s_lo = 0, s_hi = 0;
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                s_lo = dp4a(int(q[i] & 0x0f0f0f0fu), av[i], s_lo);
-                s_hi = dp4a(int((q[i] >> 4) & 0x0f0f0f0fu), av[8 + i], s_hi);
+                for (int i = 0; i < 8; ++i) {
+                    s_lo = dp4a(int(q[i] & 0x0f0f0f0fu), av[i], s_lo);
+                    s_hi = dp4a(int((q[i] >> 4) & 0x0f0f0f0fu), av[8 + i], s_hi);
+                }
+                const int2 bs = __ldg(reinterpret_cast<const int2 *>(a.bsums + row * (a.cols / 16) + uint64_t(b) * 16 + 4 * c));
+                const int b0 = int(int16_t(bs.x & 0xffff)), b1 = int(int16_t(uint32_t(bs.x) >> 16));
+                const int b2 = int(int16_t(bs.y & 0xffff)), b3 = int(int16_t(uint32_t(bs.y) >> 16));
+                isum = sc_lo * s_lo + sc_hi * s_hi;
+                msum = m_lo * (b0 + b1) + m_hi * (b2 + b3);
+                da = __ldg(a.d + row * nb + b);
             }
-            const int2 bs = __ldg(reinterpret_cast<const int2 *>(a.bsums + row * (a.cols / 16) + uint64_t(b) * 16 + 4 * c));
-            const int b0 = int(int16_t(bs.x & 0xffff)), b1 = int(int16_t(uint32_t(bs.x) >> 16));
-            const int b2 = int(int16_t(bs.y & 0xffff)), b3 = int(int16_t(uint32_t(bs.y) >> 16));
-            const int isum = sc_lo * s_lo + sc_hi * s_hi;
-            const int msum = m_lo * (b0 + b1) + m_hi * (b2 + b3);
-            const float da = __ldg(a.d + row * nb + b);
-            acc[t] += __fmul_rn(d, da) * float(isum) - __fmul_rn(dmin, da) * float(msum);
+            isum = block_lanes_sum(isum);
+            msum = block_lanes_sum(msum);
+            if (valid && c == 0) {
+                const float cb = __fsub_rn(__fmul_rn(__fmul_rn(d, da), float(isum)),
+                                           __fmul_rn(__fmul_rn(dmin, da), float(msum)));
+                acc[t] += double(cb);
+            }
         }
     } else if constexpr (TYPE == JF_TENSOR_Q6_K) {
         const int h = c >> 1, part = c & 1;
         const uint8_t * blk = p0 + block * 192;
-        const uint4 l0 = ldg16(blk + 64 * h + 32 * part);
-        const uint4 l1 = ldg16(blk + 64 * h + 32 * part + 16);
-        const uint4 h0 = ldg16(blk + 128 + 32 * h);
-        const uint4 h1 = ldg16(blk + 128 + 32 * h + 16);
-        const uint4 scv = ldg16(p1 + block * 16);
-        const float d = half_bits_to_float(uint16_t(p2[block * 2] | (p2[block * 2 + 1] << 8)));
+        const uint4 zero = make_uint4(0, 0, 0, 0);
+        const uint4 l0 = valid ? ldg16(blk + 64 * h + 32 * part) : zero;
+        const uint4 l1 = valid ? ldg16(blk + 64 * h + 32 * part + 16) : zero;
+        const uint4 h0 = valid ? ldg16(blk + 128 + 32 * h) : zero;
+        const uint4 h1 = valid ? ldg16(blk + 128 + 32 * h + 16) : zero;
+        const uint4 scv = valid ? ldg16(p1 + block * 16) : zero;
+        const float d = valid ? half_bits_to_float(uint16_t(p2[block * 2] | (p2[block * 2 + 1] << 8))) : 0.0f;
         const uint32_t L[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
         const uint32_t H[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
         int qa[8], qb[8];
@@ -132,37 +158,43 @@ __device__ __forceinline__ void lane_block(const jfb_weight & w, uint64_t block,
         for (int t = 0; t < kGroup; ++t) {
             if (t >= nt) break;
             const uint64_t row = uint64_t(t0 + t);
-            const int8_t * aq = a.qs + row * a.cols + uint64_t(b) * kQK + 128 * h + 32 * part;
-            const int4 x0 = __ldg(reinterpret_cast<const int4 *>(aq));
-            const int4 x1 = __ldg(reinterpret_cast<const int4 *>(aq + 16));
-            const int4 y0 = __ldg(reinterpret_cast<const int4 *>(aq + 64));
-            const int4 y1 = __ldg(reinterpret_cast<const int4 *>(aq + 80));
-            const int ax[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-            const int ay[8] = {y0.x, y0.y, y0.z, y0.w, y1.x, y1.y, y1.z, y1.w};
-            int s[4] = {0, 0, 0, 0};
+            int isum = 0;
+            float da = 0.0f;
+            if (valid) {
+                const int8_t * aq = a.qs + row * a.cols + uint64_t(b) * kQK + 128 * h + 32 * part;
+                const int4 x0 = __ldg(reinterpret_cast<const int4 *>(aq));
+                const int4 x1 = __ldg(reinterpret_cast<const int4 *>(aq + 16));
+                const int4 y0 = __ldg(reinterpret_cast<const int4 *>(aq + 64));
+                const int4 y1 = __ldg(reinterpret_cast<const int4 *>(aq + 80));
+                const int ax[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+                const int ay[8] = {y0.x, y0.y, y0.z, y0.w, y1.x, y1.y, y1.z, y1.w};
+                int s[4] = {0, 0, 0, 0};
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                s[0] = dp4a(qa[i], ax[i], s[0]);
-                s[1] = dp4a(qa[4 + i], ax[4 + i], s[1]);
-                s[2] = dp4a(qb[i], ay[i], s[2]);
-                s[3] = dp4a(qb[4 + i], ay[4 + i], s[3]);
+                for (int i = 0; i < 4; ++i) {
+                    s[0] = dp4a(qa[i], ax[i], s[0]);
+                    s[1] = dp4a(qa[4 + i], ax[4 + i], s[1]);
+                    s[2] = dp4a(qb[i], ay[i], s[2]);
+                    s[3] = dp4a(qb[4 + i], ay[4 + i], s[3]);
+                }
+                const int16_t * bs = a.bsums + row * (a.cols / 16) + uint64_t(b) * 16;
+                // codes are stored +32: subtract 32 * (sum of the group's activations)
+                s[0] -= 32 * int(__ldg(bs + ga));
+                s[1] -= 32 * int(__ldg(bs + ga + 1));
+                s[2] -= 32 * int(__ldg(bs + gb));
+                s[3] -= 32 * int(__ldg(bs + gb + 1));
+                isum = sa0 * s[0] + sa1 * s[1] + sb0 * s[2] + sb1 * s[3];
+                da = __ldg(a.d + row * nb + b);
             }
-            const int16_t * bs = a.bsums + row * (a.cols / 16) + uint64_t(b) * 16;
-            // codes are stored +32: subtract 32 * (sum of the group's activations)
-            s[0] -= 32 * int(__ldg(bs + ga));
-            s[1] -= 32 * int(__ldg(bs + ga + 1));
-            s[2] -= 32 * int(__ldg(bs + gb));
-            s[3] -= 32 * int(__ldg(bs + gb + 1));
-            const int isum = sa0 * s[0] + sa1 * s[1] + sb0 * s[2] + sb1 * s[3];
-            const float da = __ldg(a.d + row * nb + b);
-            acc[t] += __fmul_rn(d, da) * float(isum);
+            isum = block_lanes_sum(isum);
+            if (valid && c == 0) acc[t] += double(__fmul_rn(__fmul_rn(d, da), float(isum)));
         }
     } else {  // Q2_K
         const int h = c >> 1, sp = c & 1;
-        const uint4 c0 = ldg16(p0 + block * 64 + 32 * h);
-        const uint4 c1 = ldg16(p0 + block * 64 + 32 * h + 16);
-        const uint4 scv = ldg16(p1 + block * 16);
-        const uint32_t dd = __ldg(reinterpret_cast<const uint32_t *>(p2) + block);
+        const uint4 zero = make_uint4(0, 0, 0, 0);
+        const uint4 c0 = valid ? ldg16(p0 + block * 64 + 32 * h) : zero;
+        const uint4 c1 = valid ? ldg16(p0 + block * 64 + 32 * h + 16) : zero;
+        const uint4 scv = valid ? ldg16(p1 + block * 16) : zero;
+        const uint32_t dd = valid ? __ldg(reinterpret_cast<const uint32_t *>(p2) + block) : 0u;
         const float d = half_bits_to_float(uint16_t(dd & 0xffffu));
         const float dmin = half_bits_to_float(uint16_t(dd >> 16));
         const uint32_t Q[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
@@ -184,30 +216,39 @@ __device__ __forceinline__ void lane_block(const jfb_weight & w, uint64_t block,
         for (int t = 0; t < kGroup; ++t) {
             if (t >= nt) break;
             const uint64_t row = uint64_t(t0 + t);
-            const int8_t * aq = a.qs + row * a.cols + uint64_t(b) * kQK + 128 * h + 64 * sp;
-            const int4 x0 = __ldg(reinterpret_cast<const int4 *>(aq));
-            const int4 x1 = __ldg(reinterpret_cast<const int4 *>(aq + 16));
-            const int4 x2 = __ldg(reinterpret_cast<const int4 *>(aq + 32));
-            const int4 x3 = __ldg(reinterpret_cast<const int4 *>(aq + 48));
-            const int ax[16] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w,
-                                x2.x, x2.y, x2.z, x2.w, x3.x, x3.y, x3.z, x3.w};
-            int s[4] = {0, 0, 0, 0};
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                s[0] = dp4a(qe[i], ax[i], s[0]);
-                s[1] = dp4a(qe[4 + i], ax[4 + i], s[1]);
-                s[2] = dp4a(qo[i], ax[8 + i], s[2]);
-                s[3] = dp4a(qo[4 + i], ax[12 + i], s[3]);
-            }
-            const int16_t * bs = a.bsums + row * (a.cols / 16) + uint64_t(b) * 16 + g0;
             int isum = 0, msum = 0;
+            float da = 0.0f;
+            if (valid) {
+                const int8_t * aq = a.qs + row * a.cols + uint64_t(b) * kQK + 128 * h + 64 * sp;
+                const int4 x0 = __ldg(reinterpret_cast<const int4 *>(aq));
+                const int4 x1 = __ldg(reinterpret_cast<const int4 *>(aq + 16));
+                const int4 x2 = __ldg(reinterpret_cast<const int4 *>(aq + 32));
+                const int4 x3 = __ldg(reinterpret_cast<const int4 *>(aq + 48));
+                const int ax[16] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w,
+                                    x2.x, x2.y, x2.z, x2.w, x3.x, x3.y, x3.z, x3.w};
+                int s[4] = {0, 0, 0, 0};
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                isum += scl[k] * s[k];
-                msum += mnl[k] * int(__ldg(bs + k));
+                for (int i = 0; i < 4; ++i) {
+                    s[0] = dp4a(qe[i], ax[i], s[0]);
+                    s[1] = dp4a(qe[4 + i], ax[4 + i], s[1]);
+                    s[2] = dp4a(qo[i], ax[8 + i], s[2]);
+                    s[3] = dp4a(qo[4 + i], ax[12 + i], s[3]);
+                }
+                const int16_t * bs = a.bsums + row * (a.cols / 16) + uint64_t(b) * 16 + g0;
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    isum += scl[k] * s[k];
+                    msum += mnl[k] * int(__ldg(bs + k));
+                }
+                da = __ldg(a.d + row * nb + b);
             }
-            const float da = __ldg(a.d + row * nb + b);
-            acc[t] += __fmul_rn(d, da) * float(isum) - __fmul_rn(dmin, da) * float(msum);
+            isum = block_lanes_sum(isum);
+            msum = block_lanes_sum(msum);
+            if (valid && c == 0) {
+                const float cb = __fsub_rn(__fmul_rn(__fmul_rn(d, da), float(isum)),
+                                           __fmul_rn(__fmul_rn(dmin, da), float(msum)));
+                acc[t] += double(cb);
+            }
         }
     }
 }
@@ -221,18 +262,20 @@ __global__ void __launch_bounds__(kWarps * 32) mmv_kquant_kernel(jfb_weight w, A
     if (row >= w.rows || t0 >= n) return;
     const int nt = int(min(uint32_t(kGroup), n - t0));
     const uint32_t nb = w.cols / kQK;
-    float acc[kGroup];
+    double acc[kGroup];
 #pragma unroll
-    for (int t = 0; t < kGroup; ++t) acc[t] = 0.0f;
+    for (int t = 0; t < kGroup; ++t) acc[t] = 0.0;
     const int c = lane & 3;
-    for (uint32_t b = uint32_t(lane >> 2); b < nb; b += 8) {
-        lane_block<TYPE>(w, uint64_t(row) * nb + b, c, a, b, t0, nt, acc);
+    for (uint32_t b0 = 0; b0 < nb; b0 += 8) {  // warp-uniform trip count (the block lanes shuffle)
+        const uint32_t b = b0 + uint32_t(lane >> 2);
+        const bool valid = b < nb;
+        lane_block<TYPE>(w, uint64_t(row) * nb + (valid ? b : 0), c, a, b, t0, nt, valid, acc);
     }
 #pragma unroll
     for (int t = 0; t < kGroup; ++t) {
         if (t >= nt) break;
-        const float v = warp_sum(acc[t]);
-        if (lane == 0) store_out(v, row, t0 + t, w.rows, out, ep);
+        const double v = warp_sum(acc[t]);
+        if (lane == 0) store_out(float(v), row, t0 + t, w.rows, out, ep);
     }
 }
 
@@ -248,7 +291,7 @@ __global__ void __launch_bounds__(kWarps * 32) mmv_float_kernel(jfb_weight w, co
     const int nt = int(min(uint32_t(kGroup), n - t0));
     for (int t = 0; t < nt; ++t) {
         const float * xr = x + uint64_t(t0 + t) * w.cols;
-        float acc = 0.0f;
+        double acc = 0.0;
         for (uint32_t k = lane; k < w.cols; k += 32) {
             float wv, xv = xr[k];
             if constexpr (HALF) {
@@ -257,10 +300,10 @@ __global__ void __launch_bounds__(kWarps * 32) mmv_float_kernel(jfb_weight w, co
             } else {
                 wv = static_cast<const float *>(w.plane[0])[uint64_t(row) * w.cols + k];
             }
-            acc = fmaf(wv, xv, acc);
+            acc += double(__fmul_rn(wv, xv));  // products rounded to float, summed in double
         }
         acc = warp_sum(acc);
-        if (lane == 0) store_out(acc, row, t0 + t, w.rows, out, ep);
+        if (lane == 0) store_out(float(acc), row, t0 + t, w.rows, out, ep);
     }
 }
 

@@ -78,7 +78,7 @@ __global__ void __launch_bounds__(kThreads) quantize_kernel(const float * __rest
 // silu(g) * u with silu(g) = g / (1 + e^-g), each step rounded
 // (ggml_swiglu_split / ggml_silu + ggml_mul, qwen2_architecture.cpp:508-520).
 __device__ __forceinline__ float swiglu(float g, float u) {
-    return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+    return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, exp_cw(-g))), u);
 }
 
 __global__ void __launch_bounds__(kThreads) swiglu_quant_kernel(const float * __restrict__ gate, const float * __restrict__ up,

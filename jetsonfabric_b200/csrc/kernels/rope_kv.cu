@@ -3,47 +3,44 @@
 // qwen2_architecture.cpp:400-424, 499-506).
 //
 // GGML's rope cache builds the angle of pair i as theta_0 = position,
-// theta_{i+1} = theta_i * theta_scale in float, and rotates (x_i, x_{i+d/2}):
+// theta_{i+1} = theta_i * theta_scale in float and stores cosf/sinf of it;
+// the pair (x_i, x_{i+d/2}) becomes
 //     y_i       = x_i * cos - x_{i+d/2} * sin
 //     y_{i+d/2} = x_i * sin + x_{i+d/2} * cos
-// Every product and sum is rounded separately here (no fused multiply-add)
-// so the result matches the CPU oracle's float evaluation.
+// The (cos, sin) table is computed once on the host with the same C library
+// calls (jfb_rope_table_host) and read here; every product and sum is
+// rounded separately (no fused multiply-add) like the CPU evaluation.
 #include "common.cuh"
+
+#include <cmath>
 
 namespace jfb {
 namespace {
 
 constexpr int kThreads = 128;
-constexpr int kMaxPairs = 256;  // rope_dims up to 512
 
 __global__ void __launch_bounds__(kThreads) rope_kv_kernel(float * __restrict__ q, const float * __restrict__ k,
                                                          const float * __restrict__ v, const int32_t * __restrict__ seq,
                                                          const int32_t * __restrict__ pos, uint32_t heads,
                                                          uint32_t kv_heads, uint32_t head_dim, uint32_t rope_dims,
-                                                         float theta_scale, const jfb_kv_slot * __restrict__ slots,
-                                                         uint32_t layer) {
-    __shared__ float cos_s[kMaxPairs], sin_s[kMaxPairs];
+                                                         const float2 * __restrict__ table, uint32_t table_positions,
+                                                         const jfb_kv_slot * __restrict__ slots, uint32_t layer) {
     const uint32_t r = blockIdx.x;
     const int32_t p = pos[r];
     const jfb_kv_slot slot = slots[seq[r]];
+    if (p < 0 || uint32_t(p) >= slot.capacity || uint32_t(p) >= table_positions) return;  // never issued by the engine
     const uint32_t pairs = rope_dims / 2;
-    for (uint32_t i = threadIdx.x; i < pairs; i += kThreads) {
-        float theta = float(p);
-        for (uint32_t s = 0; s < i; ++s) theta = __fmul_rn(theta, theta_scale);
-        cos_s[i] = cosf(theta);
-        sin_s[i] = sinf(theta);
-    }
-    __syncthreads();
+    const float2 * cs = table + uint64_t(p) * pairs;
     const uint32_t hd = heads * head_dim, kvd = kv_heads * head_dim;
     float * qr = q + uint64_t(r) * hd;
     for (uint32_t idx = threadIdx.x; idx < heads * pairs; idx += kThreads) {
         const uint32_t h = idx / pairs, i = idx % pairs;
         float * x = qr + h * head_dim;
+        const float2 c = cs[i];
         const float x0 = x[i], x1 = x[i + pairs];
-        x[i] = __fsub_rn(__fmul_rn(x0, cos_s[i]), __fmul_rn(x1, sin_s[i]));
-        x[i + pairs] = __fadd_rn(__fmul_rn(x0, sin_s[i]), __fmul_rn(x1, cos_s[i]));
+        x[i] = __fsub_rn(__fmul_rn(x0, c.x), __fmul_rn(x1, c.y));
+        x[i + pairs] = __fadd_rn(__fmul_rn(x0, c.y), __fmul_rn(x1, c.x));
     }
-    if (p < 0 || uint32_t(p) >= slot.capacity) return;  // the engine never issues these
     const uint64_t row = (uint64_t(layer) * slot.capacity + uint64_t(p)) * kvd;
     const float * kr = k + uint64_t(r) * kvd;
     const float * vr = v + uint64_t(r) * kvd;
@@ -52,9 +49,10 @@ __global__ void __launch_bounds__(kThreads) rope_kv_kernel(float * __restrict__ 
         float y;
         if (e < rope_dims) {
             const uint32_t i = e % pairs;
+            const float2 c = cs[i];
             const float x0 = kr[h * head_dim + i], x1 = kr[h * head_dim + i + pairs];
-            y = e < pairs ? __fsub_rn(__fmul_rn(x0, cos_s[i]), __fmul_rn(x1, sin_s[i]))
-                          : __fadd_rn(__fmul_rn(x0, sin_s[i]), __fmul_rn(x1, cos_s[i]));
+            y = e < pairs ? __fsub_rn(__fmul_rn(x0, c.x), __fmul_rn(x1, c.y))
+                          : __fadd_rn(__fmul_rn(x0, c.y), __fmul_rn(x1, c.x));
         } else {
             y = kr[idx];
         }
@@ -68,19 +66,35 @@ __global__ void __launch_bounds__(kThreads) rope_kv_kernel(float * __restrict__ 
 
 using namespace jfb;
 
+extern "C" void jfb_rope_table_host(float * table, uint32_t positions, uint32_t rope_dims, float freq_base) {
+    const uint32_t pairs = rope_dims / 2;
+    const float theta_scale = ::powf(freq_base, -2.0f / float(rope_dims));
+    for (uint32_t p = 0; p < positions; ++p) {
+        float theta = float(p);
+        float * row = table + uint64_t(p) * pairs * 2;
+        for (uint32_t i = 0; i < pairs; ++i) {
+            row[2 * i] = ::cosf(theta);
+            row[2 * i + 1] = ::sinf(theta);
+            theta = theta * theta_scale;
+        }
+    }
+}
+
 extern "C" jfb_status jfb_rope_kv_append(float * q, const float * k, const float * v, uint32_t n, const int32_t * seq,
                                          const int32_t * pos, uint32_t heads, uint32_t kv_heads, uint32_t head_dim,
-                                         uint32_t rope_dims, float theta_scale, const jfb_kv_slot * slots,
-                                         uint32_t layer, void * stream) {
-    if (q == nullptr || k == nullptr || v == nullptr || seq == nullptr || pos == nullptr || slots == nullptr) {
+                                         uint32_t rope_dims, const float * rope_table, uint32_t table_positions,
+                                         const jfb_kv_slot * slots, uint32_t layer, void * stream) {
+    if (q == nullptr || k == nullptr || v == nullptr || seq == nullptr || pos == nullptr || slots == nullptr ||
+        rope_table == nullptr) {
         return status_error(JFB_STATUS_INVALID_ARGUMENT, "rope/kv append operands are required");
     }
     if (heads == 0 || kv_heads == 0 || heads % kv_heads != 0 || head_dim == 0 || rope_dims == 0 ||
-        rope_dims > head_dim || rope_dims % 2 != 0 || rope_dims / 2 > uint32_t(kMaxPairs)) {
+        rope_dims > head_dim || rope_dims % 2 != 0) {
         return status_error(JFB_STATUS_INVALID_ARGUMENT, "rope/kv append dimensions are inconsistent");
     }
     if (n == 0) return status_ok();
     rope_kv_kernel<<<n, kThreads, 0, as_stream(stream)>>>(q, k, v, seq, pos, heads, kv_heads, head_dim, rope_dims,
-                                                          theta_scale, slots, layer);
+                                                          reinterpret_cast<const float2 *>(rope_table), table_positions,
+                                                          slots, layer);
     return launch_status("jfb_rope_kv_append");
 }

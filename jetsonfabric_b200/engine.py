@@ -189,13 +189,17 @@ class GenerationResult:
 
 
 class NativeSession:
+    """A session; it must not outlive its engine, so NativeEngine.close()
+    closes every session still open on it first."""
+
     def __init__(self, engine: "NativeEngine", handle: C.c_void_p):
         self.engine = engine
         self._h = handle
 
     def close(self) -> None:
         if self._h:
-            lib().jfb_session_close(self._h)
+            if self.engine._h:
+                lib().jfb_session_close(self._h)
             self._h = C.c_void_p()
 
     def __del__(self):
@@ -233,9 +237,15 @@ class NativeSession:
                                                 0 if acts is None else acts.size))
         return self._result(out, acts)
 
+    def _check_activation(self, a: np.ndarray) -> None:
+        # f32[sequence_length, hidden_size] (runtime/adapters/native_stage_executor.cpp:16-45)
+        if a.ndim != 2 or a.shape[0] == 0 or a.shape[1] != self.engine.hidden:
+            raise InvalidArgument("native stage activation shape is invalid")
+
     def prefill_stage_activations(self, activation: np.ndarray) -> StageResult:
         a = np.ascontiguousarray(activation, dtype=np.float32)
-        rows = a.shape[0] if a.ndim == 2 else 0
+        self._check_activation(a)
+        rows = a.shape[0]
         acts = self._acts(max(rows, 1))
         out = StageOutputC()
         check(lib().jfb_session_prefill_activations(self._h, a.ctypes.data, rows, C.byref(out),
@@ -253,7 +263,8 @@ class NativeSession:
 
     def decode_stage_activation(self, activation: np.ndarray) -> StageResult:
         a = np.ascontiguousarray(activation, dtype=np.float32)
-        if a.ndim != 2 or a.shape[0] != 1:
+        self._check_activation(a)
+        if a.shape[0] != 1:
             raise InvalidArgument("native decode activation must contain one token row")
         acts = self._acts(1)
         out = StageOutputC()
@@ -288,6 +299,8 @@ class NativeEngine:
                              ATTENTION_KERNELS[decode_attention_kernel], threads, layer_start,
                              0xFFFFFFFF if layer_end is None else layer_end, device)
         handle = C.c_void_p()
+        import weakref
+        self._sessions = weakref.WeakSet()
         check(lib().jfb_engine_open(str(package_path).encode(), C.byref(opts), C.byref(handle)))
         self._h = handle
         info = ModelInfoC()
@@ -300,6 +313,8 @@ class NativeEngine:
 
     def close(self) -> None:
         if getattr(self, "_h", None):
+            for s in list(self._sessions):
+                s.close()
             lib().jfb_engine_close(self._h)
             self._h = C.c_void_p()
 
@@ -338,7 +353,9 @@ class NativeEngine:
     def create_session(self, capacity: int) -> NativeSession:
         h = C.c_void_p()
         check(lib().jfb_session_open(self._h, int(capacity), C.byref(h)))
-        return NativeSession(self, h)
+        session = NativeSession(self, h)
+        self._sessions.add(session)
+        return session
 
     def logits(self, tokens: Sequence[int]) -> np.ndarray:
         t = _i32(tokens)

@@ -46,7 +46,8 @@ def _bind():
         "jfb_swiglu_quant": ([_VP, _VP, C.c_uint32, C.c_uint32, _VP, C.POINTER(Q8K), _VP], Status),
         "jfb_matmul": ([C.POINTER(Weight), C.POINTER(Q8K), _VP, C.c_uint32, C.c_uint32, _VP, _VP, _VP, _VP], Status),
         "jfb_rope_kv_append": ([_VP, _VP, _VP, C.c_uint32, _VP, _VP, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32,
-                                C.c_float, _VP, C.c_uint32, _VP], Status),
+                                _VP, C.c_uint32, _VP, C.c_uint32, _VP], Status),
+        "jfb_rope_table_host": ([_VP, C.c_uint32, C.c_uint32, C.c_float], None),
         "jfb_attention_scratch_bytes": ([C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32], C.c_uint64),
         "jfb_attention": ([_VP, C.c_uint32, _VP, _VP, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, _VP, C.c_uint32,
                            _VP, C.c_uint64, _VP, C.POINTER(Q8K), _VP], Status),
@@ -143,9 +144,18 @@ def attention_scratch_bytes(n, heads, head_dim, max_keys) -> int:
     return int(_bind().jfb_attention_scratch_bytes(n, heads, head_dim, max_keys))
 
 
-def rope_kv_append(q, k, v, seq, pos, heads, kv_heads, head_dim, rope_dims, theta_scale, slots, layer):
+def rope_table(positions: int, rope_dims: int, freq_base: float):
+    """Host-built GGML rope cache (cos, sin) [positions][rope_dims/2][2] as a CUDA tensor."""
+    import numpy as np
+    import torch
+    t = np.empty((positions, rope_dims // 2, 2), dtype=np.float32)
+    _bind().jfb_rope_table_host(t.ctypes.data, positions, rope_dims, freq_base)
+    return torch.from_numpy(t).cuda()
+
+
+def rope_kv_append(q, k, v, seq, pos, heads, kv_heads, head_dim, rope_dims, table, slots, layer):
     check(_bind().jfb_rope_kv_append(ptr(q), ptr(k), ptr(v), q.shape[0], ptr(seq), ptr(pos), heads, kv_heads,
-                                     head_dim, rope_dims, theta_scale, ptr(slots), layer, stream_ptr()))
+                                     head_dim, rope_dims, ptr(table), table.shape[0], ptr(slots), layer, stream_ptr()))
 
 
 def attention(q, seq, pos, heads, kv_heads, head_dim, max_keys, slots, layer, scratch, out, out_q8=None):

@@ -70,6 +70,12 @@ def lib() -> C.CDLL:
         L.orc_rope_neox.argtypes = [C.c_void_p, C.c_int64, C.c_int64, C.c_int64, C.c_int32, C.c_float]
         L.orc_argmax.argtypes = [C.c_void_p, C.c_int64]
         L.orc_argmax.restype = C.c_int32
+        L.orc_expf.argtypes = [C.c_float]
+        L.orc_expf.restype = C.c_float
+        L.orc_silu_mul.argtypes = [C.c_float, C.c_float]
+        L.orc_silu_mul.restype = C.c_float
+        L.orc_attention_row.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_int64, C.c_int64,
+                                        C.c_int64, C.c_void_p]
         L.orc_f32_to_f16.argtypes = [C.c_float]
         L.orc_f32_to_f16.restype = C.c_uint16
         L.orc_codec_float_to_half.argtypes = [C.c_float]

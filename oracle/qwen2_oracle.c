@@ -42,6 +42,36 @@ void orc_set_threads(int threads) {
 #endif
 }
 
+/* ---- exp ------------------------------------------------------------------
+ * exp(x) by Cody-Waite argument reduction (x = n ln2 + r, ln2 split in a
+ * short high part and a correction) and the degree-7 Taylor polynomial of
+ * e^r in Horner form with fused multiply-adds, then an exact two-step scaling
+ * by 2^n. Used for softmax and SiLU. The CUDA library implements the same
+ * method in its own code, so both produce identical bits (fmaf, rintf and the
+ * float multiplications are correctly rounded on both). */
+static float bitsf(uint32_t u);
+static float pow2i(int e) { return bitsf((uint32_t) (e + 127) << 23); }  /* 2^e, -126 <= e <= 127 */
+
+float orc_expf(float x) {
+    if (x != x) return x;
+    if (x > 88.72283935546875f) return INFINITY;
+    if (x < -103.972084045410156f) return 0.0f;
+    const float n = rintf(x * 1.44269502162933349609375f);
+    float r = fmaf(-n, 0.693145751953125f, x);
+    r = fmaf(-n, 1.4286068203094172e-06f, r);
+    float p = 1.98412701138295233e-04f;            /* 1/7! */
+    p = fmaf(p, r, 1.38888892251998186e-03f);      /* 1/6! */
+    p = fmaf(p, r, 8.33333376795053482e-03f);      /* 1/5! */
+    p = fmaf(p, r, 4.16666679084300995e-02f);      /* 1/4! */
+    p = fmaf(p, r, 1.66666671633720398e-01f);      /* 1/3! */
+    p = fmaf(p, r, 0.5f);
+    p = fmaf(p, r, 1.0f);
+    p = fmaf(p, r, 1.0f);
+    const int e = (int) n;
+    const int e1 = e / 2, e2 = e - e1;
+    return (p * pow2i(e1)) * pow2i(e2);
+}
+
 /* ---- binary16 (IEEE 754, round to nearest even) ------------------------ */
 
 static uint32_t fbits(float f) { uint32_t u; memcpy(&u, &f, 4); return u; }
@@ -262,8 +292,13 @@ void orc_quantize_row_q8_k(const float * x, void * blocks, int64_t k) {
  * scaled by the 6/4-bit sub-block scales, then one float scale per 256-block:
  *   sum += (d_w*d_a)*isum - (dmin_w*d_a)*msum. */
 
+/* The per-block contributions are rounded to float exactly as written and
+ * summed in double, which makes the row result independent of the order in
+ * which blocks are added (the double sum of up to a few hundred floats is
+ * exact or off by far less than a float ulp), so a GPU reduction in any order
+ * reproduces it bit for bit. */
 static float dot_q4_k(const uint8_t * w, const q8k_block * a, int64_t nb) {
-    float sum = 0.0f;
+    double sum = 0.0;
     for (int64_t b = 0; b < nb; ++b, w += 144) {
         const uint8_t * qs = w + 16;
         int32_t isum = 0, msum = 0;
@@ -281,13 +316,14 @@ static float dot_q4_k(const uint8_t * w, const q8k_block * a, int64_t nb) {
         memcpy(&hm, w + 2, 2);
         const float d = orc_f16_to_f32(hd) * a[b].d;
         const float dmin = orc_f16_to_f32(hm) * a[b].d;
-        sum += d * (float) isum - dmin * (float) msum;
+        const float c = d * (float) isum - dmin * (float) msum;
+        sum += (double) c;
     }
-    return sum;
+    return (float) sum;
 }
 
 static float dot_q6_k(const uint8_t * w, const q8k_block * a, int64_t nb) {
-    float sum = 0.0f;
+    double sum = 0.0;
     for (int64_t b = 0; b < nb; ++b, w += 210) {
         const int8_t * sc = (const int8_t *) (w + 192);
         int32_t isum = 0;
@@ -298,13 +334,14 @@ static float dot_q6_k(const uint8_t * w, const q8k_block * a, int64_t nb) {
         }
         uint16_t hd;
         memcpy(&hd, w + 208, 2);
-        sum += (orc_f16_to_f32(hd) * a[b].d) * (float) isum;
+        const float c = (orc_f16_to_f32(hd) * a[b].d) * (float) isum;
+        sum += (double) c;
     }
-    return sum;
+    return (float) sum;
 }
 
 static float dot_q2_k(const uint8_t * w, const q8k_block * a, int64_t nb) {
-    float sum = 0.0f;
+    double sum = 0.0;
     for (int64_t b = 0; b < nb; ++b, w += 84) {
         int32_t isum = 0, msum = 0;
         for (int g = 0; g < 16; ++g) {
@@ -318,9 +355,10 @@ static float dot_q2_k(const uint8_t * w, const q8k_block * a, int64_t nb) {
         memcpy(&hm, w + 82, 2);
         const float d = orc_f16_to_f32(hd) * a[b].d;
         const float dmin = orc_f16_to_f32(hm) * a[b].d;
-        sum += d * (float) isum - dmin * (float) msum;
+        const float c = d * (float) isum - dmin * (float) msum;
+        sum += (double) c;
     }
-    return sum;
+    return (float) sum;
 }
 
 /* ggml_mul_mat on the CPU backend (qwen2_architecture.cpp:347-371 builds it):
@@ -476,51 +514,61 @@ static int fail_with(char * error, size_t size, const char * message) {
     return -1;
 }
 
-/* Attention of rows [0, n) at absolute positions p0 + t against cache keys
- * [0, p0 + t] (the -inf mask of qwen2_architecture.cpp:697-708 removes the
- * rest). Scores: K (f16) . q rounded to f16, accumulated in f32
- * (ggml_vec_dot_f16 with src1 converted to F16); soft_max_ext with scale
- * 1/sqrt(head_length): x*scale + mask, exp(x - max), sum in double,
- * p = e * (float)(1/sum); P rounded to f16 before the V product (src1 of the
- * second mul_mat is converted to F16); output accumulated in f32. GQA:
- * query head h reads kv head h / (H / KVH) (ggml_mul_mat broadcast). */
-static void attention(const orc_model * m, const uint16_t * kc, const uint16_t * vc, const float * q,
-                      size_t n, size_t p0, float * out) {
-    const int64_t H = m->head_count, KVH = m->kv_head_count;
-    const int64_t hl = (int64_t) m->embedding_length / H, kvd = hl * KVH, group = H / KVH;
+/* Attention of one query row at absolute position pos against cache keys
+ * [0, pos] (the -inf mask of qwen2_architecture.cpp:697-708 removes the
+ * rest). Scores: K (f16) . q rounded to f16, the products (exact in float)
+ * summed in double and rounded to float once (ggml_vec_dot_f16 with src1
+ * converted to F16, f32 result); soft_max_ext with scale 1/sqrt(head_dim):
+ * x = score*scale, e = exp(x - max), sum in double, p = e * (float)(1/sum),
+ * P rounded to f16 before the V product (src1 of the second mul_mat is
+ * converted to F16); output = sum of exact f16*f16 products in double,
+ * rounded once. GQA: query head h reads kv head h / (heads / kv_heads)
+ * (ggml_mul_mat broadcast). */
+void orc_attention_row(const float * q, const uint16_t * kc, const uint16_t * vc, int64_t pos, int64_t H,
+                       int64_t KVH, int64_t hl, float * out) {
+    const int64_t kvd = hl * KVH, group = H / KVH, keys = pos + 1;
     const float scale = 1.0f / sqrtf((float) hl);
-#pragma omp parallel for collapse(2) schedule(dynamic)
-    for (int64_t t = 0; t < (int64_t) n; ++t) {
-        for (int64_t h = 0; h < H; ++h) {
-            const int64_t keys = (int64_t) p0 + t + 1;
-            const int64_t g = h / group;
-            float qh[512];
-            for (int64_t d = 0; d < hl; ++d) qh[d] = orc_f16_to_f32(orc_f32_to_f16(q[t * m->embedding_length + h * hl + d]));
-            float * p = malloc(sizeof(float) * (size_t) keys);
-            float mx = -INFINITY;
-            for (int64_t j = 0; j < keys; ++j) {
-                const uint16_t * kr = kc + j * kvd + g * hl;
-                double s = 0.0;
-                for (int64_t d = 0; d < hl; ++d) s += (double) (orc_f16_to_f32(kr[d]) * qh[d]);
-                p[j] = (float) s * scale;
-                if (p[j] > mx) mx = p[j];
-            }
-            double sum = 0.0;
-            for (int64_t j = 0; j < keys; ++j) {
-                p[j] = expf(p[j] - mx);
-                sum += (double) p[j];
-            }
-            const float inv = (float) (1.0 / sum);
-            for (int64_t j = 0; j < keys; ++j) p[j] = orc_f16_to_f32(orc_f32_to_f16(p[j] * inv));
-            for (int64_t d = 0; d < hl; ++d) {
-                double acc = 0.0;
-                for (int64_t j = 0; j < keys; ++j) acc += (double) (orc_f16_to_f32(vc[j * kvd + g * hl + d]) * p[j]);
-                out[t * m->embedding_length + h * hl + d] = (float) acc;
-            }
-            free(p);
+    float * p = malloc(sizeof(float) * (size_t) keys);
+    float qh[512];
+    for (int64_t h = 0; h < H; ++h) {
+        const int64_t g = h / group;
+        for (int64_t d = 0; d < hl; ++d) qh[d] = orc_f16_to_f32(orc_f32_to_f16(q[h * hl + d]));
+        float mx = -INFINITY;
+        for (int64_t j = 0; j < keys; ++j) {
+            const uint16_t * kr = kc + j * kvd + g * hl;
+            double s = 0.0;
+            for (int64_t d = 0; d < hl; ++d) s += (double) (orc_f16_to_f32(kr[d]) * qh[d]);
+            p[j] = (float) s * scale;
+            if (p[j] > mx) mx = p[j];
+        }
+        double sum = 0.0;
+        for (int64_t j = 0; j < keys; ++j) {
+            p[j] = orc_expf(p[j] - mx);
+            sum += (double) p[j];
+        }
+        const float inv = (float) (1.0 / sum);
+        for (int64_t j = 0; j < keys; ++j) p[j] = orc_f16_to_f32(orc_f32_to_f16(p[j] * inv));
+        for (int64_t d = 0; d < hl; ++d) {
+            double acc = 0.0;
+            for (int64_t j = 0; j < keys; ++j) acc += (double) (orc_f16_to_f32(vc[j * kvd + g * hl + d]) * p[j]);
+            out[h * hl + d] = (float) acc;
         }
     }
+    free(p);
 }
+
+static void attention(const orc_model * m, const uint16_t * kc, const uint16_t * vc, const float * q,
+                      size_t n, size_t p0, float * out) {
+    const int64_t H = m->head_count, KVH = m->kv_head_count, hl = (int64_t) m->embedding_length / H;
+#pragma omp parallel for schedule(dynamic)
+    for (int64_t t = 0; t < (int64_t) n; ++t) {
+        orc_attention_row(q + t * m->embedding_length, kc, vc, (int64_t) p0 + t, H, KVH, hl,
+                          out + t * m->embedding_length);
+    }
+}
+
+/* silu(g) * u with silu(g) = g / (1 + e^-g) (ggml_swiglu_split / ggml_silu). */
+float orc_silu_mul(float g, float u) { return (g / (1.0f + orc_expf(-g))) * u; }
 
 /* One transformer layer over n rows (qwen2_architecture.cpp:575-583). */
 static void layer_forward(orc_session * s, size_t li, float * hidden, size_t n, size_t p0) {
@@ -565,7 +613,7 @@ static void layer_forward(orc_session * s, size_t li, float * hidden, size_t n, 
     /* swiglu / silu*mul (qwen2_architecture.cpp:508-520): silu(g) = g/(1+e^-g) */
     for (size_t i = 0; i < n * (size_t) f; ++i) {
         const float g = gate[i];
-        gate[i] = (g / (1.0f + expf(-g))) * up[i];
+        gate[i] = orc_silu_mul(g, up[i]);
     }
     orc_matmul(&L->ffn_down, gate, (int64_t) n, o);
     for (size_t i = 0; i < n * (size_t) h; ++i) hidden[i] = o[i] + hidden[i];

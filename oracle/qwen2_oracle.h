@@ -72,6 +72,13 @@ void orc_rope_neox(float * x, int64_t heads, int64_t head_length, int64_t dims, 
                    float freq_base);
 int32_t orc_argmax(const float * x, int64_t n);
 uint16_t orc_f32_to_f16(float value);
+/* exp by Cody-Waite reduction + degree-7 Taylor polynomial (see the .c file) */
+float orc_expf(float x);
+float orc_silu_mul(float g, float u);
+/* Attention of one query row (heads*head_dim floats, already rotated) at
+ * absolute position pos over token-major f16 caches [pos+1][kv_heads*head_dim]. */
+void orc_attention_row(const float * q, const uint16_t * k_cache, const uint16_t * v_cache, int64_t pos,
+                       int64_t heads, int64_t kv_heads, int64_t head_dim, float * out);
 float orc_f16_to_f32(uint16_t value);
 /* The reference's F16 activation codec (builtin_activation_codecs.cpp:51-137). */
 uint16_t orc_codec_float_to_half(float value);

@@ -10,7 +10,8 @@ Mirrors the reference's engine tests:
 and adds the quantized-model parity the north star asks for: greedy token
 streams identical to the CPU oracle (the GGML-CPU restatement) with per-step
 logits within 2e-2 max-abs and 1e-3 relative (relative = L2 norm of the
-difference over L2 norm of the oracle logits).
+difference over L2 norm of the oracle logits). The engine reproduces the
+oracle's arithmetic exactly, so the logits are also checked for bit equality.
 """
 from __future__ import annotations
 
@@ -39,6 +40,7 @@ def check_logits(got: np.ndarray, ref: np.ndarray):
     max_abs = float(np.abs(got - ref).max())
     rel = float(np.linalg.norm(got - ref) / max(np.linalg.norm(ref), 1e-30))
     assert max_abs <= LOGIT_MAX_ABS and rel <= LOGIT_REL, (max_abs, rel)
+    assert np.array_equal(got.view(np.uint32), ref.view(np.uint32)), ("not bit-identical", max_abs, rel)
     return max_abs, rel
 
 
