@@ -157,6 +157,32 @@ jfb_status jfb_attention(const float * q, uint32_t n, const int32_t * seq, const
                          uint32_t layer, void * scratch, uint64_t scratch_bytes, float * out,
                          const jfb_q8k * out_q8, void * stream);
 
+/* Attention for callers that cannot allocate device memory.
+ *
+ * No counterpart in the reference. Same computation and arguments as
+ * jfb_attention, minus the scratch buffer: the scratch comes from a
+ * file-scope device array of JFB_ATTENTION_STATIC_SCRATCH_BYTES that every
+ * GPU loading this library holds until the process exits. It serves callers
+ * that may not call cudaMalloc at all: a stage hosted inside a process whose
+ * device memory is owned by another allocator (a framework's caching pool
+ * that must see every byte), or a latency-critical step where cudaMalloc's
+ * implicit device synchronisation is not acceptable.
+ *
+ * The first call on a device looks up the array's device address
+ * (cudaGetSymbolAddress, which may load the module); make that first call
+ * before any stream capture. Calls that need more scratch than the array
+ * holds (see jfb_attention_scratch_bytes) are rejected with
+ * JFB_STATUS_INVALID_ARGUMENT. All calls on a device share the one array and
+ * the array keeps the last call's contents; nothing in it needs to start at
+ * zero (each call writes every scratch value before reading it). Calls whose
+ * work overlaps on the GPU (different streams, or host threads without
+ * ordering) race on the array. */
+#define JFB_ATTENTION_STATIC_SCRATCH_BYTES (16u * 1024u * 1024u)
+jfb_status jfb_attention_static_scratch(const float * q, uint32_t n, const int32_t * seq, const int32_t * pos,
+                                        uint32_t heads, uint32_t kv_heads, uint32_t head_dim, uint32_t max_keys,
+                                        const jfb_kv_slot * slots, uint32_t layer, float * out,
+                                        const jfb_q8k * out_q8, void * stream);
+
 /* First index of the maximum of each row (ggml_argmax, qwen2_architecture.cpp:594). */
 jfb_status jfb_argmax(const float * logits, uint32_t n, uint32_t cols, int32_t * out, void * stream);
 

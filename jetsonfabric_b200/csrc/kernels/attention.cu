@@ -22,6 +22,8 @@
 // share its kv head, so each K and V row is read once for G heads.
 #include "common.cuh"
 
+#include <mutex>
+
 namespace jfb {
 namespace {
 
@@ -289,4 +291,62 @@ extern "C" jfb_status jfb_attention(const float * q, uint32_t n, const int32_t *
     const jfb_q8k q8 = out_q8 != nullptr ? *out_q8 : jfb_q8k{nullptr, nullptr, nullptr};
     combine_kernel<<<n, 256, 0, s>>>(pos, heads, head_dim, splits, sc, out, q8, out_q8 != nullptr);
     return launch_status("jfb_attention");
+}
+
+// ---- attention without caller-provided scratch --------------------------------
+
+// The scratch of jfb_attention_static_scratch: allocated with the module on
+// every device that loads this library, never by a call.
+static __device__ __align__(256) unsigned char g_attention_scratch[JFB_ATTENTION_STATIC_SCRATCH_BYTES];
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mutex;
+void * g_scratch_address[kMaxDevices] = {};
+
+// Device address of g_attention_scratch on the current device. In host code
+// the symbol's name is only a host-side handle, so the address is looked up
+// once per device with that device current, and cached.
+jfb_status static_scratch_address(void ** address) {
+    int device = -1;
+    cudaError_t e = cudaGetDevice(&device);
+    if (e != cudaSuccess) return status_error(JFB_STATUS_CUDA_ERROR, "cudaGetDevice: %s", cudaGetErrorString(e));
+    if (device < 0 || device >= kMaxDevices) {
+        return status_error(JFB_STATUS_UNSUPPORTED, "device ordinal %d is beyond the static scratch table", device);
+    }
+    std::lock_guard lock(g_scratch_mutex);
+    if (g_scratch_address[device] == nullptr) {
+        void * p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_attention_scratch);
+        if (e != cudaSuccess || p == nullptr) {
+            return status_error(JFB_STATUS_CUDA_ERROR, "cudaGetSymbolAddress(attention scratch): %s",
+                                cudaGetErrorString(e));
+        }
+        g_scratch_address[device] = p;
+    }
+    *address = g_scratch_address[device];
+    return status_ok();
+}
+
+}  // namespace
+
+extern "C" jfb_status jfb_attention_static_scratch(const float * q, uint32_t n, const int32_t * seq, const int32_t * pos,
+                                                   uint32_t heads, uint32_t kv_heads, uint32_t head_dim,
+                                                   uint32_t max_keys, const jfb_kv_slot * slots, uint32_t layer,
+                                                   float * out, const jfb_q8k * out_q8, void * stream) {
+    if (heads == 0 || head_dim == 0 || max_keys == 0) {
+        return status_error(JFB_STATUS_INVALID_ARGUMENT, "attention dimensions are unsupported");
+    }
+    const uint64_t needed = jfb_attention_scratch_bytes(n, heads, head_dim, max_keys);
+    if (needed > JFB_ATTENTION_STATIC_SCRATCH_BYTES) {
+        return status_error(JFB_STATUS_INVALID_ARGUMENT,
+                            "attention needs %llu scratch bytes, more than the %u-byte static scratch array",
+                            static_cast<unsigned long long>(needed), JFB_ATTENTION_STATIC_SCRATCH_BYTES);
+    }
+    void * scratch = nullptr;
+    const jfb_status s = static_scratch_address(&scratch);
+    if (s.code != JFB_STATUS_OK) return s;
+    return jfb_attention(q, n, seq, pos, heads, kv_heads, head_dim, max_keys, slots, layer, scratch,
+                         JFB_ATTENTION_STATIC_SCRATCH_BYTES, out, out_q8, stream);
 }
