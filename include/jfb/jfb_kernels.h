@@ -120,6 +120,33 @@ jfb_status jfb_matmul(const jfb_weight * weight, const jfb_q8k * x_q8, const flo
                       uint32_t epilogue, const float * bias, const float * residual, float * out,
                       void * stream);
 
+/* The same product as jfb_matmul for K-quant weights (Q4_K, Q6_K, Q2_K) on
+ * the tcgen05 tensor cores, bit-identical to it for every input. Per 256-value
+ * block the weight operand holds integer scale*code values in f16 and the
+ * activation operand the Q8_K codes in f16. Each f32 accumulator chain is
+ * bounded below 2^24 in magnitude, so it holds an exact integer sum:
+ *   - Q4_K: one accumulator per 128-value half;
+ *   - Q6_K: the 8-bit scale is split into 16*hi + lo, with two operands and
+ *     two accumulators;
+ *   - Q4_K and Q2_K: the mins term is one more K=16 product of the mins with
+ *     the Q8_K partial sums.
+ * The epilogue applies the per-block float terms exactly as the CPU rounds
+ * them and sums them in double. The kernel is persistent: one CTA per SM walks
+ * a contiguous range of (tile, block) work (stream-K, tiles of 128 weight rows
+ * x 32 activation rows). A tile shared by several CTAs is finished by the last
+ * contributor, which sums the double partials in CTA order.
+ *
+ * The workspace holds the partials and the per-tile arrival counters. It must
+ * be zero-filled before its first use; every successful call leaves it that
+ * way, and a call that reports an error through error_flag may not, so clear
+ * it again after one. error_flag (may be NULL) receives a nonzero code when a
+ * bounded pipeline wait gave up. */
+int jfb_matmul_tc_supported(const jfb_weight * weight);
+uint64_t jfb_matmul_tc_workspace_bytes(uint32_t rows, uint32_t cols, uint32_t n);
+jfb_status jfb_matmul_tc(const jfb_weight * weight, const jfb_q8k * x_q8, uint32_t n, uint32_t epilogue,
+                         const float * bias, const float * residual, float * out, void * workspace,
+                         uint64_t workspace_bytes, int32_t * error_flag, void * stream);
+
 /* NEOX rotary embedding of q and k plus the F16 KV-cache append
  * (ggml_rope_ext NEOX + ggml_set_rows, qwen2_architecture.cpp:400-424,
  * 499-506). Row r belongs to slots[seq[r]] at absolute position pos[r]; its K

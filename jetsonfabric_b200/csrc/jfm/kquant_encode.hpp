@@ -15,9 +15,10 @@
 // The encoders are this project's own (min/max affine fit per sub-block, then
 // 6-bit or 4-bit quantization of the sub-block scales); they do not reproduce
 // GGML's iterative quantizers, which is fine because the packages they write
-// are decoded by the same published formulas on every side. Q6_K scales are
-// kept in [0, 63], so every product scale*(q-32) stays within +-2016 and is
-// exactly representable in binary16 (the tensor-core GEMM relies on this).
+// are decoded by the same published formulas on every side. Q6_K scales use
+// the whole signed int8 range the way GGML's do: each group's scale carries
+// the sign that maps its largest-magnitude value to code -32 (the wide side of
+// [-32, 31]), and d maps the block's largest group scale to -128.
 #pragma once
 
 #include "half.hpp"
@@ -81,23 +82,25 @@ inline void encode_q4_k(const float * x, std::uint8_t * out) {
 
 inline void encode_q6_k(const float * x, std::uint8_t * out) {
     float scale[16];
-    float max_scale = 0.0f;
+    float max_scale = 0.0f;  // the signed group scale of largest magnitude
     for (int g = 0; g < 16; ++g) {
-        float amax = 0.0f;
-        for (int l = 0; l < 16; ++l) amax = std::max(amax, std::fabs(x[16 * g + l]));
-        scale[g] = amax / 31.0f;
-        max_scale = std::max(max_scale, scale[g]);
+        float peak = 0.0f;
+        for (int l = 0; l < 16; ++l) {
+            if (std::fabs(x[16 * g + l]) > std::fabs(peak)) peak = x[16 * g + l];
+        }
+        scale[g] = -peak / 32.0f;
+        if (std::fabs(scale[g]) > std::fabs(max_scale)) max_scale = scale[g];
     }
-    const std::uint16_t d16 = float_to_half_rne(max_scale / 63.0f);
+    const std::uint16_t d16 = float_to_half_rne(-max_scale / 128.0f);
     const float d = half_to_float(d16);
     std::uint8_t * ql = out;
     std::uint8_t * qh = out + 128;
     std::int8_t * sc = reinterpret_cast<std::int8_t *>(out + 192);
     std::memset(out, 0, 192);
-    for (int g = 0; g < 16; ++g) sc[g] = static_cast<std::int8_t>(d > 0.0f ? round_clamp(scale[g] / d, 0, 63) : 0);
+    for (int g = 0; g < 16; ++g) sc[g] = static_cast<std::int8_t>(d != 0.0f ? round_clamp(scale[g] / d, -128, 127) : 0);
     for (int e = 0; e < kBlock; ++e) {
         const float step = d * static_cast<float>(sc[e / 16]);
-        const int q = (step > 0.0f ? round_clamp(x[e] / step, -32, 31) : 0) + 32;
+        const int q = (step != 0.0f ? round_clamp(x[e] / step, -32, 31) : 0) + 32;
         // half h = e/128; within it e' : low nibble in ql[64h + e'%64] (nibble e'/64),
         // high two bits in qh[32h + e'%32] (bit pair e'/32)
         const int h = e / 128, r = e % 128;

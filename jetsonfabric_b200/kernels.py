@@ -45,6 +45,10 @@ def _bind():
         "jfb_quantize_q8k": ([_VP, C.c_uint32, C.c_uint32, C.POINTER(Q8K), _VP], Status),
         "jfb_swiglu_quant": ([_VP, _VP, C.c_uint32, C.c_uint32, _VP, C.POINTER(Q8K), _VP], Status),
         "jfb_matmul": ([C.POINTER(Weight), C.POINTER(Q8K), _VP, C.c_uint32, C.c_uint32, _VP, _VP, _VP, _VP], Status),
+        "jfb_matmul_tc_supported": ([C.POINTER(Weight)], C.c_int),
+        "jfb_matmul_tc_workspace_bytes": ([C.c_uint32, C.c_uint32, C.c_uint32], C.c_uint64),
+        "jfb_matmul_tc": ([C.POINTER(Weight), C.POINTER(Q8K), C.c_uint32, C.c_uint32, _VP, _VP, _VP, _VP, C.c_uint64,
+                           _VP, _VP], Status),
         "jfb_rope_kv_append": ([_VP, _VP, _VP, C.c_uint32, _VP, _VP, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32,
                                 _VP, C.c_uint32, _VP, C.c_uint32, _VP], Status),
         "jfb_rope_table_host": ([_VP, C.c_uint32, C.c_uint32, C.c_float], None),
@@ -126,6 +130,18 @@ def matmul(w: DeviceWeight, n: int, out, x_q8: Q8Buffer | None = None, x_f32=Non
            bias=None, residual=None, stream=None):
     check(_bind().jfb_matmul(C.byref(w.desc), None if x_q8 is None else C.byref(x_q8.desc), ptr(x_f32), n,
                              epilogue, ptr(bias), ptr(residual), ptr(out), stream_ptr(stream)))
+
+
+def matmul_tc_workspace_bytes(rows: int, cols: int, n: int) -> int:
+    return int(_bind().jfb_matmul_tc_workspace_bytes(rows, cols, n))
+
+
+def matmul_tc(w: DeviceWeight, n: int, out, x_q8: Q8Buffer, workspace, epilogue=EPILOGUE_STORE, bias=None,
+              residual=None, error_flag=None, stream=None, workspace_bytes=None):
+    """The tcgen05 path (jfb_matmul_tc); `workspace` is a zero-filled uint8 CUDA tensor."""
+    size = workspace.numel() if workspace_bytes is None else workspace_bytes
+    check(_bind().jfb_matmul_tc(C.byref(w.desc), C.byref(x_q8.desc), n, epilogue, ptr(bias), ptr(residual), ptr(out),
+                                ptr(workspace), size, ptr(error_flag), stream_ptr(stream)))
 
 
 def argmax(logits, out):
