@@ -136,10 +136,13 @@ jfb_status jfb_matmul(const jfb_weight * weight, const jfb_q8k * x_q8, const flo
  * x 32 activation rows). A tile shared by several CTAs is finished by the last
  * contributor, which sums the double partials in CTA order.
  *
- * The workspace holds the partials and the per-tile arrival counters. It must
- * be zero-filled before its first use; every successful call leaves it that
- * way, and a call that reports an error through error_flag may not, so clear
- * it again after one. error_flag (may be NULL) receives a nonzero code when a
+ * The workspace holds the partials and the per-tile arrival counters at
+ * offsets that do not depend on the shape, so one workspace (sized for the
+ * largest call) serves calls of any shape on one stream. It must be
+ * zero-filled before its first use; every successful call leaves it that way,
+ * and a call that reports an error through error_flag may not, so clear it
+ * again after one. error_flag (may be NULL; device memory or host memory
+ * mapped into the device address space) receives a nonzero code when a
  * bounded pipeline wait gave up. */
 int jfb_matmul_tc_supported(const jfb_weight * weight);
 uint64_t jfb_matmul_tc_workspace_bytes(uint32_t rows, uint32_t cols, uint32_t n);

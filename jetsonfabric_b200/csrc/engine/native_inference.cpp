@@ -500,6 +500,7 @@ void prefill_batch_device(NativeEngine & engine, std::span<NativeSession * const
 void synchronize(NativeEngine & engine) {
     jfb::engine::cuda_check(cudaStreamSynchronize(BatchAccess::impl_of(engine).model->stream()),
                             "native Qwen2 stage computation failed");
+    BatchAccess::impl_of(engine).stage->check_device_errors();
 }
 
 void * stream(NativeEngine & engine) { return BatchAccess::impl_of(engine).model->stream(); }

@@ -16,9 +16,11 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <iomanip>
 #include <sstream>
+#include <string>
 #include <stdexcept>
 #include <unordered_map>
 
@@ -33,6 +35,13 @@ void jfb_check(const jfb_status & s) {
     if (s.code == JFB_STATUS_INVALID_ARGUMENT) throw std::invalid_argument(s.message);
     throw std::runtime_error(s.message);
 }
+
+namespace {
+
+// Activation rows from which K-quant matmuls run on the tensor cores.
+constexpr std::uint32_t kTensorCoreMinRows = 8;
+
+}  // namespace
 
 namespace {
 
@@ -362,7 +371,26 @@ KvCache::~KvCache() {
 
 // ---- stage forward ----------------------------------------------------------
 
-Qwen2Stage::Qwen2Stage(DeviceModel & model) : m_(model) {}
+Qwen2Stage::Qwen2Stage(DeviceModel & model) : m_(model) {
+    // JFB_MATMUL_PATH selects between the two bit-identical K-quant matmuls:
+    // "auto" (default), "cuda-core" or "tensor-core".
+    if (const char * path = std::getenv("JFB_MATMUL_PATH")) {
+        const std::string v(path);
+        if (v == "cuda-core") matmul_path_ = 1;
+        else if (v == "tensor-core") matmul_path_ = 2;
+        else if (v != "auto" && !v.empty()) throw std::invalid_argument("JFB_MATMUL_PATH must be auto, cuda-core or tensor-core");
+    }
+}
+
+void Qwen2Stage::check_device_errors() {
+    if (tc_error_host_ == nullptr || *tc_error_host_ == 0) return;
+    const int code = *tc_error_host_;
+    *tc_error_host_ = 0;
+    // an aborted launch may leave stream-K arrival counters mid-count
+    if (tc_workspace_ != nullptr) cudaMemset(tc_workspace_, 0, tc_workspace_bytes_);
+    throw std::runtime_error("native Qwen2 tensor-core matmul stalled: pipeline wait " + std::to_string(code) +
+                             " timed out");
+}
 
 Qwen2Stage::~Qwen2Stage() {
     free_scratch();
@@ -372,6 +400,7 @@ Qwen2Stage::~Qwen2Stage() {
         cudaEventDestroy(t.stop);
     }
     for (cudaEvent_t e : event_pool_) cudaEventDestroy(e);
+    if (tc_error_host_ != nullptr) cudaFreeHost(const_cast<int *>(tc_error_host_));
 }
 
 cudaEvent_t Qwen2Stage::take_event() {
@@ -413,7 +442,7 @@ void Qwen2Stage::free_scratch() {
                      static_cast<void *>(gate_), static_cast<void *>(up_), static_cast<void *>(q8_.qs),
                      static_cast<void *>(q8_.d), static_cast<void *>(q8_.bsums), attn_scratch_,
                      static_cast<void *>(logits_), static_cast<void *>(tokens_dev_),
-                     static_cast<void *>(error_flag_), meta_dev_}) {
+                     static_cast<void *>(error_flag_), meta_dev_, tc_workspace_}) {
         if (p != nullptr) cudaFree(p);
     }
     if (meta_host_ != nullptr) cudaFreeHost(meta_host_);
@@ -421,6 +450,8 @@ void Qwen2Stage::free_scratch() {
     q8_ = jfb_q8k{};
     attn_scratch_ = meta_dev_ = meta_host_ = nullptr;
     tokens_dev_ = error_flag_ = nullptr;
+    tc_workspace_ = nullptr;
+    tc_workspace_bytes_ = 0;
     cap_rows_ = cap_seqs_ = cap_keys_ = 0;
     scratch_bytes_ = 0;
 }
@@ -459,6 +490,31 @@ void Qwen2Stage::ensure_scratch(std::uint32_t rows, std::uint32_t seqs, std::uin
     meta_bytes_ = align256(std::uint64_t(3 * R + S) * 4) + std::uint64_t(S) * sizeof(jfb_kv_slot) + 256;
     alloc(&meta_dev_, meta_bytes_);
     cuda_check(cudaMallocHost(&meta_host_, meta_bytes_), "allocate pinned staging");
+    // stream-K workspace of the tensor-core matmul: the largest need of any
+    // weight of this stage at R rows (S rows for the output head)
+    auto tc_need = [](const jfb_weight & w, std::uint32_t n) -> std::uint64_t {
+        return jfb_matmul_tc_supported(&w) ? jfb_matmul_tc_workspace_bytes(w.rows, w.cols, n) : 0;
+    };
+    std::uint64_t tc = 0;
+    for (std::uint32_t li = 0; li < m_.layers(); ++li) {
+        const LayerWeights & lw = m_.layer(li);
+        for (const jfb_weight * x : {&lw.q, &lw.k, &lw.v, &lw.o, &lw.gate, &lw.up, &lw.down}) tc = std::max(tc, tc_need(*x, R));
+    }
+    if (m_.last_stage()) tc = std::max(tc, tc_need(m_.output(), S));
+    if (tc > 0) {
+        alloc(&tc_workspace_, tc);
+        tc_workspace_bytes_ = std::max<std::uint64_t>(tc, 256);
+        cuda_check(cudaMemsetAsync(tc_workspace_, 0, tc_workspace_bytes_, m_.stream()), "clear matmul workspace");
+    }
+    if (tc_error_host_ == nullptr) {
+        int * host = nullptr;
+        cuda_check(cudaHostAlloc(reinterpret_cast<void **>(&host), sizeof(int), cudaHostAllocMapped),
+                   "allocate matmul error word");
+        *host = 0;
+        tc_error_host_ = host;
+        cuda_check(cudaHostGetDevicePointer(reinterpret_cast<void **>(&tc_error_dev_), host, 0),
+                   "map matmul error word");
+    }
     cap_rows_ = R;
     cap_seqs_ = S;
     cap_keys_ = K;
@@ -548,7 +604,16 @@ void Qwen2Stage::forward(std::span<const SequenceRows> seqs, const ForwardIo & i
     };
     auto mm = [&](const jfb_weight & w, const float * xf, std::uint32_t n, std::uint32_t ep, const float * bias,
                   const float * residual, float * out) {
-        timed(0, matmul_bytes(w, n, ep), [&] { jfb_check(jfb_matmul(&w, &q8_, xf, n, ep, bias, residual, out, st)); });
+        const bool tc = matmul_path_ != 1 && tc_workspace_ != nullptr && jfb_matmul_tc_supported(&w) &&
+                        (matmul_path_ == 2 || n >= kTensorCoreMinRows);
+        timed(0, matmul_bytes(w, n, ep), [&] {
+            if (tc) {
+                jfb_check(jfb_matmul_tc(&w, &q8_, n, ep, bias, residual, out, tc_workspace_, tc_workspace_bytes_,
+                                        tc_error_dev_, st));
+            } else {
+                jfb_check(jfb_matmul(&w, &q8_, xf, n, ep, bias, residual, out, st));
+            }
+        });
     };
     double kv_rows = 0.0;  // keys read per layer, summed over rows
     for (const SequenceRows & s : seqs) {
@@ -610,7 +675,10 @@ void Qwen2Stage::forward(std::span<const SequenceRows> seqs, const ForwardIo & i
                        "read logits");
         }
     }
-    if (io.synchronize) cuda_check(cudaStreamSynchronize(st), "native Qwen2 stage computation failed");
+    if (io.synchronize) {
+        cuda_check(cudaStreamSynchronize(st), "native Qwen2 stage computation failed");
+        check_device_errors();
+    }
 }
 
 }  // namespace jfb::engine

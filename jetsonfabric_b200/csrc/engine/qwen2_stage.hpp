@@ -162,6 +162,9 @@ public:
     std::uint64_t scratch_bytes() const { return scratch_bytes_; }
     std::uint64_t kernel_launches() const { return launches_; }
     void set_timing(bool enabled) { timing_ = enabled; }
+    // Throws std::runtime_error when a tensor-core matmul of an earlier
+    // launch gave up on a pipeline wait; call after the stream is synchronised.
+    void check_device_errors();
     // Waits for the timed launches of the last forward and sums them up.
     KernelTiming collect_timing();
 
@@ -185,6 +188,13 @@ private:
     float * logits_ = nullptr;
     std::int32_t * tokens_dev_ = nullptr;
     std::int32_t * error_flag_ = nullptr;
+    // tensor-core matmul: stream-K workspace (zero-filled) and an error word
+    // in host-mapped pinned memory, readable without a copy after a sync
+    void * tc_workspace_ = nullptr;
+    std::uint64_t tc_workspace_bytes_ = 0;
+    volatile int * tc_error_host_ = nullptr;
+    int * tc_error_dev_ = nullptr;
+    int matmul_path_ = 0;  // 0 auto, 1 CUDA cores only, 2 tensor cores wherever supported
     // per-call metadata: seq[R], pos[R], last_row[S], tokens[R], slots[S]
     void * meta_dev_ = nullptr;
     void * meta_host_ = nullptr;

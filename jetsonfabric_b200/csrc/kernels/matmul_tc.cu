@@ -162,7 +162,7 @@ __device__ __noinline__ bool mbar_wait_slow(uint64_t * bar, uint32_t parity, vol
         if ((i & 63u) == 0 && global_ns() - t0 > kWaitNs) break;
     }
     *abort_flag = 1;
-    if (error != nullptr) atomicExch(error, code);
+    if (error != nullptr) *reinterpret_cast<volatile int *>(error) = code;  // device or host-mapped word
     return false;
 }
 
@@ -717,9 +717,12 @@ Plan make_plan(uint32_t rows, uint32_t cols, uint32_t n) {
     return pl;
 }
 
-uint64_t partial_bytes(uint32_t grid) { return uint64_t(2) * grid * kSlotDoubles * sizeof(double); }
+// Workspace: partial slots for the largest grid this device runs (two per
+// SM), then the arrival counters. Both offsets are the same for every shape,
+// so calls of different shapes can share one workspace on a stream.
+uint64_t partial_bytes() { return uint64_t(2) * uint64_t(sm_count()) * kSlotDoubles * sizeof(double); }
 uint64_t workspace_bytes(const Plan & pl) {
-    return partial_bytes(pl.grid) + uint64_t(pl.tiles) * kEpilogueWarps * sizeof(uint32_t);
+    return partial_bytes() + uint64_t(pl.tiles) * kEpilogueWarps * sizeof(uint32_t);
 }
 
 template <uint32_t TYPE>
@@ -799,7 +802,7 @@ extern "C" jfb_status jfb_matmul_tc(const jfb_weight * weight, const jfb_q8k * x
     p.residual = residual;
     p.out = out;
     p.partial = static_cast<double *>(workspace);
-    p.counters = reinterpret_cast<uint32_t *>(static_cast<uint8_t *>(workspace) + partial_bytes(pl.grid));
+    p.counters = reinterpret_cast<uint32_t *>(static_cast<uint8_t *>(workspace) + partial_bytes());
     p.error = error_flag;
     cudaStream_t s = as_stream(stream);
     switch (weight->type) {

@@ -158,11 +158,27 @@ def test_tc_workspace_reuse_leaves_counters_zero(K):
     for _ in range(3):
         again, _, ws = run_tc(K, w, x, workspace=ws)
         assert np.array_equal(bits(again), bits(first))
-    work = 8 * 2 * (cols // 256)  # row tiles x token tiles x blocks
-    grid = min(work, torch.cuda.get_device_properties(0).multi_processor_count)
-    partial_bytes = 2 * grid * 128 * 32 * 8
+    partial_bytes = 2 * torch.cuda.get_device_properties(0).multi_processor_count * 128 * 32 * 8
     counters = ws[partial_bytes:].view(torch.int32)
     assert int(counters.abs().sum().item()) == 0
+
+
+def test_tc_shapes_share_one_workspace(K):
+    """Calls of different grids and tile counts interleaved on one workspace,
+    as a stage runs its weights: each stays bit-exact."""
+    shapes = [(jfm.JF_TENSOR_Q4_K, 1000, 11008, 33), (jfm.JF_TENSOR_Q4_K, 256, 1536, 24),
+              (jfm.JF_TENSOR_Q6_K, 1536, 8960, 24), (jfm.JF_TENSOR_Q2_K, 96, 2048, 5), (jfm.JF_TENSOR_Q6_K, 4000, 1536, 1)]
+    size = max(K.matmul_tc_workspace_bytes(r, c, n) for _, r, c, n in shapes)
+    ws = torch.zeros(size, dtype=torch.uint8, device="cuda")
+    cases = []
+    for i, (t, r, c, n) in enumerate(shapes):
+        raw = random_blocks(t, r, c, 50 + i)
+        x = activations(n, c, 60 + i)
+        cases.append((K.DeviceWeight(t, r, c, raw), x, oracle_matmul(t, raw, r, c, x)))
+    for _ in range(2):
+        for w, x, ref in cases:
+            got, _, ws = run_tc(K, w, x, workspace=ws)
+            assert np.array_equal(bits(got), bits(ref))
 
 
 def test_tc_rejects_bad_arguments(K):
