@@ -258,7 +258,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         achieved = timing["matmul_bytes"] / (timing["matmul_ms"] / 1000.0) / 1e9
         roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                 "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": traffic_from_profiles(),
-                "kernel": "decode matmuls (K-quant x Q8_K dp4a), one decode step",
+                "kernel": "decode matmuls (K-quant x Q8_K on tcgen05 for 8+ rows), one decode step",
                 "launches": timing["matmul_launches"],
                 "bytes_per_launch": timing["matmul_bytes"] / max(1, timing["matmul_launches"]),
                 "ms_per_launch": timing["matmul_ms"] / max(1, timing["matmul_launches"]),

@@ -34,46 +34,63 @@
 // all contributors' partials in CTA order, so the result does not depend on
 // timing and no CTA ever waits for another.
 //
-// Warp roles (13 warps, 416 threads):
+// Warp roles (14 warps, 448 threads):
 //   warps 0-3   epilogue: warp w owns TMEM lanes 32w..32w+31 (weight rows)
 //               and all 32 token columns;
-//   warps 4-11  producers: per stage (half a block, 128 K values) thread
-//               (m, part) writes 64 values of weight row m as f16 products in
-//               the canonical no-swizzle K-major layout (core matrices of
-//               8 rows x 16 bytes; LBO = 128 B between the two K-halves of one
-//               16-wide MMA step, SBO = 2048 B between 8-row groups), and all
-//               producers convert the activation codes (and, once per block,
-//               the mins and partial sums) the same way;
-//   warp 12     TMEM allocation and the single-thread tcgen05.mma issue.
+//   warps 4-11  converters: per stage (half a block, 128 K values) thread
+//               (m, part) turns 64 raw values of weight row m into f16
+//               products and writes them to tensor memory (tcgen05.st): the A
+//               operand lives in TMEM (lane = weight row, each 32-bit column
+//               a pair of consecutive K values), so it never takes shared
+//               memory bandwidth. All converters also turn the activation
+//               codes (and, once per block, the mins and partial sums) into
+//               f16 B tiles in shared memory, in the canonical no-swizzle
+//               K-major layout (core matrices of 8 rows x 16 bytes; LBO = 128 B
+//               between the two K-halves of one 16-wide MMA step, SBO between
+//               8-row groups);
+//   warp 12     TMEM allocation and the single-thread tcgen05.mma issue;
+//   warp 13     one thread issuing the 2D TMA loads (cp.async.bulk.tensor, no
+//               multicast) of the raw weight rows, activation codes and
+//               partial sums into a ring of raw stages, several stages ahead
+//               of the converters, completing on mbarrier transaction counts.
 // Accumulators are double-buffered in TMEM, so the MMAs of block i+1 overlap
-// the epilogue of block i. Every mbarrier wait is bounded by a 2 s
+// the epilogue of block i. The epilogue stages its per-block scales (weight
+// d/dmin of its row, activation d of its lane's token) with cp.async several
+// blocks ahead. Every mbarrier wait is bounded by a 2 s
 // global-timer limit: on expiry the kernel records an error code, every role
-// stops, in-flight MMAs are drained and TMEM is released.
+// stops, in-flight MMAs and TMA loads are drained and TMEM is released.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include <algorithm>
+#include <cstring>
+#include <map>
 #include <mutex>
+#include <tuple>
 
 #include "common.cuh"
 
 namespace jfb {
 namespace {
 
-constexpr int kThreads = 416;
+constexpr int kThreads = 448;
 constexpr int kEpilogueThreads = 128;  // warps 0-3
 constexpr int kEpilogueWarps = 4;
-constexpr int kProducerThreads = 256;  // warps 4-11
+constexpr int kConverterThreads = 256;  // warps 4-11
 constexpr int kMmaWarp = 12;
+constexpr int kTmaWarp = 13;
 constexpr int kRows = 128;             // MMA M: weight rows per tile
 constexpr int kBN = 32;                // MMA N: activation rows per tile
 constexpr int kKStage = 128;           // K values per pipeline stage
 constexpr uint32_t kSbo = 2048;        // 8-row group stride of a 128-wide K tile
 constexpr uint32_t kSbo16 = 256;       // same for the K = 16 mins tiles
-constexpr uint32_t kTileBytes = kRows * kKStage * 2;  // one f16 A plane, 32 KB
 constexpr uint32_t kBBytes = kBN * kKStage * 2;       // 8 KB
 constexpr uint32_t kA2Bytes = kRows * 16 * 2;         // 4 KB
 constexpr uint32_t kB2Bytes = kBN * 16 * 2;           // 1 KB
 constexpr uint32_t kMaxSmem = 232448;                 // sm_100 opt-in limit per block
 constexpr uint32_t kTailBytes = 1024;                 // barriers, TMEM slot, flags, activation scales
-constexpr uint64_t kWaitNs = 2000000000ull;
+constexpr uint64_t kWaitNs = 2000000000ull;            // bound of every pipeline wait
+constexpr uint32_t kSuspendNs = 1000000;               // longest single suspension of a waiting thread
 constexpr uint32_t kSlotDoubles = kRows * kBN;        // one partial tile
 
 enum : int {
@@ -81,43 +98,84 @@ enum : int {
     kErrWaitAccEmpty = 2,
     kErrWaitFull = 3,
     kErrWaitAccFull = 4,
+    kErrWaitRawEmpty = 5,
+    kErrWaitRawFull = 6,
 };
 
+// Raw stage (TMA destination, per half-block): the weight boxes W0 (and W1)
+// of 128 rows, the scale/header box of 128 x 16 bytes, the activation codes
+// (32 x 128 bytes) and, for types with mins, the Q8_K partial sums (32 x 32).
 template <uint32_t TYPE>
 struct TypeTraits;
 template <>
 struct TypeTraits<JF_TENSOR_Q4_K> {
     static constexpr int kPlanes = 1, kAcc = 3;  // D(half 0), D(half 1), mins
     static constexpr bool kMins = true;
+    static constexpr uint32_t kW0 = 64, kW1 = 0;  // bytes per row: codes of the half-block
+    static constexpr uint32_t kBlockBytes = 128;  // plane-0 bytes per block
 };
 template <>
 struct TypeTraits<JF_TENSOR_Q6_K> {
     static constexpr int kPlanes = 2, kAcc = 2;  // D(hi), D(lo)
     static constexpr bool kMins = false;
+    static constexpr uint32_t kW0 = 64, kW1 = 32;  // ql, qh of the half-block
+    static constexpr uint32_t kBlockBytes = 192;
 };
 template <>
 struct TypeTraits<JF_TENSOR_Q2_K> {
     static constexpr int kPlanes = 1, kAcc = 2;  // D, mins
     static constexpr bool kMins = true;
+    static constexpr uint32_t kW0 = 32, kW1 = 0;
+    static constexpr uint32_t kBlockBytes = 64;
 };
 
 template <uint32_t TYPE>
+struct RawLayout {
+    using T = TypeTraits<TYPE>;
+    static constexpr uint32_t kW0Off = 0;
+    static constexpr uint32_t kW1Off = kW0Off + kRows * T::kW0;
+    static constexpr uint32_t kScOff = kW1Off + kRows * T::kW1;
+    static constexpr uint32_t kActOff = kScOff + kRows * 16;
+    static constexpr uint32_t kBsOff = kActOff + kBN * 128;
+    static constexpr uint32_t kBytes = kBsOff + (T::kMins ? kBN * 32 : 0);  // also the TMA transaction size
+};
+
+// Operand stage in shared memory: the f16 B tile (activation codes) and, for
+// types with mins, the K = 16 mins (A2) and partial-sum (B2) tiles. The A
+// operand of a stage lives in TMEM.
+template <uint32_t TYPE>
 __host__ __device__ constexpr uint32_t stage_bytes() {
-    return TypeTraits<TYPE>::kPlanes * kTileBytes + kBBytes + (TypeTraits<TYPE>::kMins ? kA2Bytes + kB2Bytes : 0);
+    return kBBytes + (TypeTraits<TYPE>::kMins ? kA2Bytes + kB2Bytes : 0);
 }
 template <uint32_t TYPE>
+__host__ __device__ constexpr uint32_t acc_columns() {  // both accumulator buffers
+    return 2 * TypeTraits<TYPE>::kAcc * kBN;
+}
+template <uint32_t TYPE>
+__host__ __device__ constexpr uint32_t a_columns() {  // one stage of A: 64 columns per plane
+    return TypeTraits<TYPE>::kPlanes * (kKStage / 2);
+}
+// Operand stages: as many A stages as fit next to the accumulators in the
+// 512 TMEM columns, at most 4.
+template <uint32_t TYPE>
 __host__ __device__ constexpr int stage_count() {
-    return int((kMaxSmem - kTailBytes) / stage_bytes<TYPE>()) < 6 ? int((kMaxSmem - kTailBytes) / stage_bytes<TYPE>()) : 6;
+    return int((512 - acc_columns<TYPE>()) / a_columns<TYPE>()) < 4 ? int((512 - acc_columns<TYPE>()) / a_columns<TYPE>())
+                                                                      : 4;
+}
+constexpr int kScaleRing = 4;  // blocks of epilogue scales staged ahead
+constexpr uint32_t kScaleBytes = kEpilogueWarps * kScaleRing * (32 + 32) * 4;
+template <uint32_t TYPE>
+__host__ __device__ constexpr int raw_count() {
+    return int((kMaxSmem - kTailBytes - kScaleBytes - stage_count<TYPE>() * stage_bytes<TYPE>()) / RawLayout<TYPE>::kBytes) < 10
+               ? int((kMaxSmem - kTailBytes - kScaleBytes - stage_count<TYPE>() * stage_bytes<TYPE>()) / RawLayout<TYPE>::kBytes)
+               : 10;
 }
 template <uint32_t TYPE>
 __host__ __device__ constexpr uint32_t smem_bytes() {
-    return stage_count<TYPE>() * stage_bytes<TYPE>() + kTailBytes;
+    return stage_count<TYPE>() * stage_bytes<TYPE>() + raw_count<TYPE>() * RawLayout<TYPE>::kBytes + kScaleBytes +
+           kTailBytes;
 }
-template <uint32_t TYPE>
-__host__ __device__ constexpr uint32_t tmem_columns() {
-    const uint32_t need = 2 * TypeTraits<TYPE>::kAcc * kBN;
-    return need <= 32 ? 32 : need <= 64 ? 64 : need <= 128 ? 128 : need <= 256 ? 256 : 512;
-}
+constexpr uint32_t kTmemCols = 512;  // one CTA per SM owns all of TMEM
 
 // ---- PTX wrappers -------------------------------------------------------------
 
@@ -151,15 +209,29 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t * bar, uint32_t parity) {
     return ok != 0;
 }
 
+// try_wait that lets the hardware suspend the thread until the phase
+// completes, for at most `hint_ns`, so waiting roles take no issue slots.
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint64_t * bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.b32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+
 // Bounded wait: false (with the abort flag raised and `code` recorded) when
 // the phase has not completed within kWaitNs, or when another role aborted.
 __device__ __noinline__ bool mbar_wait_slow(uint64_t * bar, uint32_t parity, volatile int * abort_flag, int * error,
                                             int code) {
     const uint64_t t0 = global_ns();
-    for (uint32_t i = 1;; ++i) {
-        if (mbar_try_wait(bar, parity)) return true;
+    for (;;) {
+        if (mbar_try_wait_suspend(bar, parity, kSuspendNs)) return true;
         if (*abort_flag) return false;
-        if ((i & 63u) == 0 && global_ns() - t0 > kWaitNs) break;
+        if (global_ns() - t0 > kWaitNs) break;
     }
     *abort_flag = 1;
     if (error != nullptr) *reinterpret_cast<volatile int *>(error) = code;  // device or host-mapped word
@@ -170,6 +242,22 @@ __device__ __forceinline__ bool mbar_wait(uint64_t * bar, uint32_t parity, volat
                                           int code) {
     if (mbar_try_wait(bar, parity)) return true;
     return mbar_wait_slow(bar, parity, abort_flag, error, code);
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t * bar, uint32_t bytes) {
+    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+// 2D tiled TMA load of one box into this CTA's shared memory (no multicast).
+// x is the byte offset along the row: always a multiple of 16 here.
+__device__ __forceinline__ void tma_load_2d(void * dst, const CUtensorMap * map, int32_t x, int32_t y, uint64_t * bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
 }
 
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
@@ -198,6 +286,38 @@ __device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64
         "setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
         "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
+}
+
+// The same with the A operand read from TMEM (K-major: lane = row, each
+// 32-bit column a pair of consecutive K values).
+__device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                           uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate));
+}
+
+// 16 consecutive 32-bit columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t * v) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+        "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// 4-byte asynchronous global -> shared copy (completes at cp_async_wait).
+__device__ __forceinline__ void cp_async4(void * dst, const void * src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
 __device__ __forceinline__ void mma_commit(uint64_t * bar) {
@@ -233,6 +353,13 @@ __device__ __forceinline__ uint2 scaled4(uint32_t w, __half2 scale, __half2 nbia
 
 __device__ __forceinline__ __half2 h2_int(int v) { return __half2half2(__int2half_rn(v)); }
 
+// f16 pair (V, V) of an exactly representable integer constant.
+template <int V>
+__device__ __forceinline__ __half2 h2_int_const() {
+    constexpr float f = float(V);
+    return __float2half2_rn(f);
+}
+
 __device__ __forceinline__ uint32_t byte_at(const uint4 & v, int i) {
     const uint32_t w = i < 4 ? v.x : i < 8 ? v.y : i < 12 ? v.z : v.w;
     return (w >> (8 * (i & 3))) & 0xffu;
@@ -249,6 +376,12 @@ __device__ __forceinline__ void q4k_scale_min_hdr(const uint4 & hdr, int j, int 
         m = (s(j + 4) >> 4) | ((s(j) >> 6) << 4);
     }
 }
+
+// Tensor maps of one launch: weight boxes W0/W1 and the scale box (128 rows
+// each), the activation codes (32 x 128 bytes) and partial sums (32 x 32).
+struct TcMaps {
+    CUtensorMap w0, w1, sc, act, bsums;
+};
 
 struct TcParams {
     jfb_weight w;
@@ -277,93 +410,151 @@ __device__ __forceinline__ uint32_t cta_of(uint64_t unit, uint64_t work, uint64_
     return uint32_t(((unit + 1) * g - 1) / work);
 }
 
-// Weight half-block `h`, values [64*part, 64*part + 64), of block `block` for
-// tile row m, as f16 products in the A plane(s).
-template <uint32_t TYPE>
-__device__ __forceinline__ void produce_a(const jfb_weight & w, uint64_t block, int h, int part, uint8_t * a_tile,
-                                          int m) {
-    const uint8_t * p0 = static_cast<const uint8_t *>(w.plane[0]);
-    const uint8_t * p1 = static_cast<const uint8_t *>(w.plane[1]);
-    uint8_t * row_base = a_tile + (m >> 3) * kSbo + (m & 7) * 16;
+// f16 pair (v, v) of a small integer v with v + BIAS in [0, 1024), without a
+// conversion instruction: 0x6400 | u is the f16 number 1024 + u, and
+// subtracting 1024 + BIAS is exact.
+template <int BIAS>
+__device__ __forceinline__ __half2 small_h2(int v) {
+    const uint32_t u = uint32_t(v + BIAS) | 0x6400u;
+    return __hsub2(bits_h2(u * 0x00010001u), h2_int_const<1024 + BIAS>());
+}
+
+// Converts values [64*PART, 64*PART + 64) of raw half-block H of tile row m
+// (raw stage `r`) into f16 products and stores them into this thread's TMEM
+// lane of the stage's A operand (`a_col`: address of plane 0, column 0; plane
+// 1 follows 64 columns later). Value k of the half goes to column k / 2, two
+// values per 32-bit column. H and PART are compile-time so every byte, nibble
+// and register index below is a constant. Warp-collective (tcgen05.st).
+template <uint32_t TYPE, int H, int PART>
+__device__ __forceinline__ void convert_a(const uint8_t * r, uint32_t a_col, int m) {
+    using RL = RawLayout<TYPE>;
+    const uint4 scv = *reinterpret_cast<const uint4 *>(r + RL::kScOff + m * 16);
+    const uint32_t col = a_col + 32 * PART;
     if constexpr (TYPE == JF_TENSOR_Q4_K) {
-        // codes: byte 32c + l holds element 64c + l (low nibble) and 64c + 32 + l
-        // (high nibble); this thread covers c = 2h + part.
-        const int c = 2 * h + part;
-        const uint4 hdr = __ldg(reinterpret_cast<const uint4 *>(p1 + block * 16));
-        const uint4 * codes = reinterpret_cast<const uint4 *>(p0 + block * 128 + 32 * c);
-        const uint4 v0 = __ldg(codes), v1 = __ldg(codes + 1);
+        // raw row: code bytes [64H, 64H + 64) of the block; byte 32c' + l holds
+        // element 64c' + l (low nibble) and 64c' + 32 + l (high nibble) of the
+        // half; this thread covers c' = PART, i.e. sub-blocks 2c and 2c + 1
+        // of the block with c = 2H + PART.
+        constexpr int c = 2 * H + PART;
+        const uint4 * codes = reinterpret_cast<const uint4 *>(r + RL::kW0Off + m * 64 + 32 * PART);
+        const uint4 v0 = codes[0], v1 = codes[1];
         const uint32_t wv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
 #pragma unroll
         for (int nib = 0; nib < 2; ++nib) {
             int sc, mn;
-            q4k_scale_min_hdr(hdr, 2 * c + nib, sc, mn);
-            const __half2 scale = h2_int(sc), nbias = h2_int(-1024 * sc);
+            q4k_scale_min_hdr(scv, 2 * c + nib, sc, mn);
+            const __half2 scale = small_h2<0>(sc);
+            const __half2 nbias = __hmul2(scale, h2_int_const<-1024>());
+            uint32_t w[16];
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
                 const uint2 a = scaled4((wv[2 * q] >> (4 * nib)) & 0x0f0f0f0fu, scale, nbias);
                 const uint2 b = scaled4((wv[2 * q + 1] >> (4 * nib)) & 0x0f0f0f0fu, scale, nbias);
-                const int chunk = 8 * part + 4 * nib + q;
-                *reinterpret_cast<uint4 *>(row_base + chunk * 128) = make_uint4(a.x, a.y, b.x, b.y);
+                w[4 * q + 0] = a.x;
+                w[4 * q + 1] = a.y;
+                w[4 * q + 2] = b.x;
+                w[4 * q + 3] = b.y;
             }
+            tmem_st16(col + 16 * nib, w);  // values [32*nib, 32*nib + 32) of this thread
         }
     } else if constexpr (TYPE == JF_TENSOR_Q6_K) {
-        // element r (0..127) of half h: nibble r / 64 of ql[64h + r % 64] and
-        // bits 2*(r / 32) of qh[32h + r % 32]; this thread covers
-        // r in [64*part, 64*part + 64).
-        const uint8_t * blk = p0 + block * 192;
-        const uint4 * ql = reinterpret_cast<const uint4 *>(blk + 64 * h);
-        const uint4 * qh = reinterpret_cast<const uint4 *>(blk + 128 + 32 * h);
-        const uint4 scv = __ldg(reinterpret_cast<const uint4 *>(p1 + block * 16));
-        const uint4 l0 = __ldg(ql), l1 = __ldg(ql + 1), l2 = __ldg(ql + 2), l3 = __ldg(ql + 3);
-        const uint4 q0 = __ldg(qh), q1 = __ldg(qh + 1);
+        // raw rows: ql bytes [64H, 64H + 64) and qh bytes [32H, 32H + 32) of
+        // the block. Element r' (0..127) of the half is nibble r' / 64 of
+        // ql[r' % 64] with bits 2*(r' / 32) of qh[r' % 32]; this thread covers
+        // r' in [64*PART, 64*PART + 64): nibble PART of every ql byte.
+        const uint4 * ql = reinterpret_cast<const uint4 *>(r + RL::kW0Off + m * 64);
+        const uint4 * qh = reinterpret_cast<const uint4 *>(r + RL::kW1Off + m * 32);
+        const uint4 l0 = ql[0], l1 = ql[1], l2 = ql[2], l3 = ql[3];
+        const uint4 q0 = qh[0], q1 = qh[1];
         const uint32_t L[16] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w,
                                 l2.x, l2.y, l2.z, l2.w, l3.x, l3.y, l3.z, l3.w};
-        const uint32_t H[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-        uint8_t * row_lo = row_base + kTileBytes;
+        const uint32_t Hq[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+        const __half2 k1056 = h2_int_const<-1056>();  // 1056 = 1024 + 32
 #pragma unroll
-        for (int ch = 0; ch < 8; ++ch) {
-            const int r0 = 64 * part + 8 * ch;
-            const int s = int(int8_t(byte_at(scv, (128 * h + r0) / 16)));
-            const int s_lo = s & 15, s_hi = (s - s_lo) / 16;
-            const __half2 shi = h2_int(s_hi), nhi = h2_int(-1056 * s_hi);  // 1056 = 1024 + 32
-            const __half2 slo = h2_int(s_lo), nlo = h2_int(-1056 * s_lo);
-            uint32_t q[2];
+        for (int gp = 0; gp < 2; ++gp) {  // 32 values (two scale groups) per pass
+            uint32_t whi[16], wlo[16];
 #pragma unroll
-            for (int k = 0; k < 2; ++k) {
-                const int r = r0 + 4 * k;
-                q[k] = ((L[(r % 64) / 4] >> (4 * (r / 64))) & 0x0f0f0f0fu) |
-                       (((H[(r % 32) / 4] >> (2 * (r / 32))) & 0x03030303u) << 4);
+            for (int g2 = 0; g2 < 2; ++g2) {
+                const int grp = 2 * gp + g2;
+                const int s = int(int8_t(byte_at(scv, 8 * H + 4 * PART + grp)));
+                const int s_lo = s & 15, s_hi = (s - s_lo) / 16;
+                const __half2 shi = small_h2<8>(s_hi), nhi = __hmul2(shi, k1056);
+                const __half2 slo = small_h2<0>(s_lo), nlo = __hmul2(slo, k1056);
+#pragma unroll
+                for (int half_grp = 0; half_grp < 2; ++half_grp) {
+                    const int ch = 2 * grp + half_grp;  // 8-value chunk of this thread
+                    uint32_t q[2];
+#pragma unroll
+                    for (int k = 0; k < 2; ++k) {
+                        const int rr = 64 * PART + 8 * ch + 4 * k;
+                        q[k] = ((L[(rr % 64) / 4] >> (4 * (rr / 64))) & 0x0f0f0f0fu) |
+                               (((Hq[(rr % 32) / 4] >> (2 * (rr / 32))) & 0x03030303u) << 4);
+                    }
+                    const __half2 x0 = magic_pair(q[0], 0x4140u), x1 = magic_pair(q[0], 0x4342u);
+                    const __half2 x2 = magic_pair(q[1], 0x4140u), x3 = magic_pair(q[1], 0x4342u);
+                    const int o = 4 * (2 * g2 + half_grp);
+                    whi[o + 0] = h2_bits(__hfma2(x0, shi, nhi));
+                    whi[o + 1] = h2_bits(__hfma2(x1, shi, nhi));
+                    whi[o + 2] = h2_bits(__hfma2(x2, shi, nhi));
+                    whi[o + 3] = h2_bits(__hfma2(x3, shi, nhi));
+                    wlo[o + 0] = h2_bits(__hfma2(x0, slo, nlo));
+                    wlo[o + 1] = h2_bits(__hfma2(x1, slo, nlo));
+                    wlo[o + 2] = h2_bits(__hfma2(x2, slo, nlo));
+                    wlo[o + 3] = h2_bits(__hfma2(x3, slo, nlo));
+                }
             }
-            const int chunk = 8 * part + ch;
-            const uint2 a0 = scaled4(q[0], shi, nhi), a1 = scaled4(q[1], shi, nhi);
-            *reinterpret_cast<uint4 *>(row_base + chunk * 128) = make_uint4(a0.x, a0.y, a1.x, a1.y);
-            const uint2 b0 = scaled4(q[0], slo, nlo), b1 = scaled4(q[1], slo, nlo);
-            *reinterpret_cast<uint4 *>(row_lo + chunk * 128) = make_uint4(b0.x, b0.y, b1.x, b1.y);
+            tmem_st16(col + 16 * gp, whi);
+            tmem_st16(col + 64 + 16 * gp, wlo);
         }
-    } else {  // Q2_K: element 128h + 32s + l lives in bits 2s of qs[32h + l]
-        const uint4 * qs = reinterpret_cast<const uint4 *>(p0 + block * 64 + 32 * h);
-        const uint4 a0 = __ldg(qs), a1 = __ldg(qs + 1);
+    } else {
+        // raw row: qs bytes [32H, 32H + 32); element 32s + l of the half lives
+        // in bits 2s of byte l
+        const uint4 * qs = reinterpret_cast<const uint4 *>(r + RL::kW0Off + m * 32);
+        const uint4 a0 = qs[0], a1 = qs[1];
         const uint32_t Q[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-        const uint4 scv = __ldg(reinterpret_cast<const uint4 *>(p1 + block * 16));
 #pragma unroll
-        for (int ch = 0; ch < 8; ++ch) {
-            const int r0 = 64 * part + 8 * ch;
-            const int s = r0 / 32, l0 = r0 % 32;
-            const int sc = int(byte_at(scv, (128 * h + r0) / 16) & 15);
-            const __half2 scale = h2_int(sc), nbias = h2_int(-1024 * sc);
-            const uint2 x = scaled4((Q[l0 / 4] >> (2 * s)) & 0x03030303u, scale, nbias);
-            const uint2 y = scaled4((Q[l0 / 4 + 1] >> (2 * s)) & 0x03030303u, scale, nbias);
-            *reinterpret_cast<uint4 *>(row_base + (8 * part + ch) * 128) = make_uint4(x.x, x.y, y.x, y.y);
+        for (int gp = 0; gp < 2; ++gp) {
+            uint32_t w[16];
+#pragma unroll
+            for (int g2 = 0; g2 < 2; ++g2) {
+                const int grp = 2 * gp + g2;
+                const __half2 scale = small_h2<0>(int(byte_at(scv, 8 * H + 4 * PART + grp) & 15));
+                const __half2 nbias = __hmul2(scale, h2_int_const<-1024>());
+#pragma unroll
+                for (int half_grp = 0; half_grp < 2; ++half_grp) {
+                    const int r0 = 64 * PART + 16 * grp + 8 * half_grp;
+                    const int sh = r0 / 32, l0 = r0 % 32;
+                    const uint2 x = scaled4((Q[l0 / 4] >> (2 * sh)) & 0x03030303u, scale, nbias);
+                    const uint2 y = scaled4((Q[l0 / 4 + 1] >> (2 * sh)) & 0x03030303u, scale, nbias);
+                    const int o = 4 * (2 * g2 + half_grp);
+                    w[o + 0] = x.x;
+                    w[o + 1] = x.y;
+                    w[o + 2] = y.x;
+                    w[o + 3] = y.y;
+                }
+            }
+            tmem_st16(col + 16 * gp, w);
         }
+    }
+}
+
+template <uint32_t TYPE>
+__device__ __forceinline__ void convert_a_dispatch(const uint8_t * r, int h, int part, uint32_t a_col, int m) {
+    if (h == 0) {
+        if (part == 0) convert_a<TYPE, 0, 0>(r, a_col, m);
+        else convert_a<TYPE, 0, 1>(r, a_col, m);
+    } else {
+        if (part == 0) convert_a<TYPE, 1, 0>(r, a_col, m);
+        else convert_a<TYPE, 1, 1>(r, a_col, m);
     }
 }
 
 // The 16 per-16-value mins of one block as a K = 16 f16 operand row (Q4_K:
 // the 6-bit min of each 32-value sub-block, twice; Q2_K: the high nibble of
-// each scale byte).
+// each scale byte), from the raw scale row of tile row m.
 template <uint32_t TYPE>
-__device__ __forceinline__ void produce_mins(const jfb_weight & w, uint64_t block, uint8_t * tile, int m) {
-    const uint4 meta = __ldg(reinterpret_cast<const uint4 *>(static_cast<const uint8_t *>(w.plane[1]) + block * 16));
+__device__ __forceinline__ void convert_mins(const uint8_t * r, uint8_t * tile, int m) {
+    const uint4 meta = *reinterpret_cast<const uint4 *>(r + RawLayout<TYPE>::kScOff + m * 16);
     uint32_t h2[8];
 #pragma unroll
     for (int g = 0; g < 16; g += 2) {
@@ -376,7 +567,8 @@ __device__ __forceinline__ void produce_mins(const jfb_weight & w, uint64_t bloc
             m0 = int(byte_at(meta, g) >> 4);
             m1 = int(byte_at(meta, g + 1) >> 4);
         }
-        h2[g / 2] = h2_bits(__halves2half2(__int2half_rn(m0), __int2half_rn(m1)));
+        const uint32_t u = (uint32_t(m0) | 0x6400u) | ((uint32_t(m1) | 0x6400u) << 16);  // mins < 64
+        h2[g / 2] = h2_bits(__hsub2(bits_h2(u), h2_int_const<1024>()));
     }
     uint8_t * base = tile + (m >> 3) * kSbo16 + (m & 7) * 16;
     *reinterpret_cast<uint4 *>(base) = make_uint4(h2[0], h2[1], h2[2], h2[3]);
@@ -384,25 +576,31 @@ __device__ __forceinline__ void produce_mins(const jfb_weight & w, uint64_t bloc
 }
 
 template <uint32_t TYPE>
-__global__ void __launch_bounds__(kThreads, 1) mmq_tc_kernel(TcParams p) {
+__global__ void __launch_bounds__(kThreads, 1) mmq_tc_kernel(const __grid_constant__ TcMaps maps, TcParams p) {
     using T = TypeTraits<TYPE>;
+    using RL = RawLayout<TYPE>;
     constexpr int NS = stage_count<TYPE>();
+    constexpr int NR = raw_count<TYPE>();
     constexpr uint32_t kStage = stage_bytes<TYPE>();
-    constexpr uint32_t kBOff = T::kPlanes * kTileBytes;
+    constexpr uint32_t kBOff = 0;
     constexpr uint32_t kA2Off = kBOff + kBBytes;
     constexpr uint32_t kB2Off = kA2Off + kA2Bytes;
-    constexpr uint32_t kTmemCols = tmem_columns<TYPE>();
+    constexpr uint32_t kAccCols = acc_columns<TYPE>();
+    constexpr uint32_t kACols = a_columns<TYPE>();
 
     extern __shared__ __align__(1024) uint8_t smem[];
-    uint8_t * tail = smem + NS * kStage;
+    uint8_t * raw = smem + NS * kStage;                    // [NR][RL::kBytes]
+    uint8_t * scales = raw + NR * RL::kBytes;              // epilogue scale rings
+    uint8_t * tail = scales + kScaleBytes;
     uint64_t * full = reinterpret_cast<uint64_t *>(tail);  // [NS]
     uint64_t * empty = full + NS;                          // [NS]
-    uint64_t * acc_full = empty + NS;                      // [2]
+    uint64_t * raw_full = empty + NS;                      // [NR]
+    uint64_t * raw_empty = raw_full + NR;                  // [NR]
+    uint64_t * acc_full = raw_empty + NR;                  // [2]
     uint64_t * acc_empty = acc_full + 2;                   // [2]
     uint64_t * drain = acc_empty + 2;                      // [1]
     uint32_t * tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
     volatile int * abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
-    float * da_rows = reinterpret_cast<float *>(tail + 512);  // [kEpilogueWarps][kBN]
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint64_t g = gridDim.x;
@@ -412,8 +610,12 @@ __global__ void __launch_bounds__(kThreads, 1) mmq_tc_kernel(TcParams p) {
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < NS; ++s) {
-            mbar_init(&full[s], kProducerThreads);
+            mbar_init(&full[s], kConverterThreads);
             mbar_init(&empty[s], 1);
+        }
+        for (int s = 0; s < NR; ++s) {
+            mbar_init(&raw_full[s], 1);
+            mbar_init(&raw_empty[s], kConverterThreads);
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(&acc_full[a], 1);
@@ -433,78 +635,108 @@ __global__ void __launch_bounds__(kThreads, 1) mmq_tc_kernel(TcParams p) {
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp >= kEpilogueWarps && warp < kMmaWarp) {
-        // ---------------- producers ----------------
+    if (warp == kTmaWarp) {
+        // ---------------- TMA loads of the raw stages (one thread) ----------------
+        if (lane == 0) {
+            uint32_t rs = 0, rph = 0;
+            uint64_t issued = 0;
+            bool ok = true;
+            for (uint64_t w = w_begin; w < w_end && ok && !*abort_flag; ++w) {
+                const uint32_t tile = uint32_t(w / nb), b = uint32_t(w % nb);
+                const int32_t y_w = int32_t((tile % p.tiles_m) * kRows), y_a = int32_t((tile / p.tiles_m) * kBN);
+                for (int h = 0; h < 2; ++h) {
+                    if (!mbar_wait(&raw_empty[rs], rph ^ 1u, abort_flag, p.error, kErrWaitRawEmpty)) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t * r = raw + rs * RL::kBytes;
+                    mbar_arrive_expect_tx(&raw_full[rs], RL::kBytes);
+                    const int32_t x_blk = int32_t(b * T::kBlockBytes);
+                    tma_load_2d(r + RL::kW0Off, &maps.w0, x_blk + int32_t(T::kW0 * h), y_w, &raw_full[rs]);
+                    if constexpr (T::kW1 > 0) {
+                        tma_load_2d(r + RL::kW1Off, &maps.w1, x_blk + 128 + int32_t(T::kW1 * h), y_w, &raw_full[rs]);
+                    }
+                    tma_load_2d(r + RL::kScOff, &maps.sc, int32_t(b * 16), y_w, &raw_full[rs]);
+                    tma_load_2d(r + RL::kActOff, &maps.act, int32_t(b * kQK + 128 * h), y_a, &raw_full[rs]);
+                    if constexpr (T::kMins) tma_load_2d(r + RL::kBsOff, &maps.bsums, int32_t(b * 32), y_a, &raw_full[rs]);
+                    ++issued;
+                    if (++rs == NR) {
+                        rs = 0;
+                        rph ^= 1u;
+                    }
+                }
+            }
+            // a stopped kernel must not exit with loads still landing in its
+            // shared memory: wait (bounded) for the last issue of every stage
+            if (*abort_flag) {
+                volatile int no_abort = 0;
+                for (uint64_t j = issued > uint64_t(NR) ? issued - NR : 0; j < issued; ++j) {
+                    (void) mbar_wait(&raw_full[j % NR], uint32_t((j / NR) & 1u), &no_abort, nullptr, 0);
+                }
+            }
+        }
+        __syncwarp();
+    } else if (warp >= kEpilogueWarps && warp < kMmaWarp) {
+        // ---------------- converters ----------------
         const int pt = threadIdx.x - kEpilogueThreads;
-        const int m = pt & (kRows - 1), part = pt >> 7;
+        const int m = pt & (kRows - 1), part = pt >> 7;  // part is uniform per warp
+        const uint32_t lane_base = uint32_t((warp & 3) * 32) << 16;  // this warp's TMEM lane quarter
         const __half2 act_nbias = h2_int(-1152);  // codes arrive as q + 128 after the sign flip
         const __half2 one = h2_int(1);
-        uint32_t stage = 0, phase = 0;
-        bool ok = true;
-        for (uint64_t w = w_begin; w < w_end && ok && !*abort_flag; ++w) {
-            const uint32_t tile = uint32_t(w / nb), b = uint32_t(w % nb);
-            const uint32_t tm = tile % p.tiles_m, tn = tile / p.tiles_m;
-            const uint32_t row = tm * kRows + uint32_t(m), tok0 = tn * kBN;
-            const uint64_t block = uint64_t(row) * nb + b;
+        uint32_t stage = 0, phase = 0, rs = 0, rph = 0;
+        for (uint64_t w = w_begin; w < w_end; ++w) {
+            if (__any_sync(0xffffffffu, *abort_flag != 0)) break;
+            bool ok = true;
             for (int h = 0; h < 2; ++h) {
-                if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.error, kErrWaitEmpty)) {
+                // the whole warp proceeds or stops together (TMEM stores are warp-collective)
+                const bool ready = mbar_wait(&raw_full[rs], rph, abort_flag, p.error, kErrWaitRawFull) &&
+                                   mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.error, kErrWaitEmpty);
+                if (!__all_sync(0xffffffffu, ready)) {
                     ok = false;
                     break;
                 }
+                tc_fence_after();
+                const uint8_t * r = raw + rs * RL::kBytes;
                 uint8_t * st = smem + stage * kStage;
-                if (row < p.w.rows) {
-                    produce_a<TYPE>(p.w, block, h, part, st, m);
-                    if (T::kMins && h == 0 && part == 0) produce_mins<TYPE>(p.w, block, st + kA2Off, m);
-                } else {
-#pragma unroll
-                    for (int pl = 0; pl < T::kPlanes; ++pl) {
-                        uint8_t * base = st + pl * kTileBytes + (m >> 3) * kSbo + (m & 7) * 16;
-                        for (int c = 8 * part; c < 8 * part + 8; ++c) {
-                            *reinterpret_cast<uint4 *>(base + c * 128) = make_uint4(0, 0, 0, 0);
-                        }
-                    }
-                    if (T::kMins && h == 0 && part == 0) {
-                        uint8_t * base = st + kA2Off + (m >> 3) * kSbo16 + (m & 7) * 16;
-                        *reinterpret_cast<uint4 *>(base) = make_uint4(0, 0, 0, 0);
-                        *reinterpret_cast<uint4 *>(base + 128) = make_uint4(0, 0, 0, 0);
-                    }
-                }
+                convert_a_dispatch<TYPE>(r, h, part, tmem + lane_base + kAccCols + stage * kACols, m);
+                if (T::kMins && h == 0 && part == 0) convert_mins<TYPE>(r, st + kA2Off, m);
                 // activation codes: kBN rows x 16 chunks of 8
-                for (int idx = pt; idx < kBN * 16; idx += kProducerThreads) {
+                for (int idx = pt; idx < kBN * 16; idx += kConverterThreads) {
                     const int t = idx >> 4, c = idx & 15;
-                    uint4 v = make_uint4(0, 0, 0, 0);
-                    if (tok0 + t < p.n) {
-                        const uint2 raw = __ldg(reinterpret_cast<const uint2 *>(
-                            p.qs + uint64_t(tok0 + t) * (uint64_t(nb) * kQK) + uint64_t(b) * kQK + 128 * h + 8 * c));
-                        const uint2 x = scaled4(raw.x ^ 0x80808080u, one, act_nbias);
-                        const uint2 y = scaled4(raw.y ^ 0x80808080u, one, act_nbias);
-                        v = make_uint4(x.x, x.y, y.x, y.y);
-                    }
-                    *reinterpret_cast<uint4 *>(st + kBOff + (t >> 3) * kSbo + c * 128 + (t & 7) * 16) = v;
+                    const uint2 v = *reinterpret_cast<const uint2 *>(r + RL::kActOff + t * 128 + 8 * c);
+                    const uint2 x = scaled4(v.x ^ 0x80808080u, one, act_nbias);
+                    const uint2 y = scaled4(v.y ^ 0x80808080u, one, act_nbias);
+                    *reinterpret_cast<uint4 *>(st + kBOff + (t >> 3) * kSbo + c * 128 + (t & 7) * 16) =
+                        make_uint4(x.x, x.y, y.x, y.y);
                 }
                 if (T::kMins && h == 0 && pt < kBN * 2) {
                     const int t = pt >> 1, c = pt & 1;
-                    uint32_t hv[4] = {0, 0, 0, 0};
-                    if (tok0 + t < p.n) {
-                        const uint4 raw = __ldg(reinterpret_cast<const uint4 *>(
-                            p.bsums + uint64_t(tok0 + t) * (uint64_t(nb) * 16) + uint64_t(b) * 16 + 8 * c));
-                        const uint32_t rw[4] = {raw.x, raw.y, raw.z, raw.w};
+                    const uint4 v = *reinterpret_cast<const uint4 *>(r + RL::kBsOff + t * 32 + 16 * c);
+                    const uint32_t rw[4] = {v.x, v.y, v.z, v.w};
+                    uint32_t hv[4];
 #pragma unroll
-                        for (int k = 0; k < 4; ++k) {
-                            hv[k] = h2_bits(__halves2half2(__int2half_rn(int(int16_t(rw[k] & 0xffffu))),
-                                                           __int2half_rn(int(int16_t(rw[k] >> 16)))));
-                        }
+                    for (int k = 0; k < 4; ++k) {
+                        hv[k] = h2_bits(__halves2half2(__int2half_rn(int(int16_t(rw[k] & 0xffffu))),
+                                                       __int2half_rn(int(int16_t(rw[k] >> 16)))));
                     }
                     *reinterpret_cast<uint4 *>(st + kB2Off + (t >> 3) * kSbo16 + c * 128 + (t & 7) * 16) =
                         make_uint4(hv[0], hv[1], hv[2], hv[3]);
                 }
+                tmem_wait_st();
+                tc_fence_before();
                 fence_proxy_async();
                 mbar_arrive(&full[stage]);
+                mbar_arrive(&raw_empty[rs]);
                 if (++stage == NS) {
                     stage = 0;
                     phase ^= 1u;
                 }
+                if (++rs == NR) {
+                    rs = 0;
+                    rph ^= 1u;
+                }
             }
+            if (!ok) break;
         }
     } else if (warp == kMmaWarp) {
         // ---------------- MMA issue (one thread) ----------------
@@ -524,17 +756,18 @@ __global__ void __launch_bounds__(kThreads, 1) mmq_tc_kernel(TcParams p) {
                     }
                     tc_fence_after();
                     const uint32_t st = smem_u32(smem + stage * kStage);
+                    const uint32_t a = tmem + kAccCols + stage * kACols;
 #pragma unroll
                     for (int ks = 0; ks < kKStage / 16; ++ks) {
                         const uint64_t bdesc = smem_desc(st + kBOff + ks * 256, 128, kSbo);
                         if constexpr (TYPE == JF_TENSOR_Q4_K) {
-                            mma_f16(d + h * kBN, smem_desc(st + ks * 256, 128, kSbo), bdesc, idesc, ks > 0 ? 1u : 0u);
+                            mma_f16_ts(d + h * kBN, a + ks * 8, bdesc, idesc, ks > 0 ? 1u : 0u);
                         } else if constexpr (TYPE == JF_TENSOR_Q6_K) {
                             const uint32_t accum = (h > 0 || ks > 0) ? 1u : 0u;
-                            mma_f16(d, smem_desc(st + ks * 256, 128, kSbo), bdesc, idesc, accum);
-                            mma_f16(d + kBN, smem_desc(st + kTileBytes + ks * 256, 128, kSbo), bdesc, idesc, accum);
+                            mma_f16_ts(d, a + ks * 8, bdesc, idesc, accum);
+                            mma_f16_ts(d + kBN, a + 64 + ks * 8, bdesc, idesc, accum);
                         } else {
-                            mma_f16(d, smem_desc(st + ks * 256, 128, kSbo), bdesc, idesc, (h > 0 || ks > 0) ? 1u : 0u);
+                            mma_f16_ts(d, a + ks * 8, bdesc, idesc, (h > 0 || ks > 0) ? 1u : 0u);
                         }
                     }
                     if (T::kMins && h == 0) {
@@ -559,42 +792,61 @@ __global__ void __launch_bounds__(kThreads, 1) mmq_tc_kernel(TcParams p) {
         // ---------------- epilogue (warps 0-3) ----------------
         const int m = warp * 32 + lane;
         const uint32_t lane_base = uint32_t(warp * 32) << 16;
-        float * da_s = da_rows + warp * kBN;
+        // scale rings of this warp: [kScaleRing][32] weight scale words (own row), [kScaleRing][32] activation d
+        uint32_t * dring = reinterpret_cast<uint32_t *>(scales) + warp * kScaleRing * 64;
+        float * aring = reinterpret_cast<float *>(dring + kScaleRing * 32);
         const uint8_t * p1 = static_cast<const uint8_t *>(p.w.plane[1]);
         const uint8_t * p2 = static_cast<const uint8_t *>(p.w.plane[2]);
         const uint32_t first_tile = uint32_t(w_begin / nb);
+        // stage unit w's scales into ring slot `slot` (one commit group per unit, possibly empty)
+        auto stage_scales = [&](uint64_t w, int slot) {
+            if (w < w_end) {
+                const uint32_t tile = uint32_t(w / nb), b = uint32_t(w % nb);
+                const uint32_t row = (tile % p.tiles_m) * kRows + uint32_t(m), tok = (tile / p.tiles_m) * kBN + lane;
+                if (row < p.w.rows) {
+                    const uint64_t block = uint64_t(row) * nb + b;
+                    const uint8_t * src = TYPE == JF_TENSOR_Q4_K ? p1 + block * 16        // d | dmin << 16
+                                          : TYPE == JF_TENSOR_Q6_K ? p2 + ((block * 2) & ~uint64_t(3))  // word holding d
+                                                                   : p2 + block * 4;      // d | dmin << 16
+                    cp_async4(&dring[slot * 32 + lane], src);
+                } else {
+                    dring[slot * 32 + lane] = 0;
+                }
+                if (tok < p.n) cp_async4(&aring[slot * 32 + lane], p.da + uint64_t(tok) * nb + b);
+                else aring[slot * 32 + lane] = 0.0f;
+            }
+            cp_async_commit();
+        };
+#pragma unroll
+        for (int k = 0; k < kScaleRing; ++k) stage_scales(w_begin + k, k);
         double sum[kBN];
         uint64_t seg_begin = w_begin;
         uint32_t i = 0;
         for (uint64_t w = w_begin; w < w_end; ++w, ++i) {
             // warp-uniform stop: the warp collectives below need every lane
             if (__any_sync(0xffffffffu, *abort_flag != 0)) break;
-            const uint32_t tile = uint32_t(w / nb), b = uint32_t(w % nb);
+            const uint32_t tile = uint32_t(w / nb);
             const uint32_t tm = tile % p.tiles_m, tn = tile / p.tiles_m;
             const uint32_t row = tm * kRows + uint32_t(m), tok0 = tn * kBN;
             if (w == seg_begin) {
 #pragma unroll
                 for (int t = 0; t < kBN; ++t) sum[t] = 0.0;
             }
-            // per-block scales: this row's d (and dmin), the tile's activation d
-            float dw = 0.0f, dmin = 0.0f;
-            if (row < p.w.rows) {
-                const uint64_t block = uint64_t(row) * nb + b;
-                if constexpr (TYPE == JF_TENSOR_Q4_K) {
-                    const uint32_t dd = __ldg(reinterpret_cast<const uint32_t *>(p1 + block * 16));
-                    dw = half_bits_to_float(uint16_t(dd & 0xffffu));
-                    dmin = half_bits_to_float(uint16_t(dd >> 16));
-                } else if constexpr (TYPE == JF_TENSOR_Q6_K) {
-                    dw = half_bits_to_float(__ldg(reinterpret_cast<const uint16_t *>(p2) + block));
+            const int slot = int(i % kScaleRing);
+            cp_async_wait<kScaleRing - 1>();  // unit i's group is complete
+            __syncwarp();
+            float dw, dmin = 0.0f;
+            {
+                const uint32_t word = dring[slot * 32 + lane];
+                if constexpr (TYPE == JF_TENSOR_Q6_K) {
+                    const uint64_t block = uint64_t(row) * nb + uint32_t(w % nb);
+                    dw = half_bits_to_float(uint16_t((block & 1) ? word >> 16 : word & 0xffffu));
                 } else {
-                    const uint32_t dd = __ldg(reinterpret_cast<const uint32_t *>(p2) + block);
-                    dw = half_bits_to_float(uint16_t(dd & 0xffffu));
-                    dmin = half_bits_to_float(uint16_t(dd >> 16));
+                    dw = half_bits_to_float(uint16_t(word & 0xffffu));
+                    dmin = half_bits_to_float(uint16_t(word >> 16));
                 }
             }
-            __syncwarp();
-            da_s[lane] = tok0 + lane < p.n ? __ldg(p.da + uint64_t(tok0 + lane) * nb + b) : 0.0f;
-            __syncwarp();
+            const float * da_s = aring + slot * 32;
 
             const uint32_t acc = i & 1u, use = i >> 1;
             // the whole warp proceeds or stops together
@@ -634,14 +886,16 @@ __global__ void __launch_bounds__(kThreads, 1) mmq_tc_kernel(TcParams p) {
                     sum[8 * ch + k] += double(c);
                 }
             }
+            __syncwarp();  // every lane is done with slot `slot` before it is refilled
+            stage_scales(w + kScaleRing, slot);
 
             // a segment ends where the CTA's range or the tile's K range ends
             if (w + 1 != w_end && (w + 1) % nb != 0) continue;
             const bool complete = seg_begin == uint64_t(tile) * nb && w + 1 == uint64_t(tile + 1) * nb;
             seg_begin = w + 1;
             if (!complete) {
-                const uint32_t slot = 2 * blockIdx.x + (tile == first_tile ? 0 : 1);
-                double * part = p.partial + uint64_t(slot) * kSlotDoubles;
+                const uint32_t slot_p = 2 * blockIdx.x + (tile == first_tile ? 0 : 1);
+                double * part = p.partial + uint64_t(slot_p) * kSlotDoubles;
 #pragma unroll
                 for (int t = 0; t < kBN; ++t) part[t * kRows + m] = sum[t];
                 __threadfence();
@@ -680,6 +934,7 @@ __global__ void __launch_bounds__(kThreads, 1) mmq_tc_kernel(TcParams p) {
                 }
             }
         }
+        cp_async_wait<0>();  // no copy may land after the kernel ends
     }
     tc_fence_before();
     __syncthreads();
@@ -725,17 +980,85 @@ uint64_t workspace_bytes(const Plan & pl) {
     return partial_bytes() + uint64_t(pl.tiles) * kEpilogueWarps * sizeof(uint32_t);
 }
 
+// ---- tensor maps ----------------------------------------------------------------
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void * f = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess) {
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+        }
+    });
+    return fn;
+}
+
+// A tensor map is a pure function of its parameters, so encoded maps are
+// cached by the full parameter tuple (bounded; cleared when it grows large).
+bool byte_tensor_map(CUtensorMap & out, const void * base, uint64_t row_bytes, uint64_t rows, uint32_t box_bytes,
+                     uint32_t box_rows) {
+    using Key = std::tuple<uintptr_t, uint64_t, uint64_t, uint32_t, uint32_t>;
+    static std::mutex mu;
+    static std::map<Key, CUtensorMap> cache;
+    const Key key{reinterpret_cast<uintptr_t>(base), row_bytes, rows, box_bytes, box_rows};
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) {
+        out = it->second;
+        return true;
+    }
+    PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
+    if (encode == nullptr) return false;
+    const cuuint64_t dims[2] = {row_bytes, rows};
+    const cuuint64_t strides[1] = {row_bytes};
+    const cuuint32_t box[2] = {box_bytes, box_rows};
+    const cuuint32_t elem[2] = {1, 1};
+    CUtensorMap map;
+    std::memset(&map, 0, sizeof(map));
+    if (encode(&map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides, box, elem,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS) {
+        return false;
+    }
+    if (cache.size() >= 4096) cache.clear();
+    cache.emplace(key, map);
+    out = map;
+    return true;
+}
+
 template <uint32_t TYPE>
-jfb_status launch(const TcParams & p, uint32_t grid, cudaStream_t s) {
+jfb_status build_maps(TcMaps & maps, const TcParams & p, uint32_t cols) {
+    using T = TypeTraits<TYPE>;
+    const uint64_t nb = p.blocks;
+    bool ok = byte_tensor_map(maps.w0, p.w.plane[0], nb * T::kBlockBytes, p.w.rows, T::kW0, kRows) &&
+              byte_tensor_map(maps.w1, p.w.plane[0], nb * T::kBlockBytes, p.w.rows, T::kW1 > 0 ? T::kW1 : 16, kRows) &&
+              byte_tensor_map(maps.sc, p.w.plane[1], nb * 16, p.w.rows, 16, kRows) &&
+              byte_tensor_map(maps.act, p.qs, cols, p.n, 128, kBN) &&
+              byte_tensor_map(maps.bsums, p.bsums, uint64_t(cols) / 8, p.n, 32, kBN);
+    if (!ok) return status_error(JFB_STATUS_CUDA_ERROR, "jfb_matmul_tc: could not encode a TMA tensor map");
+    return status_ok();
+}
+
+template <uint32_t TYPE>
+jfb_status launch(TcParams & p, uint32_t cols, uint32_t grid, cudaStream_t s) {
     constexpr uint32_t bytes = smem_bytes<TYPE>();
     static_assert(bytes <= kMaxSmem, "shared memory budget");
-    static_assert(stage_count<TYPE>() >= 2, "pipeline depth");
+    static_assert(raw_count<TYPE>() >= 2, "raw pipeline depth");
+    static_assert(stage_count<TYPE>() >= 2, "operand pipeline depth");
+    static_assert(acc_columns<TYPE>() + stage_count<TYPE>() * a_columns<TYPE>() <= kTmemCols, "TMEM budget");
+    static_assert(RawLayout<TYPE>::kBytes % 128 == 0, "TMA destinations stay 128-byte aligned");
+    TcMaps maps;
+    jfb_status st = build_maps<TYPE>(maps, p, cols);
+    if (st.code != JFB_STATUS_OK) return st;
     auto kernel = mmq_tc_kernel<TYPE>;
     const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(bytes));
     if (e != cudaSuccess) {
         return status_error(JFB_STATUS_CUDA_ERROR, "jfb_matmul_tc: shared memory attribute: %s", cudaGetErrorString(e));
     }
-    kernel<<<grid, kThreads, bytes, s>>>(p);
+    kernel<<<grid, kThreads, bytes, s>>>(maps, p);
     return launch_status("jfb_matmul_tc");
 }
 
@@ -770,8 +1093,8 @@ extern "C" jfb_status jfb_matmul_tc(const jfb_weight * weight, const jfb_q8k * x
     if (x_q8->qs == nullptr || x_q8->d == nullptr || x_q8->bsums == nullptr) {
         return status_error(JFB_STATUS_INVALID_ARGUMENT, "Q8_K activation planes are required");
     }
-    if ((reinterpret_cast<uintptr_t>(x_q8->qs) & 7u) != 0 || (reinterpret_cast<uintptr_t>(x_q8->bsums) & 15u) != 0) {
-        return status_error(JFB_STATUS_INVALID_ARGUMENT, "Q8_K codes must be 8-byte and partial sums 16-byte aligned");
+    if ((reinterpret_cast<uintptr_t>(x_q8->qs) & 15u) != 0 || (reinterpret_cast<uintptr_t>(x_q8->bsums) & 15u) != 0) {
+        return status_error(JFB_STATUS_INVALID_ARGUMENT, "Q8_K codes and partial sums must be 16-byte aligned");
     }
     for (int i = 0; i < 2; ++i) {
         if ((reinterpret_cast<uintptr_t>(weight->plane[i]) & 15u) != 0) {
@@ -806,8 +1129,8 @@ extern "C" jfb_status jfb_matmul_tc(const jfb_weight * weight, const jfb_q8k * x
     p.error = error_flag;
     cudaStream_t s = as_stream(stream);
     switch (weight->type) {
-    case JF_TENSOR_Q4_K: return launch<JF_TENSOR_Q4_K>(p, pl.grid, s);
-    case JF_TENSOR_Q6_K: return launch<JF_TENSOR_Q6_K>(p, pl.grid, s);
-    default: return launch<JF_TENSOR_Q2_K>(p, pl.grid, s);
+    case JF_TENSOR_Q4_K: return launch<JF_TENSOR_Q4_K>(p, weight->cols, pl.grid, s);
+    case JF_TENSOR_Q6_K: return launch<JF_TENSOR_Q6_K>(p, weight->cols, pl.grid, s);
+    default: return launch<JF_TENSOR_Q2_K>(p, weight->cols, pl.grid, s);
     }
 }

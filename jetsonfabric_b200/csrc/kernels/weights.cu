@@ -156,7 +156,10 @@ using namespace jfb;
 
 extern "C" uint64_t jfb_weight_device_bytes(uint32_t type, uint32_t rows, uint32_t cols) {
     const PlaneSizes p = plane_sizes(type, rows, cols);
-    return align_up(p.bytes[0], kPlaneAlign) + align_up(p.bytes[1], kPlaneAlign) + align_up(p.bytes[2], kPlaneAlign);
+    // K-quant weights keep 16 bytes past the last plane, so kernels may read
+    // the whole aligned 4-byte word that holds a block's 2-byte scale
+    const uint64_t tail = is_kquant(type) ? 16 : 0;
+    return align_up(p.bytes[0], kPlaneAlign) + align_up(p.bytes[1], kPlaneAlign) + align_up(p.bytes[2] + tail, kPlaneAlign);
 }
 
 static jfb_status check_weight_shape(uint32_t type, uint32_t rows, uint32_t cols) {
