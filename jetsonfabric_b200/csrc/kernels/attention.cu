@@ -13,7 +13,9 @@
 //     of the row, and p is rounded to f16 exactly as GGML does before P V;
 //   - exp is exp_cw (common.cuh), the same method the CPU oracle implements.
 //
-// Four launches over a (row, kv head, 64-key chunk) grid:
+// Rows of up to 8192 keys with head_dim 64 or 128 take a single launch (see
+// the single-launch path below). Otherwise four launches over a
+// (row, kv head, 64-key chunk) grid:
 //   1. scores x_j (and each chunk's maximum) -> scratch
 //   2. per (row, head): max over chunks, sum_j exp(x_j - max) in double
 //   3. P V partial sums per chunk in double -> scratch
@@ -249,6 +251,262 @@ __global__ void __launch_bounds__(256) combine_kernel(const int32_t * __restrict
     }
 }
 
+// ---- single-launch path -------------------------------------------------------
+//
+// One CTA per (row, kv head, group of HPC query heads) does the whole row:
+//   scores   16 lanes per key for D = 128 (each lane 8 dims, one 16-byte load
+//            of the K row, so a K row is one coalesced 256-byte read); each
+//            lane keeps its 8 dims of f16(q) for the HPC heads in registers
+//            as doubles and accumulates k*q with DFMA (the f16*f16 product is
+//            exact, so this equals adding the exact products in double); the
+//            lane partials are added by a shuffle tree;
+//   softmax  block reductions for the maximum and the double sum of exp;
+//   P V      each thread owns 4 dims x HPC heads in double over an interleaved
+//            share of the keys; the shares are added in a fixed order.
+// The exact semantics are those of the four-launch path above. Scores and
+// probabilities live in shared memory, so the row's key count is bounded by
+// kFusedMaxKeys; longer rows use the four-launch path.
+constexpr int kFusedThreads = 256;
+constexpr uint32_t kFusedMaxKeys = 8192;
+
+template <int HPC, int D>
+__host__ __device__ constexpr uint32_t fused_smem_bytes(uint32_t keys_cap) {
+    return (kFusedThreads / (D / 4)) * HPC * D * 8  // PV partials [S][HPC][D] double
+           + HPC * D * 4                             // output values of the CTA
+           + HPC * keys_cap * 4;                     // scores / probabilities [HPC][keys_cap]
+}
+
+template <int HPC, int D>
+__global__ void __launch_bounds__(kFusedThreads, 1) fused_kernel(const float * __restrict__ q, const int32_t * __restrict__ seq,
+                                                            const int32_t * __restrict__ pos, uint32_t heads,
+                                                            uint32_t kv_heads, const jfb_kv_slot * __restrict__ slots,
+                                                            uint32_t layer, float scale, uint32_t keys_cap,
+                                                            float * __restrict__ out, jfb_q8k q8, int quantize) {
+    constexpr int L = D / 8;                  // lanes per key in the score pass
+    constexpr int KPW = 32 / L;               // keys per warp step
+    constexpr int DT = D / 4;                 // threads per key share in the P V pass
+    constexpr int S = kFusedThreads / DT;     // key shares
+    constexpr int W = kFusedThreads / 32;
+    extern __shared__ __align__(16) uint8_t smem_raw[];
+    double * red = reinterpret_cast<double *>(smem_raw);   // [S][HPC][D]
+    float * outs = reinterpret_cast<float *>(red + S * HPC * D);  // [HPC * D]
+    float * xs = outs + HPC * D;                            // [HPC][keys_cap]
+    __shared__ float wmax[W][HPC];
+    __shared__ double wsum[W][HPC];
+    __shared__ float stat[HPC][2];  // max, 1 / sum
+    __shared__ unsigned long long q8_keys[8];
+
+    const uint32_t r = blockIdx.x;
+    const uint32_t G = heads / kv_heads, groups = G / HPC;
+    const uint32_t kvh = blockIdx.y / groups;
+    const uint32_t h0 = kvh * G + (blockIdx.y % groups) * HPC;  // first query head of this CTA
+    // keys beyond the caller's max_keys are ignored, as on the four-launch path
+    const uint32_t keys = min(uint32_t(pos[r]) + 1u, keys_cap), kvd = kv_heads * D;
+    const jfb_kv_slot slot = slots[seq[r]];
+    const uint16_t * kbase = slot.k + uint64_t(layer) * slot.capacity * kvd + kvh * D;
+    const uint16_t * vbase = slot.v + uint64_t(layer) * slot.capacity * kvd + kvh * D;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    // ---- scores
+    {
+        const int sub = lane / L, li = lane % L;
+        double qr[HPC][8];
+#pragma unroll
+        for (int h = 0; h < HPC; ++h) {
+            const float * qh = q + uint64_t(r) * heads * D + uint64_t(h0 + h) * D + 8 * li;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                qr[h][e] = double(__half2float(__float2half_rn(qh[e])));
+                asm volatile("" : "+d"(qr[h][e]));  // keep in a register: no reload inside the key loop
+            }
+        }
+        float mx[HPC];
+#pragma unroll
+        for (int h = 0; h < HPC; ++h) mx[h] = -INFINITY;
+        constexpr int U = 8;  // key steps whose loads are in flight together
+        for (uint32_t jb = uint32_t(warp) * KPW; jb < keys; jb += W * KPW * U) {
+            uint4 raw[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const uint32_t j = jb + uint32_t(u * W * KPW + sub);
+                raw[u] = j < keys ? __ldg(reinterpret_cast<const uint4 *>(kbase + uint64_t(j) * kvd + 8 * li))
+                                  : make_uint4(0, 0, 0, 0);
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const uint32_t j = jb + uint32_t(u * W * KPW + sub);
+                double acc[HPC];
+#pragma unroll
+                for (int h = 0; h < HPC; ++h) acc[h] = 0.0;
+                const uint32_t wv[4] = {raw[u].x, raw[u].y, raw[u].z, raw[u].w};
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    const double kd = double(half_bits_to_float(uint16_t(wv[e / 2] >> (16 * (e & 1)))));
+#pragma unroll
+                    for (int h = 0; h < HPC; ++h) acc[h] = fma(kd, qr[h][e], acc[h]);
+                }
+#pragma unroll
+                for (int o = L / 2; o > 0; o >>= 1) {
+#pragma unroll
+                    for (int h = 0; h < HPC; ++h) acc[h] += __shfl_xor_sync(0xffffffffu, acc[h], o);
+                }
+                if (li == 0 && j < keys) {
+#pragma unroll
+                    for (int h = 0; h < HPC; ++h) {
+                        const float x = __fmul_rn(__double2float_rn(acc[h]), scale);
+                        xs[h * keys_cap + j] = x;
+                        mx[h] = fmaxf(mx[h], x);
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int h = 0; h < HPC; ++h) {
+            const float m = warp_max(mx[h]);
+            if (lane == 0) wmax[warp][h] = m;
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x < HPC) {
+        float m = -INFINITY;
+        for (int w = 0; w < W; ++w) m = fmaxf(m, wmax[w][threadIdx.x]);
+        stat[threadIdx.x][0] = m;
+    }
+    __syncthreads();
+
+    // ---- softmax: e = exp(x - max), 1 / double sum, p = f16(e * inv)
+    {
+        double sum[HPC];
+#pragma unroll
+        for (int h = 0; h < HPC; ++h) {
+            const float m = stat[h][0];
+            double acc = 0.0;
+            for (uint32_t j = threadIdx.x; j < keys; j += kFusedThreads) {
+                const float e = exp_cw(__fsub_rn(xs[h * keys_cap + j], m));
+                xs[h * keys_cap + j] = e;
+                acc += double(e);
+            }
+            sum[h] = warp_sum(acc);
+        }
+        if (lane == 0) {
+#pragma unroll
+            for (int h = 0; h < HPC; ++h) wsum[warp][h] = sum[h];
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x < HPC) {
+        double t = 0.0;
+        for (int w = 0; w < W; ++w) t += wsum[w][threadIdx.x];
+        stat[threadIdx.x][1] = __double2float_rn(__ddiv_rn(1.0, t));  // t >= 1 (the maximum contributes 1)
+    }
+    __syncthreads();
+#pragma unroll
+    for (int h = 0; h < HPC; ++h) {
+        const float inv = stat[h][1];
+        for (uint32_t j = threadIdx.x; j < keys; j += kFusedThreads) {
+            xs[h * keys_cap + j] = __half2float(__float2half_rn(__fmul_rn(xs[h * keys_cap + j], inv)));
+        }
+    }
+    __syncthreads();
+
+    // ---- P V
+    {
+        const int dq = threadIdx.x % DT, share = threadIdx.x / DT;
+        double acc[HPC][4];
+#pragma unroll
+        for (int h = 0; h < HPC; ++h) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) acc[h][e] = 0.0;
+        }
+        constexpr int U = 8;  // keys whose V loads are in flight together
+        for (uint32_t jb = uint32_t(share); jb < keys; jb += S * U) {
+            uint2 raw[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const uint32_t j = jb + uint32_t(u * S);
+                raw[u] = j < keys ? __ldg(reinterpret_cast<const uint2 *>(vbase + uint64_t(j) * kvd + 4 * dq))
+                                  : make_uint2(0, 0);
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const uint32_t j = jb + uint32_t(u * S);
+                if (j >= keys) break;
+                const double v0 = double(half_bits_to_float(uint16_t(raw[u].x & 0xffffu)));
+                const double v1 = double(half_bits_to_float(uint16_t(raw[u].x >> 16)));
+                const double v2 = double(half_bits_to_float(uint16_t(raw[u].y & 0xffffu)));
+                const double v3 = double(half_bits_to_float(uint16_t(raw[u].y >> 16)));
+#pragma unroll
+                for (int h = 0; h < HPC; ++h) {
+                    const double pj = double(xs[h * keys_cap + j]);
+                    acc[h][0] = fma(v0, pj, acc[h][0]);
+                    acc[h][1] = fma(v1, pj, acc[h][1]);
+                    acc[h][2] = fma(v2, pj, acc[h][2]);
+                    acc[h][3] = fma(v3, pj, acc[h][3]);
+                }
+            }
+        }
+#pragma unroll
+        for (int h = 0; h < HPC; ++h) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) red[(share * HPC + h) * D + 4 * dq + e] = acc[h][e];
+        }
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < HPC * D; i += kFusedThreads) {
+        double t = 0.0;
+#pragma unroll
+        for (int sh = 0; sh < S; ++sh) t += red[sh * HPC * D + i];
+        const float v = __double2float_rn(t);
+        outs[i] = v;
+        out[uint64_t(r) * heads * D + uint64_t(h0) * D + i] = v;
+    }
+    if (!quantize) return;
+    __syncthreads();
+    const uint32_t blocks_per_row = heads * D / kQK;
+#pragma unroll 1
+    for (int c = 0; c < HPC * D / kQK; ++c) {
+        const uint64_t block = uint64_t(r) * blocks_per_row + (uint64_t(h0) * D) / kQK + c;
+        q8k_block_256(outs[c * kQK + threadIdx.x], q8.qs + block * kQK, q8.d + block, q8.bsums + block * 16, q8_keys);
+    }
+}
+
+template <int D>
+jfb_status launch_fused_d(int hpc, const float * q, uint32_t n, const int32_t * seq, const int32_t * pos, uint32_t heads,
+                          uint32_t kv_heads, const jfb_kv_slot * slots, uint32_t layer, float scale,
+                          uint32_t keys_cap, float * out, jfb_q8k q8, int quantize, cudaStream_t s) {
+    const dim3 grid(n, kv_heads * ((heads / kv_heads) / uint32_t(hpc)));
+    auto go = [&](auto kernel, uint32_t bytes) -> jfb_status {
+        const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(bytes));
+        if (e != cudaSuccess) {
+            return status_error(JFB_STATUS_CUDA_ERROR, "attention shared memory attribute: %s", cudaGetErrorString(e));
+        }
+        kernel<<<grid, kFusedThreads, bytes, s>>>(q, seq, pos, heads, kv_heads, slots, layer, scale, keys_cap, out, q8,
+                                                  quantize);
+        return launch_status("jfb_attention");
+    };
+    switch (hpc) {
+    case 4: return go(fused_kernel<4, D>, fused_smem_bytes<4, D>(keys_cap));
+    case 3: return go(fused_kernel<3, D>, fused_smem_bytes<3, D>(keys_cap));
+    case 2: return go(fused_kernel<2, D>, fused_smem_bytes<2, D>(keys_cap));
+    default: return go(fused_kernel<1, D>, fused_smem_bytes<1, D>(keys_cap));
+    }
+}
+
+// Query heads per CTA of the single-launch path: the largest of 4, 3, 2, 1
+// dividing the group, halved while that leaves the GPU without a full wave.
+int fused_heads_per_cta(uint32_t n, uint32_t heads, uint32_t kv_heads) {
+    const uint32_t G = heads / kv_heads;
+    int hpc = 1;
+    for (int c = 4; c >= 1; --c) {
+        if (G % uint32_t(c) == 0) {
+            hpc = c;
+            break;
+        }
+    }
+    while (hpc % 2 == 0 && uint64_t(n) * kv_heads * (G / uint32_t(hpc)) < 148) hpc /= 2;
+    return hpc;
+}
+
 }  // namespace
 }  // namespace jfb
 
@@ -282,6 +540,19 @@ extern "C" jfb_status jfb_attention(const float * q, uint32_t n, const int32_t *
         return status_error(JFB_STATUS_INVALID_ARGUMENT, "attention grid too large");
     }
     cudaStream_t s = as_stream(stream);
+    const jfb_q8k q8_fused = out_q8 != nullptr ? *out_q8 : jfb_q8k{nullptr, nullptr, nullptr};
+    if ((head_dim == 64 || head_dim == 128) && max_keys <= kFusedMaxKeys) {
+        const int hpc = fused_heads_per_cta(n, heads, kv_heads);
+        const uint32_t keys_cap = (max_keys + 3) / 4 * 4;
+        const bool fused_q8 = out_q8 != nullptr && (uint32_t(hpc) * head_dim) % kQK == 0;
+        const float fscale = 1.0f / sqrtf(float(head_dim));
+        jfb_status st = head_dim == 64 ? launch_fused_d<64>(hpc, q, n, seq, pos, heads, kv_heads, slots, layer, fscale,
+                                                            keys_cap, out, q8_fused, fused_q8 ? 1 : 0, s)
+                                       : launch_fused_d<128>(hpc, q, n, seq, pos, heads, kv_heads, slots, layer, fscale,
+                                                             keys_cap, out, q8_fused, fused_q8 ? 1 : 0, s);
+        if (st.code != JFB_STATUS_OK || out_q8 == nullptr || fused_q8) return st;
+        return jfb_quantize_q8k(out, n, heads * head_dim, out_q8, stream);
+    }
     const Scratch sc = carve(scratch, n, heads, head_dim, splits);
     const float scale = 1.0f / sqrtf(float(head_dim));
     scores_kernel<<<dim3(n, kv_heads, splits), kThreads, 0, s>>>(q, seq, pos, heads, kv_heads, head_dim, slots, layer,

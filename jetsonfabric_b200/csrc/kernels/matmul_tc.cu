@@ -549,15 +549,17 @@ __device__ __forceinline__ void convert_a_dispatch(const uint8_t * r, int h, int
     }
 }
 
-// The 16 per-16-value mins of one block as a K = 16 f16 operand row (Q4_K:
-// the 6-bit min of each 32-value sub-block, twice; Q2_K: the high nibble of
-// each scale byte), from the raw scale row of tile row m.
-template <uint32_t TYPE>
+// Mins of 16-value groups [8*PART, 8*PART + 8) of one block as half of a
+// K = 16 f16 operand row (Q4_K: the 6-bit min of each 32-value sub-block,
+// twice; Q2_K: the high nibble of each scale byte), from the raw scale row of
+// tile row m. The two parts of a row write the two 16-byte core columns.
+template <uint32_t TYPE, int PART>
 __device__ __forceinline__ void convert_mins(const uint8_t * r, uint8_t * tile, int m) {
     const uint4 meta = *reinterpret_cast<const uint4 *>(r + RawLayout<TYPE>::kScOff + m * 16);
-    uint32_t h2[8];
+    uint32_t h2[4];
 #pragma unroll
-    for (int g = 0; g < 16; g += 2) {
+    for (int k = 0; k < 4; ++k) {
+        const int g = 8 * PART + 2 * k;
         int m0, m1;
         if constexpr (TYPE == JF_TENSOR_Q4_K) {
             int sc;
@@ -568,11 +570,9 @@ __device__ __forceinline__ void convert_mins(const uint8_t * r, uint8_t * tile, 
             m1 = int(byte_at(meta, g + 1) >> 4);
         }
         const uint32_t u = (uint32_t(m0) | 0x6400u) | ((uint32_t(m1) | 0x6400u) << 16);  // mins < 64
-        h2[g / 2] = h2_bits(__hsub2(bits_h2(u), h2_int_const<1024>()));
+        h2[k] = h2_bits(__hsub2(bits_h2(u), h2_int_const<1024>()));
     }
-    uint8_t * base = tile + (m >> 3) * kSbo16 + (m & 7) * 16;
-    *reinterpret_cast<uint4 *>(base) = make_uint4(h2[0], h2[1], h2[2], h2[3]);
-    *reinterpret_cast<uint4 *>(base + 128) = make_uint4(h2[4], h2[5], h2[6], h2[7]);
+    *reinterpret_cast<uint4 *>(tile + (m >> 3) * kSbo16 + PART * 128 + (m & 7) * 16) = make_uint4(h2[0], h2[1], h2[2], h2[3]);
 }
 
 template <uint32_t TYPE>
@@ -699,15 +699,25 @@ __global__ void __launch_bounds__(kThreads, 1) mmq_tc_kernel(const __grid_consta
                 const uint8_t * r = raw + rs * RL::kBytes;
                 uint8_t * st = smem + stage * kStage;
                 convert_a_dispatch<TYPE>(r, h, part, tmem + lane_base + kAccCols + stage * kACols, m);
-                if (T::kMins && h == 0 && part == 0) convert_mins<TYPE>(r, st + kA2Off, m);
-                // activation codes: kBN rows x 16 chunks of 8
-                for (int idx = pt; idx < kBN * 16; idx += kConverterThreads) {
-                    const int t = idx >> 4, c = idx & 15;
-                    const uint2 v = *reinterpret_cast<const uint2 *>(r + RL::kActOff + t * 128 + 8 * c);
-                    const uint2 x = scaled4(v.x ^ 0x80808080u, one, act_nbias);
-                    const uint2 y = scaled4(v.y ^ 0x80808080u, one, act_nbias);
-                    *reinterpret_cast<uint4 *>(st + kBOff + (t >> 3) * kSbo + c * 128 + (t & 7) * 16) =
-                        make_uint4(x.x, x.y, y.x, y.y);
+                if (T::kMins && h == 0) {
+                    if (part == 0) convert_mins<TYPE, 0>(r, st + kA2Off, m);
+                    else convert_mins<TYPE, 1>(r, st + kA2Off, m);
+                }
+                // activation codes: one token t and 16 codes (chunk pair c16) per
+                // thread. The raw tile arrives 128-byte swizzled (16-byte chunk c
+                // of token row t at chunk c ^ (t & 7)), so the 8 lanes that share
+                // c16 read 8 different bank groups; they also write 128
+                // contiguous bytes of the B tile.
+                {
+                    const int t_low = pt & 7, c16 = (pt >> 3) & 7, t = ((pt >> 6) << 3) | t_low;
+                    const uint4 v = *reinterpret_cast<const uint4 *>(r + RL::kActOff + t * 128 + ((c16 ^ t_low) << 4));
+                    const uint2 a = scaled4(v.x ^ 0x80808080u, one, act_nbias);
+                    const uint2 b = scaled4(v.y ^ 0x80808080u, one, act_nbias);
+                    const uint2 c = scaled4(v.z ^ 0x80808080u, one, act_nbias);
+                    const uint2 d = scaled4(v.w ^ 0x80808080u, one, act_nbias);
+                    uint8_t * dst = st + kBOff + (t >> 3) * kSbo + (2 * c16) * 128 + (t & 7) * 16;
+                    *reinterpret_cast<uint4 *>(dst) = make_uint4(a.x, a.y, b.x, b.y);
+                    *reinterpret_cast<uint4 *>(dst + 128) = make_uint4(c.x, c.y, d.x, d.y);
                 }
                 if (T::kMins && h == 0 && pt < kBN * 2) {
                     const int t = pt >> 1, c = pt & 1;
@@ -999,11 +1009,11 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 // A tensor map is a pure function of its parameters, so encoded maps are
 // cached by the full parameter tuple (bounded; cleared when it grows large).
 bool byte_tensor_map(CUtensorMap & out, const void * base, uint64_t row_bytes, uint64_t rows, uint32_t box_bytes,
-                     uint32_t box_rows) {
-    using Key = std::tuple<uintptr_t, uint64_t, uint64_t, uint32_t, uint32_t>;
+                     uint32_t box_rows, bool swizzle128 = false) {
+    using Key = std::tuple<uintptr_t, uint64_t, uint64_t, uint32_t, uint32_t, bool>;
     static std::mutex mu;
     static std::map<Key, CUtensorMap> cache;
-    const Key key{reinterpret_cast<uintptr_t>(base), row_bytes, rows, box_bytes, box_rows};
+    const Key key{reinterpret_cast<uintptr_t>(base), row_bytes, rows, box_bytes, box_rows, swizzle128};
     std::lock_guard<std::mutex> lock(mu);
     auto it = cache.find(key);
     if (it != cache.end()) {
@@ -1019,7 +1029,8 @@ bool byte_tensor_map(CUtensorMap & out, const void * base, uint64_t row_bytes, u
     CUtensorMap map;
     std::memset(&map, 0, sizeof(map));
     if (encode(&map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides, box, elem,
-               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS) {
         return false;
     }
@@ -1036,7 +1047,7 @@ jfb_status build_maps(TcMaps & maps, const TcParams & p, uint32_t cols) {
     bool ok = byte_tensor_map(maps.w0, p.w.plane[0], nb * T::kBlockBytes, p.w.rows, T::kW0, kRows) &&
               byte_tensor_map(maps.w1, p.w.plane[0], nb * T::kBlockBytes, p.w.rows, T::kW1 > 0 ? T::kW1 : 16, kRows) &&
               byte_tensor_map(maps.sc, p.w.plane[1], nb * 16, p.w.rows, 16, kRows) &&
-              byte_tensor_map(maps.act, p.qs, cols, p.n, 128, kBN) &&
+              byte_tensor_map(maps.act, p.qs, cols, p.n, 128, kBN, true) &&
               byte_tensor_map(maps.bsums, p.bsums, uint64_t(cols) / 8, p.n, 32, kBN);
     if (!ok) return status_error(JFB_STATUS_CUDA_ERROR, "jfb_matmul_tc: could not encode a TMA tensor map");
     return status_ok();
@@ -1049,7 +1060,9 @@ jfb_status launch(TcParams & p, uint32_t cols, uint32_t grid, cudaStream_t s) {
     static_assert(raw_count<TYPE>() >= 2, "raw pipeline depth");
     static_assert(stage_count<TYPE>() >= 2, "operand pipeline depth");
     static_assert(acc_columns<TYPE>() + stage_count<TYPE>() * a_columns<TYPE>() <= kTmemCols, "TMEM budget");
-    static_assert(RawLayout<TYPE>::kBytes % 128 == 0, "TMA destinations stay 128-byte aligned");
+    static_assert(RawLayout<TYPE>::kBytes % 1024 == 0 && RawLayout<TYPE>::kActOff % 1024 == 0,
+                  "raw stages and the swizzled activation box stay 1024-byte aligned");
+    static_assert(kConverterThreads == kBN * 8, "one converter thread per token and 16-code chunk");
     TcMaps maps;
     jfb_status st = build_maps<TYPE>(maps, p, cols);
     if (st.code != JFB_STATUS_OK) return st;
