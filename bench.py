@@ -22,9 +22,17 @@ L2 (126 MB), so every decode step streams them from HBM.
 
 --impl reference runs the CPU oracle on the host cores instead (the
 reference's own native engine needs GGML, which cannot be built here).
-With torchrun (N > 1) every rank serves its own full-model replica of the
-workload on its GPU (weak scaling, no data-path collective); the value is
-the tokens of all ranks over the slowest rank's time.
+
+With torchrun (N > 1) the same workload runs as an N-stage pipeline (one
+process and GPU per contiguous layer range, jetsonfabric_b200/pipeline.py):
+F16 activations cross each stage boundary over NCCL point-to-point (NVLink),
+the last stage returns each micro-batch's greedy tokens to the first, and N
+micro-batches of sequences keep every stage busy. The workload is fixed as N
+grows (strong scaling); the value is its output tokens over the slowest
+rank's device time. TTFT and ITL are measured on the last stage. e2e runs
+the same pipeline through the host-buffer C ABI with host activations
+exchanged over gloo. --replicas instead gives every rank its own full-model
+replica (weak scaling, a comparison only).
 """
 from __future__ import annotations
 
@@ -67,6 +75,8 @@ def parse():
     p.add_argument("--package-dir", default=os.environ.get("JFB_BENCH_DIR", "/tmp/jfb_bench"))
     p.add_argument("--skip-e2e", action="store_true")
     p.add_argument("--skip-cpu", action="store_true")
+    p.add_argument("--micro-batches", type=int, default=0, help="pipeline micro-batches (default: one per stage)")
+    p.add_argument("--replicas", action="store_true", help="N > 1: full-model replicas instead of a pipeline")
     return p.parse_args()
 
 
@@ -295,6 +305,169 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     return result
 
 
+def run_pipeline(args, rank: int, world: int, local_rank: int) -> dict | None:
+    """N-stage pipeline over contiguous layer ranges (see the module docstring)."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+    from jetsonfabric_b200 import engine as E
+    from jetsonfabric_b200 import pipeline as PL
+
+    torch.cuda.set_device(local_rank)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local_rank))
+    pkg = ensure_package(args, local_rank)
+    dist.barrier()
+    preset = PRESETS[args.preset]
+    L = preset["layer_count"]
+    ranges = PL.stage_ranges(L, world)
+    start, end = ranges[rank]
+    eng = E.NativeEngine(pkg, "cuda", layer_start=start, layer_end=end, device=local_rank)
+    groups = PL.make_groups(world)
+    PL.warm_groups(rank, world, groups, device=torch.device("cuda", local_rank))
+    link = PL.TorchLink(rank, world, groups)
+    C, P, O = args.concurrency, args.prompt_tokens, args.output_tokens
+    micro = args.micro_batches or world
+    batches = PL.split_batches(C, micro)
+    prompts = prompts_for(args, preset["vocabulary_size"]).tolist()
+    stage = PL.EngineStage(eng, prompts, batches, capacity=P + O - 1)
+    last = rank == world - 1
+    launches = {"n": 0}
+
+    def one_run():
+        stage.reset()
+        torch.cuda.synchronize()
+        dist.barrier()
+        marks = {}
+        with torch.cuda.stream(stage.stream):
+            t0 = torch.cuda.Event(enable_timing=True)
+            t0.record(stage.stream)
+
+            def on_output(step, m, _out):
+                ev = torch.cuda.Event(enable_timing=True)
+                ev.record(stage.stream)
+                marks[(step, m)] = ev
+
+            orig_forward = stage.forward
+
+            def counted(m, prefill, inputs):
+                out = orig_forward(m, prefill, inputs)
+                launches["n"] += eng.last_launch_count()
+                return out
+
+            stage.forward = counted
+            try:
+                PL.run_schedule(rank, world, batches, [P] * C, O, stage, link, on_output if last else None)
+            finally:
+                stage.forward = orig_forward
+            t1 = torch.cuda.Event(enable_timing=True)
+            t1.record(stage.stream)
+        torch.cuda.synchronize()
+        total = t0.elapsed_time(t1)
+        ttft, gaps = [], []
+        if last:
+            for m in range(len(batches)):
+                ttft.append(t0.elapsed_time(marks[(0, m)]))
+                for t in range(1, O):
+                    gaps.append(marks[(t - 1, m)].elapsed_time(marks[(t, m)]))
+        return total, ttft, gaps
+
+    for _ in range(max(args.warmup, 0)):
+        one_run()
+    totals, ttfts, gaps = [], [], []
+    launches["n"] = 0
+    with ClockSampler(local_rank) as clocks:
+        for _ in range(args.steps):
+            t, tt, g = one_run()
+            totals.append(t)
+            ttfts.extend(tt)
+            gaps.extend(g)
+    ms = torch.tensor([statistics.mean(totals)], device="cuda", dtype=torch.float64)
+    dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    launch_total = torch.tensor([launches["n"]], device="cuda", dtype=torch.float64)
+    dist.all_reduce(launch_total, op=dist.ReduceOp.SUM)
+    lat = torch.zeros(3, device="cuda", dtype=torch.float64)
+    if last:
+        lat[0] = statistics.median(ttfts)
+        lat[1] = statistics.median(gaps)
+        lat[2] = statistics.mean(gaps)
+    dist.broadcast(lat, src=world - 1)
+    ms_per_step = float(ms.item())
+    value = C * O / (ms_per_step / 1000.0)
+
+    # roofline of the first stage's decode matmuls: one timed decode pass of micro-batch 0
+    timing: dict = {}
+    if rank == 0:
+        stage.reset()
+        with torch.cuda.stream(stage.stream):
+            mb = batches[0]
+            acts = stage.forward(0, True, stage.prompt_tokens(0))
+            toks = torch.zeros(len(mb), dtype=torch.int32, device="cuda")
+            eng.set_kernel_timing(True)
+            stage.forward(0, False, toks)
+            eng.set_kernel_timing(False)
+            timing = eng.kernel_timing()
+        del acts
+    torch.cuda.synchronize()
+    dist.barrier()
+
+    # end to end: host-buffer C ABI, host activations over gloo
+    e2e = None
+    if not args.skip_e2e:
+        hgroups = PL.make_groups(world, backend="gloo")
+        PL.warm_groups(rank, world, hgroups)
+        hlink = PL.TorchLink(rank, world, hgroups)
+        hstage = PL.HostEngineStage(eng, prompts, batches, capacity=P + O - 1)
+        times = []
+        for _ in range(max(1, args.steps)):
+            hstage.reset()
+            dist.barrier()
+            a = time.perf_counter()
+            PL.run_schedule(rank, world, batches, [P] * C, O, hstage, hlink)
+            times.append(time.perf_counter() - a)
+        hstage.close()
+        sec = torch.tensor([statistics.mean(times)], device="cuda", dtype=torch.float64)
+        dist.all_reduce(sec, op=dist.ReduceOp.MAX)
+        h = preset["embedding_length"]
+        rows = C * P + C * (O - 1)
+        hop_bytes = rows * h * 4 * (world - 1)  # f32 activations through the C ABI at every boundary
+        e2e = {"value": C * O / float(sec.item()), "unit": UNIT,
+               "h2d_bytes_per_step": C * P * 4 + (O - 1) * C * 4 + hop_bytes,
+               "d2h_bytes_per_step": O * C * 4 + hop_bytes}
+
+    result = None
+    if rank == 0:
+        peaks = measured_peaks()
+        roof = None
+        if timing.get("matmul_ms"):
+            achieved = timing["matmul_bytes"] / (timing["matmul_ms"] / 1000.0) / 1e9
+            roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                    "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": traffic_from_profiles(),
+                    "kernel": f"decode matmuls of stage 0 (layers {ranges[0][0]}-{ranges[0][1]}), one micro-batch "
+                              f"of {len(batches[0])} rows",
+                    "launches": timing["matmul_launches"], "peak_source": peaks["source"]}
+        result = {
+            "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_per_step, 3), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "q4_k/q6_k x q8_k int8 dot, f32 accumulate",
+            "data": "synthetic (seeded N(0,0.02) weights, uniform-random prompt ids)",
+            "config": {"workload": f"qwen2-{args.preset}-q4km c{C} p{P} o{O}", "model": f"Qwen2-arch {args.preset} Q4_K_M",
+                       "concurrency": C, "prompt_tokens": P, "output_tokens": O, "global_batch": C, "seq_len": P + O,
+                       "parallelism": f"pp{world}", "stages": ranges, "micro_batches": [len(b) for b in batches],
+                       "boundary": "F16 codec over NCCL send/recv (NVLink)",
+                       "l2": "weights exceed L2 every decode step"},
+            "ttft_p50_ms": round(float(lat[0].item()), 3), "itl_p50_ms": round(float(lat[1].item()), 4),
+            "decode_tok_s": round(C / (float(lat[2].item()) / 1000.0), 1),
+            "e2e": e2e, "roofline": roof, "cpu_baseline": None, "clocks": clocks.summary(),
+            "gpu_launches": int(float(launch_total.item()) / max(1, args.steps) * args.steps),
+        }
+    stage.close()
+    eng.close()
+    dist.barrier()
+    dist.destroy_process_group()
+    return result
+
+
 def traffic_from_profiles():
     path = REPO / "profiles" / "decode_matmul_traffic.json"
     if path.exists():
@@ -383,6 +556,8 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         result = run_reference(args, rank)
+    elif world > 1 and not args.replicas:
+        result = run_pipeline(args, rank, world, local_rank)
     else:
         result = run_ours(args, rank, world, local_rank)
     if result is not None:

@@ -153,6 +153,19 @@ jfb_status jfb_engine_decode_batch_device(jfb_engine * engine, jfb_session * con
 jfb_status jfb_engine_prefill_batch_device(jfb_engine * engine, jfb_session * const * sessions, size_t count,
                                            const int32_t * tokens_device, const uint32_t * token_counts,
                                            int32_t * tokens_out_device);
+/* Device-resident pass of one pipeline stage over a batch of sessions. The
+ * first stage reads token ids (tokens_device), later stages f32 activations
+ * [rows][hidden] (activations_device); the last stage writes one greedy token
+ * per session (tokens_out_device), the others f32 activations [rows][hidden]
+ * (activations_out_device). All four are device memory. prefill selects the
+ * prompt rows of each session (row_counts, host memory) or one decode row per
+ * session. Nothing is copied to the host and the call returns without waiting
+ * for the GPU. The engine counterpart of one Stagewire hop of the reference
+ * pipeline (native_stage_executor.cpp:143-180 per session). */
+jfb_status jfb_engine_stage_batch_device(jfb_engine * engine, jfb_session * const * sessions, size_t count,
+                                         int prefill, const uint32_t * row_counts, const int32_t * tokens_device,
+                                         const float * activations_device, int32_t * tokens_out_device,
+                                         float * activations_out_device);
 jfb_status jfb_engine_synchronize(jfb_engine * engine);
 
 /* Device time and algorithmic bytes of the matmul and attention launches of

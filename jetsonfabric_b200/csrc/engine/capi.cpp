@@ -438,6 +438,23 @@ jfb_status jfb_engine_decode_batch_device(jfb_engine * engine, jfb_session * con
     });
 }
 
+jfb_status jfb_engine_stage_batch_device(jfb_engine * engine, jfb_session * const * sessions, size_t count,
+                                         int prefill, const uint32_t * row_counts, const int32_t * tokens_device,
+                                         const float * activations_device, int32_t * tokens_out_device,
+                                         float * activations_out_device) {
+    if (engine == nullptr || (prefill && row_counts == nullptr)) {
+        return make(JFB_STATUS_INVALID_ARGUMENT, "engine and, for prefill, row counts are required");
+    }
+    return guarded([&] {
+        DeviceScope scope(engine->device);
+        const auto list = unwrap(engine, sessions, count);
+        native::detail::stage_batch_device(
+            *engine->engine, list, prefill != 0,
+            prefill ? std::span<const std::uint32_t>(row_counts, count) : std::span<const std::uint32_t>(),
+            tokens_device, activations_device, tokens_out_device, activations_out_device);
+    });
+}
+
 jfb_status jfb_engine_prefill_batch_device(jfb_engine * engine, jfb_session * const * sessions, size_t count,
                                            const int32_t * tokens_device, const uint32_t * token_counts,
                                            int32_t * tokens_out_device) {

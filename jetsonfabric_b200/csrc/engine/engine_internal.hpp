@@ -18,6 +18,12 @@ void decode_batch_device(NativeEngine & engine, std::span<NativeSession * const>
 void prefill_batch_device(NativeEngine & engine, std::span<NativeSession * const> sessions,
                           const std::int32_t * tokens_device, std::span<const std::uint32_t> counts,
                           std::int32_t * tokens_out_device);
+// Device-resident pass of any stage (tokens or activations in, tokens or
+// activations out, all device memory); returns without synchronising.
+void stage_batch_device(NativeEngine & engine, std::span<NativeSession * const> sessions, bool prefill,
+                        std::span<const std::uint32_t> counts, const std::int32_t * tokens_device,
+                        const float * activations_device, std::int32_t * tokens_out_device,
+                        float * activations_out_device);
 void synchronize(NativeEngine & engine);
 void * stream(NativeEngine & engine);
 std::uint64_t last_launch_count(const NativeEngine & engine);

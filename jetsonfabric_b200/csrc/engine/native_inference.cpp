@@ -229,14 +229,26 @@ struct BatchAccess {
         return std::move(run(s->engine, std::span<Item>(&item, 1), prefill, logits).front());
     }
 
-    // Device-resident pass of a full-model engine (no host copies, no sync).
+    // Device-resident pass of any stage (no host copies, no sync): the first
+    // stage reads token ids, later stages f32 activations [rows][h]; the last
+    // stage writes one greedy token per session, the others f32 activations.
     static void run_device(NativeEngine & engine, std::span<NativeSession * const> sessions, bool prefill,
-                           const std::int32_t * tokens_device, std::span<const std::uint32_t> counts,
-                           std::int32_t * tokens_out_device) {
+                           const std::int32_t * tokens_device, const float * activations_device,
+                           std::span<const std::uint32_t> counts, std::int32_t * tokens_out_device,
+                           float * activations_out_device) {
         NativeEngine::Impl & e = *engine.impl_;
         std::lock_guard lock(e.mutex);
-        if (!e.model->first_stage() || !e.model->last_stage()) {
-            throw std::logic_error("full-model native inference requires every model layer");
+        const bool first = e.model->first_stage(), last = e.model->last_stage();
+        if (first ? tokens_device == nullptr : activations_device == nullptr) {
+            throw std::invalid_argument(first ? "only the first native stage accepts tokens"
+                                              : "the first native stage does not accept activations");
+        }
+        if (last ? tokens_out_device == nullptr : activations_out_device == nullptr) {
+            throw std::invalid_argument(last ? "the last native stage returns greedy tokens"
+                                             : "an intermediate native stage returns activations");
+        }
+        if (prefill && counts.size() != sessions.size()) {
+            throw std::invalid_argument("one prompt length per session is required");
         }
         std::unordered_set<const NativeSession::Impl *> seen;
         std::vector<SequenceRows> seqs;
@@ -250,10 +262,13 @@ struct BatchAccess {
         }
         if (seqs.empty()) return;
         ForwardIo io;
-        io.tokens = tokens_device;
+        io.tokens = first ? tokens_device : nullptr;
+        io.activations = first ? nullptr : activations_device;
         io.inputs_on_device = true;
-        io.tokens_out = tokens_out_device;
+        io.tokens_out = last ? tokens_out_device : nullptr;
         io.tokens_out_on_device = true;
+        io.activations_out = last ? nullptr : activations_out_device;
+        io.activations_out_on_device = true;
         io.synchronize = false;
         e.stage->forward(seqs, io);
         for (std::size_t i = 0; i < sessions.size(); ++i) {
@@ -485,16 +500,33 @@ std::vector<StageResult> decode_stage_batch(NativeEngine & engine, std::span<Nat
 
 namespace detail {
 
+static void require_full_model_device(NativeEngine & engine) {
+    const ModelInfo info = engine.model_info();
+    if (info.resident_layer_start != 0 || info.resident_layer_end != info.layer_count) {
+        throw std::logic_error("full-model native inference requires every model layer");
+    }
+}
+
 void decode_batch_device(NativeEngine & engine, std::span<NativeSession * const> sessions,
                          const std::int32_t * tokens_device, std::int32_t * tokens_out_device) {
-    BatchAccess::run_device(engine, sessions, false, tokens_device, {}, tokens_out_device);
+    require_full_model_device(engine);
+    BatchAccess::run_device(engine, sessions, false, tokens_device, nullptr, {}, tokens_out_device, nullptr);
 }
 
 void prefill_batch_device(NativeEngine & engine, std::span<NativeSession * const> sessions,
                           const std::int32_t * tokens_device, std::span<const std::uint32_t> counts,
                           std::int32_t * tokens_out_device) {
+    require_full_model_device(engine);
     if (counts.size() != sessions.size()) throw std::invalid_argument("one prompt length per session is required");
-    BatchAccess::run_device(engine, sessions, true, tokens_device, counts, tokens_out_device);
+    BatchAccess::run_device(engine, sessions, true, tokens_device, nullptr, counts, tokens_out_device, nullptr);
+}
+
+void stage_batch_device(NativeEngine & engine, std::span<NativeSession * const> sessions, bool prefill,
+                        std::span<const std::uint32_t> counts, const std::int32_t * tokens_device,
+                        const float * activations_device, std::int32_t * tokens_out_device,
+                        float * activations_out_device) {
+    BatchAccess::run_device(engine, sessions, prefill, tokens_device, activations_device, counts, tokens_out_device,
+                            activations_out_device);
 }
 
 void synchronize(NativeEngine & engine) {

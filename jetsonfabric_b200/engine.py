@@ -121,6 +121,7 @@ def lib() -> C.CDLL:
             "jfb_engine_decode_batch_activations": ([_VP, _VP, _SZ, _VP, _VP, _VP, _SZ], Status),
             "jfb_engine_decode_batch_device": ([_VP, _VP, _SZ, _VP, _VP], Status),
             "jfb_engine_prefill_batch_device": ([_VP, _VP, _SZ, _VP, _VP, _VP], Status),
+            "jfb_engine_stage_batch_device": ([_VP, _VP, _SZ, C.c_int, _VP, _VP, _VP, _VP, _VP], Status),
             "jfb_engine_synchronize": ([_VP], Status),
             "jfb_engine_stream": ([_VP], _VP),
             "jfb_engine_last_launch_count": ([_VP], C.c_uint64),
@@ -458,6 +459,18 @@ class NativeEngine:
         check(lib().jfb_engine_decode_batch_device(self._h, handles if handles is not None else self._handles(sessions),
                                                     len(sessions), C.c_void_p(tokens_device_ptr),
                                                     C.c_void_p(tokens_out_device_ptr)))
+
+    def stage_batch_device(self, sessions: Sequence[NativeSession], prefill: bool, counts: Sequence[int] | None = None,
+                           tokens_ptr: int = 0, activations_ptr: int = 0, tokens_out_ptr: int = 0,
+                           activations_out_ptr: int = 0, handles=None) -> None:
+        """One device-resident pass of this engine's stage (jfb_engine_stage_batch_device): the first
+        stage reads token ids, later stages f32 activations; the last stage writes greedy tokens, the
+        others f32 activations. Pointers are device addresses; nothing is synchronised."""
+        c = None if counts is None else np.asarray(counts, dtype=np.uint32)
+        check(lib().jfb_engine_stage_batch_device(
+            self._h, handles if handles is not None else self._handles(sessions), len(sessions), int(prefill),
+            None if c is None else c.ctypes.data, C.c_void_p(tokens_ptr or None), C.c_void_p(activations_ptr or None),
+            C.c_void_p(tokens_out_ptr or None), C.c_void_p(activations_out_ptr or None)))
 
     def synchronize(self) -> None:
         check(lib().jfb_engine_synchronize(self._h))

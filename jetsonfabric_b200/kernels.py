@@ -148,12 +148,12 @@ def argmax(logits, out):
     check(_bind().jfb_argmax(ptr(logits), logits.shape[0], logits.shape[1], ptr(out), stream_ptr()))
 
 
-def codec_f32_to_f16(x, out):
-    check(_bind().jfb_codec_f32_to_f16(ptr(x), ptr(out), x.numel(), stream_ptr()))
+def codec_f32_to_f16(x, out, stream=None):
+    check(_bind().jfb_codec_f32_to_f16(ptr(x), ptr(out), x.numel(), stream_ptr(stream)))
 
 
-def codec_f16_to_f32(x, out):
-    check(_bind().jfb_codec_f16_to_f32(ptr(x), ptr(out), x.numel(), stream_ptr()))
+def codec_f16_to_f32(x, out, stream=None):
+    check(_bind().jfb_codec_f16_to_f32(ptr(x), ptr(out), x.numel(), stream_ptr(stream)))
 
 
 def attention_scratch_bytes(n, heads, head_dim, max_keys) -> int:

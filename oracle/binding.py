@@ -196,7 +196,7 @@ class OracleStage:
             return OrcTensor(t.type, 0, t.shape[0], t.shape[1], t.data)
 
         vocab_src = tensors.get("token_embd.weight") or tensors.get("output.weight")
-        m.vocabulary_size = vocab_src.shape[1]
+        m.vocabulary_size = vocab_src.shape[1] if vocab_src is not None else 0  # a middle stage has neither
         m.token_embd = ot("token_embd.weight")
         m.output_norm = ot("output_norm.weight")
         m.output = ot("output.weight")

@@ -1,0 +1,155 @@
+"""Pipeline-parallel schedule on CPU: gloo ranks, each running the CPU oracle
+over its contiguous layer range, must produce exactly the tokens of one
+process that chains the same stages with the F16 activation codec at every
+boundary (the reference pipeline's Stagewire hop).
+
+This covers the host side of the multi-GPU path, which the benchmark drives
+with the engine over NCCL:
+- the even layer split;
+- micro-batching;
+- message order on the activation and token links (world sizes 2 and 3,
+  more and fewer micro-batches than stages).
+"""
+from __future__ import annotations
+
+import json
+import os
+import socket
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+from jetsonfabric_b200 import pipeline  # noqa: E402
+
+
+def test_stage_ranges_and_batches():
+    assert pipeline.stage_ranges(36, 2) == [(0, 18), (18, 36)]
+    assert pipeline.stage_ranges(36, 8) == [(0, 5), (5, 10), (10, 15), (15, 20), (20, 24), (24, 28), (28, 32),
+                                            (32, 36)]
+    assert pipeline.stage_ranges(4, 3) == [(0, 2), (2, 3), (3, 4)]
+    assert pipeline.split_batches(32, 3) == [list(range(0, 11)), list(range(11, 22)), list(range(22, 32))]
+    with pytest.raises(ValueError):
+        pipeline.stage_ranges(4, 5)
+    with pytest.raises(ValueError):
+        pipeline.split_batches(2, 3)
+
+
+class OracleScheduleStage:
+    """The CPU oracle as a `pipeline.Stage`: host arrays, one oracle session
+    per sequence, boundary payloads as CPU float16 tensors."""
+
+    def __init__(self, stage, prompts, batches, capacity):
+        self.stage, self.prompts, self.batches = stage, prompts, batches
+        self.sessions = [stage.session(capacity) for _ in prompts]
+        self.first, self.last, self.hidden = stage.first, stage.last, stage.hidden
+
+    def prompt_tokens(self, m):
+        return [self.prompts[s] for s in self.batches[m]]
+
+    def empty_tokens(self, count):
+        return torch.empty(count, dtype=torch.int32)
+
+    def empty_payload(self, rows):
+        return torch.empty((rows, self.hidden), dtype=torch.float16)
+
+    def encode(self, activations):
+        return torch.from_numpy(np.ascontiguousarray(activations, dtype=np.float32).astype(np.float16))
+
+    def decode(self, payload):
+        return payload.numpy().astype(np.float32)
+
+    def forward(self, m, prefill, inputs):
+        mb = self.batches[m]
+        outs, row = [], 0
+        for i, s in enumerate(mb):
+            sess = self.sessions[s]
+            if self.first:
+                tokens = list(inputs[i]) if prefill else [int(np.asarray(inputs)[i])]
+                r = sess.forward(prefill, tokens=tokens)
+            else:
+                n = len(self.prompts[s]) if prefill else 1
+                r = sess.forward(prefill, activations=np.asarray(inputs)[row:row + n])
+                row += n
+            outs.append(r)
+        if self.last:
+            return torch.tensor([r["token"] for r in outs], dtype=torch.int32)
+        return np.concatenate([r["activations"] for r in outs], axis=0)
+
+
+def _rank_main(rank, world, port, package, prompts, micro, steps, out_path):
+    import torch.distributed as dist
+    from oracle import binding as ob
+
+    ob.set_threads(1)
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    try:
+        groups = pipeline.make_groups(world)
+        pipeline.warm_groups(rank, world, groups)
+        link = pipeline.TorchLink(rank, world, groups)
+        meta = ob.OracleStage(package)
+        layers = meta.model.layer_count
+        meta.close()
+        start, end = pipeline.stage_ranges(layers, world)[rank]
+        stage = ob.OracleStage(package, start, end)
+        batches = pipeline.split_batches(len(prompts), micro)
+        capacity = max(len(p) for p in prompts) + steps
+        sched = OracleScheduleStage(stage, prompts, batches, capacity)
+        res = pipeline.run_schedule(rank, world, batches, [len(p) for p in prompts], steps, sched, link)
+        if rank == world - 1:
+            with open(out_path, "w") as f:
+                json.dump({str(k): v for k, v in pipeline.collect_tokens(res).items()}, f)
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _chained_reference(package, prompts, world, steps):
+    """One process: stage 0 -> F16 codec -> stage 1 -> ... per sequence."""
+    from oracle import binding as ob
+
+    meta = ob.OracleStage(package)
+    layers = meta.model.layer_count
+    meta.close()
+    stages = [ob.OracleStage(package, a, b) for a, b in pipeline.stage_ranges(layers, world)]
+    capacity = max(len(p) for p in prompts) + steps
+    out = {}
+    for s, prompt in enumerate(prompts):
+        sessions = [st.session(capacity) for st in stages]
+        tokens, feed = [], list(prompt)
+        for step in range(steps):
+            prefill = step == 0
+            x = None
+            for k, sess in enumerate(sessions):
+                r = sess.forward(prefill, tokens=feed) if k == 0 else sess.forward(prefill, activations=x)
+                if k + 1 < len(sessions):
+                    x = r["activations"].astype(np.float16).astype(np.float32)
+                else:
+                    tokens.append(r["token"])
+            feed = [tokens[-1]]
+        out[s] = tokens
+    return out
+
+
+@pytest.mark.parametrize("world,micro", [(2, 2), (2, 3), (3, 2)])
+def test_pipeline_matches_chained_stages(small_q4k_package, tmp_path, world, micro):
+    import torch.multiprocessing as mp
+
+    rng = np.random.default_rng(world * 10 + micro)
+    prompts = [rng.integers(0, 1024, n).tolist() for n in (7, 3, 12, 5, 9)]
+    steps = 6
+    out_path = tmp_path / "tokens.json"
+    os.environ.setdefault("OMP_NUM_THREADS", "1")
+    mp.spawn(_rank_main, args=(world, _free_port(), str(small_q4k_package), prompts, micro, steps, str(out_path)),
+             nprocs=world, join=True)
+    got = {int(k): v for k, v in json.loads(out_path.read_text()).items()}
+    ref = _chained_reference(small_q4k_package, prompts, world, steps)
+    assert got == ref
+    assert all(len(v) == steps for v in got.values())
