@@ -34,10 +34,10 @@
 // all contributors' partials in CTA order, so the result does not depend on
 // timing and no CTA ever waits for another.
 //
-// Warp roles (14 warps, 448 threads):
-//   warps 0-3   epilogue: warp w owns TMEM lanes 32w..32w+31 (weight rows)
-//               and all 32 token columns;
-//   warps 4-11  converters: per stage (half a block, 128 K values) thread
+// Warp roles (18 warps, 576 threads):
+//   warps 0-7   epilogue: warp w owns TMEM lanes 32(w % 4)..+31 (weight rows)
+//               and token columns 16(w / 4)..+15;
+//   warps 8-15  converters: per stage (half a block, 128 K values) thread
 //               (m, part) turns 64 raw values of weight row m into f16
 //               products and writes them to tensor memory (tcgen05.st): the A
 //               operand lives in TMEM (lane = weight row, each 32-bit column
@@ -48,8 +48,8 @@
 //               K-major layout (core matrices of 8 rows x 16 bytes; LBO = 128 B
 //               between the two K-halves of one 16-wide MMA step, SBO between
 //               8-row groups);
-//   warp 12     TMEM allocation and the single-thread tcgen05.mma issue;
-//   warp 13     one thread issuing the 2D TMA loads (cp.async.bulk.tensor, no
+//   warp 16     TMEM allocation and the single-thread tcgen05.mma issue;
+//   warp 17     one thread issuing the 2D TMA loads (cp.async.bulk.tensor, no
 //               multicast) of the raw weight rows, activation codes and
 //               partial sums into a ring of raw stages, several stages ahead
 //               of the converters, completing on mbarrier transaction counts.
@@ -73,12 +73,12 @@
 namespace jfb {
 namespace {
 
-constexpr int kThreads = 448;
-constexpr int kEpilogueThreads = 128;  // warps 0-3
-constexpr int kEpilogueWarps = 4;
-constexpr int kConverterThreads = 256;  // warps 4-11
-constexpr int kMmaWarp = 12;
-constexpr int kTmaWarp = 13;
+constexpr int kThreads = 576;
+constexpr int kEpilogueThreads = 256;   // warps 0-7
+constexpr int kEpilogueWarps = 8;
+constexpr int kConverterThreads = 256;  // warps 8-15
+constexpr int kMmaWarp = 16;
+constexpr int kTmaWarp = 17;
 constexpr int kRows = 128;             // MMA M: weight rows per tile
 constexpr int kBN = 32;                // MMA N: activation rows per tile
 constexpr int kKStage = 128;           // K values per pipeline stage
@@ -410,6 +410,28 @@ __device__ __forceinline__ uint32_t cta_of(uint64_t unit, uint64_t work, uint64_
     return uint32_t(((unit + 1) * g - 1) / work);
 }
 
+// Position of a work unit: tile = tn * tiles_m + tm, K block b. Advanced one
+// unit at a time so that no role divides per unit.
+struct Cursor {
+    uint32_t tile, b, tm, tn;
+    __device__ __forceinline__ void init(uint64_t w, uint32_t nb, uint32_t tiles_m) {
+        tile = uint32_t(w / nb);
+        b = uint32_t(w - uint64_t(tile) * nb);
+        tn = tile / tiles_m;
+        tm = tile - tn * tiles_m;
+    }
+    __device__ __forceinline__ void next(uint32_t nb, uint32_t tiles_m) {
+        if (++b == nb) {
+            b = 0;
+            ++tile;
+            if (++tm == tiles_m) {
+                tm = 0;
+                ++tn;
+            }
+        }
+    }
+};
+
 // f16 pair (v, v) of a small integer v with v + BIAS in [0, 1024), without a
 // conversion instruction: 0x6400 | u is the f16 number 1024 + u, and
 // subtracting 1024 + BIAS is exact.
@@ -419,30 +441,41 @@ __device__ __forceinline__ __half2 small_h2(int v) {
     return __hsub2(bits_h2(u * 0x00010001u), h2_int_const<1024 + BIAS>());
 }
 
-// Converts values [64*PART, 64*PART + 64) of raw half-block H of tile row m
+// The scale-byte word of 16-value groups [8h + 4part, 8h + 4part + 4) of a
+// block: bytes 0..3 of the result are the scales of those four groups.
+__device__ __forceinline__ uint32_t scale_word(const uint4 & scv, int h, int part) {
+    const int w = 2 * h + part;
+    return w == 0 ? scv.x : w == 1 ? scv.y : w == 2 ? scv.z : scv.w;
+}
+
+// Converts values [64*part, 64*part + 64) of raw half-block h of tile row m
 // (raw stage `r`) into f16 products and stores them into this thread's TMEM
 // lane of the stage's A operand (`a_col`: address of plane 0, column 0; plane
 // 1 follows 64 columns later). Value k of the half goes to column k / 2, two
-// values per 32-bit column. H and PART are compile-time so every byte, nibble
-// and register index below is a constant. Warp-collective (tcgen05.st).
-template <uint32_t TYPE, int H, int PART>
-__device__ __forceinline__ void convert_a(const uint8_t * r, uint32_t a_col, int m) {
+// values per 32-bit column. h and part only move byte offsets and shift
+// amounts, so every register-array index below is a compile-time constant and
+// one body serves all four (h, part) cases. Warp-collective (tcgen05.st).
+template <uint32_t TYPE>
+__device__ __forceinline__ void convert_a(const uint8_t * r, int h, int part, uint32_t a_col, int m) {
     using RL = RawLayout<TYPE>;
     const uint4 scv = *reinterpret_cast<const uint4 *>(r + RL::kScOff + m * 16);
-    const uint32_t col = a_col + 32 * PART;
+    const uint32_t col = a_col + 32 * part;
     if constexpr (TYPE == JF_TENSOR_Q4_K) {
-        // raw row: code bytes [64H, 64H + 64) of the block; byte 32c' + l holds
+        // raw row: code bytes [64h, 64h + 64) of the block; byte 32c' + l holds
         // element 64c' + l (low nibble) and 64c' + 32 + l (high nibble) of the
-        // half; this thread covers c' = PART, i.e. sub-blocks 2c and 2c + 1
-        // of the block with c = 2H + PART.
-        constexpr int c = 2 * H + PART;
-        const uint4 * codes = reinterpret_cast<const uint4 *>(r + RL::kW0Off + m * 64 + 32 * PART);
+        // half; this thread covers c' = part, i.e. sub-blocks j = 4h + 2part
+        // and j + 1 of the block. The packed 6-bit scale/min of sub-block j:
+        // j < 4 (h = 0): low 6 bits of bytes j and j + 4 of the 12; j >= 4
+        // (h = 1): nibbles of byte j + 4 with the top 2 bits of bytes j - 4
+        // and j.
+        const uint4 * codes = reinterpret_cast<const uint4 *>(r + RL::kW0Off + m * 64 + 32 * part);
         const uint4 v0 = codes[0], v1 = codes[1];
         const uint32_t wv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
 #pragma unroll
         for (int nib = 0; nib < 2; ++nib) {
-            int sc, mn;
-            q4k_scale_min_hdr(scv, 2 * c + nib, sc, mn);
+            const int sh = 8 * (2 * part + nib);  // byte jj = j mod 4 of each 4-byte scale word
+            const uint32_t b1 = scv.y >> sh, b2 = scv.z >> sh, b3 = scv.w >> sh;
+            const int sc = h == 0 ? int(b1 & 63) : int((b3 & 0x0f) | (((b1 >> 6) & 3) << 4));
             const __half2 scale = small_h2<0>(sc);
             const __half2 nbias = __hmul2(scale, h2_int_const<-1024>());
             uint32_t w[16];
@@ -455,13 +488,15 @@ __device__ __forceinline__ void convert_a(const uint8_t * r, uint32_t a_col, int
                 w[4 * q + 2] = b.x;
                 w[4 * q + 3] = b.y;
             }
+            (void) b2;
             tmem_st16(col + 16 * nib, w);  // values [32*nib, 32*nib + 32) of this thread
         }
     } else if constexpr (TYPE == JF_TENSOR_Q6_K) {
-        // raw rows: ql bytes [64H, 64H + 64) and qh bytes [32H, 32H + 32) of
+        // raw rows: ql bytes [64h, 64h + 64) and qh bytes [32h, 32h + 32) of
         // the block. Element r' (0..127) of the half is nibble r' / 64 of
         // ql[r' % 64] with bits 2*(r' / 32) of qh[r' % 32]; this thread covers
-        // r' in [64*PART, 64*PART + 64): nibble PART of every ql byte.
+        // r' in [64*part, 64*part + 64): nibble `part` of every ql byte and
+        // bit pairs 2*part, 2*part + 1 of the qh bytes.
         const uint4 * ql = reinterpret_cast<const uint4 *>(r + RL::kW0Off + m * 64);
         const uint4 * qh = reinterpret_cast<const uint4 *>(r + RL::kW1Off + m * 32);
         const uint4 l0 = ql[0], l1 = ql[1], l2 = ql[2], l3 = ql[3];
@@ -469,6 +504,8 @@ __device__ __forceinline__ void convert_a(const uint8_t * r, uint32_t a_col, int
         const uint32_t L[16] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w,
                                 l2.x, l2.y, l2.z, l2.w, l3.x, l3.y, l3.z, l3.w};
         const uint32_t Hq[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+        const uint32_t sw = scale_word(scv, h, part);
+        const int lsh = 4 * part, hsh = 4 * part;
         const __half2 k1056 = h2_int_const<-1056>();  // 1056 = 1024 + 32
 #pragma unroll
         for (int gp = 0; gp < 2; ++gp) {  // 32 values (two scale groups) per pass
@@ -476,7 +513,7 @@ __device__ __forceinline__ void convert_a(const uint8_t * r, uint32_t a_col, int
 #pragma unroll
             for (int g2 = 0; g2 < 2; ++g2) {
                 const int grp = 2 * gp + g2;
-                const int s = int(int8_t(byte_at(scv, 8 * H + 4 * PART + grp)));
+                const int s = int(int8_t(uint8_t(sw >> (8 * grp))));
                 const int s_lo = s & 15, s_hi = (s - s_lo) / 16;
                 const __half2 shi = small_h2<8>(s_hi), nhi = __hmul2(shi, k1056);
                 const __half2 slo = small_h2<0>(s_lo), nlo = __hmul2(slo, k1056);
@@ -486,9 +523,9 @@ __device__ __forceinline__ void convert_a(const uint8_t * r, uint32_t a_col, int
                     uint32_t q[2];
 #pragma unroll
                     for (int k = 0; k < 2; ++k) {
-                        const int rr = 64 * PART + 8 * ch + 4 * k;
-                        q[k] = ((L[(rr % 64) / 4] >> (4 * (rr / 64))) & 0x0f0f0f0fu) |
-                               (((Hq[(rr % 32) / 4] >> (2 * (rr / 32))) & 0x03030303u) << 4);
+                        const int rr = 8 * ch + 4 * k;  // within the thread's 64 values
+                        q[k] = ((L[rr / 4] >> lsh) & 0x0f0f0f0fu) |
+                               (((Hq[(rr % 32) / 4] >> (hsh + 2 * (rr / 32))) & 0x03030303u) << 4);
                     }
                     const __half2 x0 = magic_pair(q[0], 0x4140u), x1 = magic_pair(q[0], 0x4342u);
                     const __half2 x2 = magic_pair(q[1], 0x4140u), x3 = magic_pair(q[1], 0x4342u);
@@ -507,25 +544,26 @@ __device__ __forceinline__ void convert_a(const uint8_t * r, uint32_t a_col, int
             tmem_st16(col + 64 + 16 * gp, wlo);
         }
     } else {
-        // raw row: qs bytes [32H, 32H + 32); element 32s + l of the half lives
-        // in bits 2s of byte l
+        // raw row: qs bytes [32h, 32h + 32); element 32s + l of the half lives
+        // in bits 2s of byte l; this thread covers s = 2*part, 2*part + 1
         const uint4 * qs = reinterpret_cast<const uint4 *>(r + RL::kW0Off + m * 32);
         const uint4 a0 = qs[0], a1 = qs[1];
         const uint32_t Q[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+        const uint32_t sw = scale_word(scv, h, part);
 #pragma unroll
         for (int gp = 0; gp < 2; ++gp) {
             uint32_t w[16];
 #pragma unroll
             for (int g2 = 0; g2 < 2; ++g2) {
                 const int grp = 2 * gp + g2;
-                const __half2 scale = small_h2<0>(int(byte_at(scv, 8 * H + 4 * PART + grp) & 15));
+                const __half2 scale = small_h2<0>(int((sw >> (8 * grp)) & 15));
                 const __half2 nbias = __hmul2(scale, h2_int_const<-1024>());
 #pragma unroll
                 for (int half_grp = 0; half_grp < 2; ++half_grp) {
-                    const int r0 = 64 * PART + 16 * grp + 8 * half_grp;
-                    const int sh = r0 / 32, l0 = r0 % 32;
-                    const uint2 x = scaled4((Q[l0 / 4] >> (2 * sh)) & 0x03030303u, scale, nbias);
-                    const uint2 y = scaled4((Q[l0 / 4 + 1] >> (2 * sh)) & 0x03030303u, scale, nbias);
+                    const int r0 = 16 * grp + 8 * half_grp;  // within the thread's 64 values
+                    const int shift = 2 * (2 * part + r0 / 32), l0 = r0 % 32;
+                    const uint2 x = scaled4((Q[l0 / 4] >> shift) & 0x03030303u, scale, nbias);
+                    const uint2 y = scaled4((Q[l0 / 4 + 1] >> shift) & 0x03030303u, scale, nbias);
                     const int o = 4 * (2 * g2 + half_grp);
                     w[o + 0] = x.x;
                     w[o + 1] = x.y;
@@ -538,41 +576,34 @@ __device__ __forceinline__ void convert_a(const uint8_t * r, uint32_t a_col, int
     }
 }
 
-template <uint32_t TYPE>
-__device__ __forceinline__ void convert_a_dispatch(const uint8_t * r, int h, int part, uint32_t a_col, int m) {
-    if (h == 0) {
-        if (part == 0) convert_a<TYPE, 0, 0>(r, a_col, m);
-        else convert_a<TYPE, 0, 1>(r, a_col, m);
-    } else {
-        if (part == 0) convert_a<TYPE, 1, 0>(r, a_col, m);
-        else convert_a<TYPE, 1, 1>(r, a_col, m);
-    }
-}
-
-// Mins of 16-value groups [8*PART, 8*PART + 8) of one block as half of a
+// Mins of 16-value groups [8*part, 8*part + 8) of one block as half of a
 // K = 16 f16 operand row (Q4_K: the 6-bit min of each 32-value sub-block,
 // twice; Q2_K: the high nibble of each scale byte), from the raw scale row of
 // tile row m. The two parts of a row write the two 16-byte core columns.
-template <uint32_t TYPE, int PART>
-__device__ __forceinline__ void convert_mins(const uint8_t * r, uint8_t * tile, int m) {
+template <uint32_t TYPE>
+__device__ __forceinline__ void convert_mins(const uint8_t * r, int part, uint8_t * tile, int m) {
     const uint4 meta = *reinterpret_cast<const uint4 *>(r + RawLayout<TYPE>::kScOff + m * 16);
     uint32_t h2[4];
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-        const int g = 8 * PART + 2 * k;
         int m0, m1;
         if constexpr (TYPE == JF_TENSOR_Q4_K) {
-            int sc;
-            q4k_scale_min_hdr(meta, g / 2, sc, m0);
+            // sub-block j = 4*part + k: j < 4 -> low 6 bits of byte j + 4 of the
+            // 12; j >= 4 -> high nibble of byte j + 4 with the top 2 bits of byte j
+            const int sh = 8 * k;
+            const uint32_t b1 = meta.y >> sh, b2 = meta.z >> sh, b3 = meta.w >> sh;
+            m0 = part == 0 ? int(b2 & 63) : int(((b3 >> 4) & 0x0f) | (((b2 >> 6) & 3) << 4));
+            (void) b1;
             m1 = m0;
         } else {
-            m0 = int(byte_at(meta, g) >> 4);
-            m1 = int(byte_at(meta, g + 1) >> 4);
+            const uint32_t word = part == 0 ? (k < 2 ? meta.x : meta.y) : (k < 2 ? meta.z : meta.w);
+            m0 = int((word >> (16 * (k & 1) + 4)) & 15);
+            m1 = int((word >> (16 * (k & 1) + 12)) & 15);
         }
         const uint32_t u = (uint32_t(m0) | 0x6400u) | ((uint32_t(m1) | 0x6400u) << 16);  // mins < 64
         h2[k] = h2_bits(__hsub2(bits_h2(u), h2_int_const<1024>()));
     }
-    *reinterpret_cast<uint4 *>(tile + (m >> 3) * kSbo16 + PART * 128 + (m & 7) * 16) = make_uint4(h2[0], h2[1], h2[2], h2[3]);
+    *reinterpret_cast<uint4 *>(tile + (m >> 3) * kSbo16 + part * 128 + (m & 7) * 16) = make_uint4(h2[0], h2[1], h2[2], h2[3]);
 }
 
 template <uint32_t TYPE>
@@ -641,9 +672,11 @@ __global__ void __launch_bounds__(kThreads, 1) mmq_tc_kernel(const __grid_consta
             uint32_t rs = 0, rph = 0;
             uint64_t issued = 0;
             bool ok = true;
-            for (uint64_t w = w_begin; w < w_end && ok && !*abort_flag; ++w) {
-                const uint32_t tile = uint32_t(w / nb), b = uint32_t(w % nb);
-                const int32_t y_w = int32_t((tile % p.tiles_m) * kRows), y_a = int32_t((tile / p.tiles_m) * kBN);
+            Cursor cur;
+            cur.init(w_begin, nb, p.tiles_m);
+            for (uint64_t w = w_begin; w < w_end && ok && !*abort_flag; ++w, cur.next(nb, p.tiles_m)) {
+                const uint32_t b = cur.b;
+                const int32_t y_w = int32_t(cur.tm * kRows), y_a = int32_t(cur.tn * kBN);
                 for (int h = 0; h < 2; ++h) {
                     if (!mbar_wait(&raw_empty[rs], rph ^ 1u, abort_flag, p.error, kErrWaitRawEmpty)) {
                         ok = false;
@@ -698,11 +731,8 @@ __global__ void __launch_bounds__(kThreads, 1) mmq_tc_kernel(const __grid_consta
                 tc_fence_after();
                 const uint8_t * r = raw + rs * RL::kBytes;
                 uint8_t * st = smem + stage * kStage;
-                convert_a_dispatch<TYPE>(r, h, part, tmem + lane_base + kAccCols + stage * kACols, m);
-                if (T::kMins && h == 0) {
-                    if (part == 0) convert_mins<TYPE, 0>(r, st + kA2Off, m);
-                    else convert_mins<TYPE, 1>(r, st + kA2Off, m);
-                }
+                convert_a<TYPE>(r, h, part, tmem + lane_base + kAccCols + stage * kACols, m);
+                if (T::kMins && h == 0) convert_mins<TYPE>(r, part, st + kA2Off, m);
                 // activation codes: one token t and 16 codes (chunk pair c16) per
                 // thread. The raw tile arrives 128-byte swizzled (16-byte chunk c
                 // of token row t at chunk c ^ (t & 7)), so the 8 lanes that share
@@ -800,19 +830,23 @@ __global__ void __launch_bounds__(kThreads, 1) mmq_tc_kernel(const __grid_consta
         __syncwarp();
     } else {
         // ---------------- epilogue (warps 0-3) ----------------
-        const int m = warp * 32 + lane;
-        const uint32_t lane_base = uint32_t(warp * 32) << 16;
+        constexpr int kCols = kBN / 2;  // token columns of this thread
+        const int m = (warp & 3) * 32 + lane;  // TMEM lane quarter of the warp = its 32 weight rows
+        const int col0 = (warp >> 2) * kCols;
+        const uint32_t lane_base = uint32_t((warp & 3) * 32) << 16;
         // scale rings of this warp: [kScaleRing][32] weight scale words (own row), [kScaleRing][32] activation d
         uint32_t * dring = reinterpret_cast<uint32_t *>(scales) + warp * kScaleRing * 64;
         float * aring = reinterpret_cast<float *>(dring + kScaleRing * 32);
         const uint8_t * p1 = static_cast<const uint8_t *>(p.w.plane[1]);
         const uint8_t * p2 = static_cast<const uint8_t *>(p.w.plane[2]);
         const uint32_t first_tile = uint32_t(w_begin / nb);
-        // stage unit w's scales into ring slot `slot` (one commit group per unit, possibly empty)
+        Cursor ahead;  // the unit whose scales are staged next
+        ahead.init(w_begin, nb, p.tiles_m);
+        // stage unit w (at cursor `ahead`) into ring slot `slot` (one commit group per unit, possibly empty)
         auto stage_scales = [&](uint64_t w, int slot) {
             if (w < w_end) {
-                const uint32_t tile = uint32_t(w / nb), b = uint32_t(w % nb);
-                const uint32_t row = (tile % p.tiles_m) * kRows + uint32_t(m), tok = (tile / p.tiles_m) * kBN + lane;
+                const uint32_t b = ahead.b;
+                const uint32_t row = ahead.tm * kRows + uint32_t(m), tok = ahead.tn * kBN + lane;
                 if (row < p.w.rows) {
                     const uint64_t block = uint64_t(row) * nb + b;
                     const uint8_t * src = TYPE == JF_TENSOR_Q4_K ? p1 + block * 16        // d | dmin << 16
@@ -824,23 +858,25 @@ __global__ void __launch_bounds__(kThreads, 1) mmq_tc_kernel(const __grid_consta
                 }
                 if (tok < p.n) cp_async4(&aring[slot * 32 + lane], p.da + uint64_t(tok) * nb + b);
                 else aring[slot * 32 + lane] = 0.0f;
+                ahead.next(nb, p.tiles_m);
             }
             cp_async_commit();
         };
 #pragma unroll
         for (int k = 0; k < kScaleRing; ++k) stage_scales(w_begin + k, k);
-        double sum[kBN];
+        double sum[kCols];
         uint64_t seg_begin = w_begin;
         uint32_t i = 0;
-        for (uint64_t w = w_begin; w < w_end; ++w, ++i) {
+        Cursor cur;
+        cur.init(w_begin, nb, p.tiles_m);
+        for (uint64_t w = w_begin; w < w_end; ++w, ++i, cur.next(nb, p.tiles_m)) {
             // warp-uniform stop: the warp collectives below need every lane
             if (__any_sync(0xffffffffu, *abort_flag != 0)) break;
-            const uint32_t tile = uint32_t(w / nb);
-            const uint32_t tm = tile % p.tiles_m, tn = tile / p.tiles_m;
-            const uint32_t row = tm * kRows + uint32_t(m), tok0 = tn * kBN;
+            const uint32_t tile = cur.tile;
+            const uint32_t row = cur.tm * kRows + uint32_t(m), tok0 = cur.tn * kBN;
             if (w == seg_begin) {
 #pragma unroll
-                for (int t = 0; t < kBN; ++t) sum[t] = 0.0;
+                for (int t = 0; t < kCols; ++t) sum[t] = 0.0;
             }
             const int slot = int(i % kScaleRing);
             cp_async_wait<kScaleRing - 1>();  // unit i's group is complete
@@ -849,8 +885,8 @@ __global__ void __launch_bounds__(kThreads, 1) mmq_tc_kernel(const __grid_consta
             {
                 const uint32_t word = dring[slot * 32 + lane];
                 if constexpr (TYPE == JF_TENSOR_Q6_K) {
-                    const uint64_t block = uint64_t(row) * nb + uint32_t(w % nb);
-                    dw = half_bits_to_float(uint16_t((block & 1) ? word >> 16 : word & 0xffffu));
+                    const uint32_t odd = ((row & nb) + cur.b) & 1u;  // parity of block row * nb + b
+                    dw = half_bits_to_float(uint16_t(odd ? word >> 16 : word & 0xffffu));
                 } else {
                     dw = half_bits_to_float(uint16_t(word & 0xffffu));
                     dmin = half_bits_to_float(uint16_t(word >> 16));
@@ -863,20 +899,20 @@ __global__ void __launch_bounds__(kThreads, 1) mmq_tc_kernel(const __grid_consta
             const bool ready = mbar_wait(&acc_full[acc], use & 1u, abort_flag, p.error, kErrWaitAccFull);
             if (!__all_sync(0xffffffffu, ready)) break;
             tc_fence_after();
-            const uint32_t base = tmem + lane_base + acc * (T::kAcc * kBN);
+            const uint32_t base = tmem + lane_base + acc * (T::kAcc * kBN) + col0;
 #pragma unroll
-            for (int ch = 0; ch < kBN / 8; ++ch) {
+            for (int ch = 0; ch < kCols / 8; ++ch) {
                 uint32_t r0[8], r1[8], r2[8];
                 tmem_ld8(base + 8 * ch, r0);
                 tmem_ld8(base + kBN + 8 * ch, r1);
                 if constexpr (T::kAcc == 3) tmem_ld8(base + 2 * kBN + 8 * ch, r2);
                 tmem_wait_ld();
-                if (ch == kBN / 8 - 1) {
+                if (ch == kCols / 8 - 1) {
                     tc_fence_before();
                     mbar_arrive(&acc_empty[acc]);  // the accumulators may be overwritten now
                 }
-                const float4 da0 = *reinterpret_cast<const float4 *>(da_s + 8 * ch);
-                const float4 da1 = *reinterpret_cast<const float4 *>(da_s + 8 * ch + 4);
+                const float4 da0 = *reinterpret_cast<const float4 *>(da_s + col0 + 8 * ch);
+                const float4 da1 = *reinterpret_cast<const float4 *>(da_s + col0 + 8 * ch + 4);
                 const float das[8] = {da0.x, da0.y, da0.z, da0.w, da1.x, da1.y, da1.z, da1.w};
 #pragma unroll
                 for (int k = 0; k < 8; ++k) {
@@ -900,14 +936,14 @@ __global__ void __launch_bounds__(kThreads, 1) mmq_tc_kernel(const __grid_consta
             stage_scales(w + kScaleRing, slot);
 
             // a segment ends where the CTA's range or the tile's K range ends
-            if (w + 1 != w_end && (w + 1) % nb != 0) continue;
+            if (w + 1 != w_end && cur.b + 1 != nb) continue;
             const bool complete = seg_begin == uint64_t(tile) * nb && w + 1 == uint64_t(tile + 1) * nb;
             seg_begin = w + 1;
             if (!complete) {
                 const uint32_t slot_p = 2 * blockIdx.x + (tile == first_tile ? 0 : 1);
                 double * part = p.partial + uint64_t(slot_p) * kSlotDoubles;
 #pragma unroll
-                for (int t = 0; t < kBN; ++t) part[t * kRows + m] = sum[t];
+                for (int t = 0; t < kCols; ++t) part[(col0 + t) * kRows + m] = sum[t];
                 __threadfence();
                 __syncwarp();
                 const uint32_t lo = cta_of(uint64_t(tile) * nb, p.work, g);
@@ -921,20 +957,36 @@ __global__ void __launch_bounds__(kThreads, 1) mmq_tc_kernel(const __grid_consta
                 arrived = __shfl_sync(0xffffffffu, arrived, 0);
                 if (arrived != hi - lo + 1) continue;
                 __threadfence();
+                // contributors after `lo` start inside this tile, so it is their
+                // first tile (slot 2c); `lo` used slot 2lo + 1 unless its range
+                // starts exactly at the tile. Partials are added in CTA order,
+                // eight tokens at a time, with the loads of several
+                // contributors in flight together.
+                const uint64_t lo_slot = 2 * uint64_t(lo) + (range_start(lo, p.work, g) == uint64_t(tile) * nb ? 0 : 1);
+                const double * lo_src = p.partial + lo_slot * kSlotDoubles + col0 * kRows + m;
+                const double * rest = p.partial + 2 * uint64_t(lo + 1) * kSlotDoubles + col0 * kRows + m;
 #pragma unroll
-                for (int t = 0; t < kBN; ++t) sum[t] = 0.0;
-                for (uint32_t c = lo; c <= hi; ++c) {
-                    const uint32_t c_first = uint32_t(range_start(c, p.work, g) / nb);
-                    const uint64_t s = 2 * uint64_t(c) + (tile == c_first ? 0 : 1);
-                    const double * src = p.partial + s * kSlotDoubles;
+                for (int t0 = 0; t0 < kCols; t0 += 8) {
+                    double acc8[8];
 #pragma unroll
-                    for (int t = 0; t < kBN; ++t) sum[t] += __ldcg(src + t * kRows + m);
+                    for (int k = 0; k < 8; ++k) acc8[k] = 0.0 + __ldcg(lo_src + (t0 + k) * kRows);
+#pragma unroll 4
+                    for (uint32_t c = 0; c < hi - lo; ++c) {
+                        const double * src = rest + uint64_t(2 * c) * kSlotDoubles;
+                        double v[8];
+#pragma unroll
+                        for (int k = 0; k < 8; ++k) v[k] = __ldcg(src + (t0 + k) * kRows);
+#pragma unroll
+                        for (int k = 0; k < 8; ++k) acc8[k] += v[k];
+                    }
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) sum[t0 + k] = acc8[k];
                 }
             }
             if (row < p.w.rows) {
 #pragma unroll
-                for (int t = 0; t < kBN; ++t) {
-                    const uint32_t tok = tok0 + t;
+                for (int t = 0; t < kCols; ++t) {
+                    const uint32_t tok = tok0 + col0 + t;
                     if (tok >= p.n) break;
                     const uint64_t at = uint64_t(tok) * p.w.rows + row;
                     float v = __double2float_rn(sum[t]);
@@ -1067,9 +1119,21 @@ jfb_status launch(TcParams & p, uint32_t cols, uint32_t grid, cudaStream_t s) {
     jfb_status st = build_maps<TYPE>(maps, p, cols);
     if (st.code != JFB_STATUS_OK) return st;
     auto kernel = mmq_tc_kernel<TYPE>;
-    const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(bytes));
-    if (e != cudaSuccess) {
-        return status_error(JFB_STATUS_CUDA_ERROR, "jfb_matmul_tc: shared memory attribute: %s", cudaGetErrorString(e));
+    // the shared-memory opt-in is a per-device function attribute: set once
+    static std::mutex mu;
+    static bool attribute_set[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        if (!attribute_set[dev]) {
+            const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(bytes));
+            if (e != cudaSuccess) {
+                return status_error(JFB_STATUS_CUDA_ERROR, "jfb_matmul_tc: shared memory attribute: %s",
+                                    cudaGetErrorString(e));
+            }
+            attribute_set[dev] = true;
+        }
     }
     kernel<<<grid, kThreads, bytes, s>>>(maps, p);
     return launch_status("jfb_matmul_tc");
