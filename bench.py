@@ -58,6 +58,9 @@ PRESETS = {
                vocabulary_size=152064),
 }
 METRIC = "aggregate decode tok/s + p50 ITL, Qwen2 Q4_K pipeline at 1/2/4/8 B200"
+# weight shapes of the 3B workload (type, rows, cols) for --matmul-shape
+MATMUL_SHAPES = {"ffn_gate": (11, 11008, 2048), "ffn_down_q6": (13, 2048, 11008), "attn_q": (11, 2048, 2048),
+                 "attn_k": (11, 256, 2048), "output_q6": (13, 151936, 2048)}
 UNIT = "tok/s"
 
 
@@ -77,6 +80,9 @@ def parse():
     p.add_argument("--skip-cpu", action="store_true")
     p.add_argument("--micro-batches", type=int, default=0, help="pipeline micro-batches (default: one per stage)")
     p.add_argument("--replicas", action="store_true", help="N > 1: full-model replicas instead of a pipeline")
+    p.add_argument("--matmul-shape", choices=sorted(MATMUL_SHAPES), default=None,
+                   help="time only the tcgen05 K-quant matmul on one weight shape of the workload (profiling target)")
+    p.add_argument("--matmul-rows", type=int, default=32, help="activation rows for --matmul-shape")
     return p.parse_args()
 
 
@@ -468,6 +474,40 @@ def run_pipeline(args, rank: int, world: int, local_rank: int) -> dict | None:
     return result
 
 
+def run_matmul_shape(args) -> dict:
+    """The tcgen05 matmul alone on one weight shape: enough weight copies to
+    exceed L2, `warmup` untimed then `steps` timed launches (CUDA events on
+    the launching stream)."""
+    import numpy as np
+    import torch
+    from jetsonfabric_b200 import jfm
+    from jetsonfabric_b200 import kernels as K
+
+    t, rows, cols = MATMUL_SHAPES[args.matmul_shape]
+    n = args.matmul_rows
+    raw = jfm.quantize_blocks(t, np.random.default_rng(args.seed).normal(0, 0.02, rows * cols).astype(np.float32))
+    copies = max(1, int(np.ceil(256e6 / len(raw))))
+    weights = [K.DeviceWeight(t, rows, cols, raw) for _ in range(copies)]
+    q8 = K.Q8Buffer(n, cols)
+    K.quantize_q8k(torch.randn(n, cols, device="cuda"), q8)
+    out = torch.empty(n, rows, device="cuda")
+    ws = torch.zeros(K.matmul_tc_workspace_bytes(rows, cols, n), dtype=torch.uint8, device="cuda")
+    for i in range(max(args.warmup, 0)):
+        K.matmul_tc(weights[i % copies], n, out, q8, ws)
+    torch.cuda.synchronize()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2 * args.steps)]
+    for i in range(args.steps):
+        ev[2 * i].record()
+        K.matmul_tc(weights[i % copies], n, out, q8, ws)
+        ev[2 * i + 1].record()
+    torch.cuda.synchronize()
+    us = sorted(ev[2 * i].elapsed_time(ev[2 * i + 1]) * 1000 for i in range(args.steps))
+    med = us[len(us) // 2]
+    return {"kernel": "jfb_matmul_tc", "shape": args.matmul_shape, "type": t, "rows": rows, "cols": cols, "n": n,
+            "weight_bytes": len(raw), "launches": args.steps, "median_us": round(med, 2),
+            "gbs": round(len(raw) / (med * 1e-6) / 1e9, 1), "l2": f"{copies} weight copies rotated"}
+
+
 def traffic_from_profiles():
     path = REPO / "profiles" / "decode_matmul_traffic.json"
     if path.exists():
@@ -554,7 +594,9 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
-    if args.impl == "reference":
+    if args.matmul_shape is not None:
+        result = run_matmul_shape(args)
+    elif args.impl == "reference":
         result = run_reference(args, rank)
     elif world > 1 and not args.replicas:
         result = run_pipeline(args, rank, world, local_rank)

@@ -167,4 +167,57 @@ __device__ __forceinline__ void q8k_block_256(float x, int8_t * qs, float * d, i
     __syncthreads();  // shared_keys / winner_value reuse safety
 }
 
+// The same Q8_K quantization of one 256-value block by one warp: lane l holds
+// elements 8l..8l+7 in v[]. Identical arithmetic to q8k_block_256 (the amax
+// key picks the signed value of largest magnitude, first on ties), with
+// shuffles only, so any number of warps of a CTA quantize blocks
+// independently. qs must be 8-byte aligned.
+struct Vals8 {
+    float v[8];
+};
+
+__device__ __forceinline__ void q8k_block_warp(const Vals8 vals, int8_t * qs, float * d, int16_t * bsums) {
+    const int lane = threadIdx.x & 31;
+    unsigned long long key = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const unsigned long long k = amax_key(fabsf(vals.v[j]), 8 * lane + j);
+        key = k > key ? k : key;
+    }
+    key = warp_max_u64(key);
+    const float amax = __uint_as_float(static_cast<unsigned>(key >> 32));
+    const int winner = static_cast<int>(0xffffffffu - static_cast<unsigned>(key & 0xffffffffull));
+    float mine = vals.v[0];
+#pragma unroll
+    for (int j = 1; j < 8; ++j) mine = (winner & 7) == j ? vals.v[j] : mine;
+    const float mx = __shfl_sync(0xffffffffu, mine, winner >> 3);
+    int q[8];
+    float dval = 0.0f;
+    if (amax != 0.0f) {
+        const float iscale = __fdiv_rn(-127.0f, mx);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int t = __float2int_rn(__fmul_rn(iscale, vals.v[j]));
+            q[j] = t < 127 ? t : 127;
+        }
+        dval = __fdiv_rn(1.0f, iscale);
+    } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) q[j] = 0;
+    }
+    uint32_t lo = 0, hi = 0;
+    int s = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        lo |= (static_cast<uint32_t>(q[j]) & 0xffu) << (8 * j);
+        hi |= (static_cast<uint32_t>(q[j + 4]) & 0xffu) << (8 * j);
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) s += q[j];
+    *reinterpret_cast<uint2 *>(qs + 8 * lane) = make_uint2(lo, hi);
+    s += __shfl_xor_sync(0xffffffffu, s, 1);  // 16-value group = lanes 2g, 2g + 1
+    if ((lane & 1) == 0) bsums[lane >> 1] = static_cast<int16_t>(s);
+    if (lane == 0) *d = dval;
+}
+
 }  // namespace jfb

@@ -2,10 +2,12 @@
 // RMSNorm (+weight) and SwiGLU, each optionally fused with the Q8_K
 // quantization GGML-CPU applies to the src1 of every K-quant mul_mat.
 //
-// One 256-thread CTA per row; for rows whose length is a multiple of 256 the
-// row is walked one 256-value Q8_K block at a time with thread t owning
-// element t of the block, so the quantizer needs no data exchange beyond the
-// block reductions.
+// Q8_K blocks are quantized one per warp (q8k_block_warp): lane l owns the
+// eight consecutive values 8l..8l+7 of its block, so the row kernels never
+// wait on a block-wide barrier per 256 values. SwiGLU and plain quantization
+// spread a row's blocks over many warps and CTAs; RMSNorm keeps one CTA per
+// row (the mean needs the whole row) and each of its warps quantizes its own
+// blocks straight from registers.
 #include "common.cuh"
 
 namespace jfb {
@@ -32,47 +34,62 @@ __device__ __forceinline__ double block_sum_double(double v, double * shared) {
 
 // ggml_rms_norm (sum of float squares accumulated in double, mean rounded to
 // float, scale = 1/sqrtf(mean + eps), y = x*scale) followed by ggml_mul with
-// the norm weight (qwen2_architecture.cpp:373-376).
+// the norm weight (qwen2_architecture.cpp:373-376). Thread t = 32w + l holds
+// elements 256(w + 8c) + 8l .. +8 for c = 0, 1, ..., so warp w's values of
+// round c are exactly Q8_K block w + 8c.
 __global__ void __launch_bounds__(kThreads) rmsnorm_quant_kernel(
     const float * __restrict__ x, const int32_t * __restrict__ row_index, const float * __restrict__ w,
     uint32_t cols, float eps, float * __restrict__ out_f32, jfb_q8k q8, int quantize) {
+    constexpr int kRounds = kMaxRowChunks / 8;  // 2048 values per round
     __shared__ double red[kThreads / 32];
-    __shared__ unsigned long long keys[8];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t row = blockIdx.x;
     const uint64_t src_row = row_index != nullptr ? uint64_t(row_index[row]) : uint64_t(row);
     const float * xr = x + src_row * cols;
-    float v[kMaxRowChunks];
+    float v[kRounds][8];
     double sq = 0.0;
 #pragma unroll
-    for (int c = 0; c < kMaxRowChunks; ++c) {
-        const uint32_t i = uint32_t(c) * kThreads + threadIdx.x;
-        v[c] = i < cols ? xr[i] : 0.0f;
-        if (i < cols) sq += double(__fmul_rn(v[c], v[c]));
+    for (int c = 0; c < kRounds; ++c) {
+        const uint32_t base = uint32_t(warp + 8 * c) * kQK + 8 * lane;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const uint32_t i = base + j;
+            v[c][j] = i < cols ? xr[i] : 0.0f;
+            if (i < cols) sq += double(__fmul_rn(v[c][j], v[c][j]));
+        }
     }
     const double sum = block_sum_double(sq, red);
     const float mean = float(sum / double(cols));
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
 #pragma unroll
-    for (int c = 0; c < kMaxRowChunks; ++c) {
-        const uint32_t i = uint32_t(c) * kThreads + threadIdx.x;
-        if (uint32_t(c) * kThreads >= cols) break;
-        const float y = i < cols ? __fmul_rn(__fmul_rn(v[c], scale), w[i]) : 0.0f;
-        if (out_f32 != nullptr && i < cols) out_f32[uint64_t(row) * cols + i] = y;
+    for (int c = 0; c < kRounds; ++c) {
+        const uint32_t blk = uint32_t(warp + 8 * c);
+        if (blk * kQK >= cols) break;  // warp-uniform
+        const uint32_t base = blk * kQK + 8 * lane;
+        Vals8 y;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const uint32_t i = base + j;
+            y.v[j] = i < cols ? __fmul_rn(__fmul_rn(v[c][j], scale), w[i]) : 0.0f;
+            if (out_f32 != nullptr && i < cols) out_f32[uint64_t(row) * cols + i] = y.v[j];
+        }
         if (quantize) {
-            const uint64_t block = uint64_t(row) * (cols / kQK) + c;
-            q8k_block_256(y, q8.qs + block * kQK, q8.d + block, q8.bsums + block * 16, keys);
+            const uint64_t block = uint64_t(row) * (cols / kQK) + blk;
+            q8k_block_warp(y, q8.qs + block * kQK, q8.d + block, q8.bsums + block * 16);
         }
     }
 }
 
+// One warp per Q8_K block: grid (ceil(blocks / 8), rows).
 __global__ void __launch_bounds__(kThreads) quantize_kernel(const float * __restrict__ x, uint32_t cols, jfb_q8k q8) {
-    __shared__ unsigned long long keys[8];
-    const uint32_t row = blockIdx.x;
-    for (uint32_t c = 0; c < cols / kQK; ++c) {
-        const float y = x[uint64_t(row) * cols + c * kQK + threadIdx.x];
-        const uint64_t block = uint64_t(row) * (cols / kQK) + c;
-        q8k_block_256(y, q8.qs + block * kQK, q8.d + block, q8.bsums + block * 16, keys);
-    }
+    const uint32_t blk = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (blk >= cols / kQK) return;  // warp-uniform
+    const uint32_t row = blockIdx.y;
+    const float4 * src = reinterpret_cast<const float4 *>(x + uint64_t(row) * cols + blk * kQK + 8 * lane);
+    const float4 a = src[0], b = src[1];
+    const Vals8 y = {{a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w}};
+    const uint64_t block = uint64_t(row) * (cols / kQK) + blk;
+    q8k_block_warp(y, q8.qs + block * kQK, q8.d + block, q8.bsums + block * 16);
 }
 
 // silu(g) * u with silu(g) = g / (1 + e^-g), each step rounded
@@ -81,21 +98,26 @@ __device__ __forceinline__ float swiglu(float g, float u) {
     return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, exp_cw(-g))), u);
 }
 
+// One warp per 256 values: grid (ceil(cols / 2048), rows). With Q8_K output
+// (cols a multiple of 256) each warp quantizes its block; the f32-only form
+// also takes rows of any length.
 __global__ void __launch_bounds__(kThreads) swiglu_quant_kernel(const float * __restrict__ gate, const float * __restrict__ up,
                                                              uint32_t cols, float * __restrict__ out_f32, jfb_q8k q8,
                                                              int quantize) {
-    __shared__ unsigned long long keys[8];
-    const uint32_t row = blockIdx.x;
-    const uint32_t chunks = (cols + kThreads - 1) / kThreads;
-    for (uint32_t c = 0; c < chunks; ++c) {
-        const uint32_t i = c * kThreads + threadIdx.x;
-        const uint64_t at = uint64_t(row) * cols + i;
-        const float y = i < cols ? swiglu(gate[at], up[at]) : 0.0f;
-        if (out_f32 != nullptr && i < cols) out_f32[at] = y;
-        if (quantize) {
-            const uint64_t block = uint64_t(row) * (cols / kQK) + c;
-            q8k_block_256(y, q8.qs + block * kQK, q8.d + block, q8.bsums + block * 16, keys);
-        }
+    const uint32_t blk = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (blk * kQK >= cols) return;  // warp-uniform
+    const uint32_t row = blockIdx.y;
+    const uint64_t base = uint64_t(row) * cols + blk * kQK + 8 * lane;
+    Vals8 y;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const bool in = blk * kQK + 8 * lane + j < cols;
+        y.v[j] = in ? swiglu(gate[base + j], up[base + j]) : 0.0f;
+        if (out_f32 != nullptr && in) out_f32[base + j] = y.v[j];
+    }
+    if (quantize) {
+        const uint64_t block = uint64_t(row) * (cols / kQK) + blk;
+        q8k_block_warp(y, q8.qs + block * kQK, q8.d + block, q8.bsums + block * 16);
     }
 }
 
@@ -136,7 +158,8 @@ extern "C" jfb_status jfb_quantize_q8k(const float * x, uint32_t n, uint32_t col
     jfb_status s = check_q8(out, cols);
     if (s.code != JFB_STATUS_OK) return s;
     if (n == 0) return status_ok();
-    quantize_kernel<<<n, kThreads, 0, as_stream(stream)>>>(x, cols, *out);
+    if (n > 65535u) return status_error(JFB_STATUS_INVALID_ARGUMENT, "Q8_K rows above 65535 per call");
+    quantize_kernel<<<dim3((cols / kQK + 7) / 8, n), kThreads, 0, as_stream(stream)>>>(x, cols, *out);
     return launch_status("jfb_quantize_q8k");
 }
 
@@ -149,6 +172,8 @@ extern "C" jfb_status jfb_swiglu_quant(const float * gate, const float * up, uin
     if (s.code != JFB_STATUS_OK) return s;
     if (n == 0 || cols == 0) return status_ok();
     const jfb_q8k q8 = out_q8 != nullptr ? *out_q8 : jfb_q8k{nullptr, nullptr, nullptr};
-    swiglu_quant_kernel<<<n, kThreads, 0, as_stream(stream)>>>(gate, up, cols, out_f32, q8, out_q8 != nullptr);
+    if (n > 65535u) return status_error(JFB_STATUS_INVALID_ARGUMENT, "swiglu rows above 65535 per call");
+    swiglu_quant_kernel<<<dim3((cols + 8 * kQK - 1) / (8 * kQK), n), kThreads, 0, as_stream(stream)>>>(
+        gate, up, cols, out_f32, q8, out_q8 != nullptr);
     return launch_status("jfb_swiglu_quant");
 }
