@@ -145,10 +145,32 @@ jfb_status jfb_matmul(const jfb_weight * weight, const jfb_q8k * x_q8, const flo
  * mapped into the device address space) receives a nonzero code when a
  * bounded pipeline wait gave up. */
 int jfb_matmul_tc_supported(const jfb_weight * weight);
+
+/* Output segments of one tensor-core launch over a weight whose rows stack
+ * several matrices (fused Q/K/V, gate/up): rows [previous row_end, row_end)
+ * are written to `out` [n][segment rows] with their own epilogue, bias
+ * [segment rows] and residual [n][segment rows]. */
+typedef struct jfb_matmul_segment {
+    uint32_t row_end;
+    uint32_t epilogue;
+    const float * bias;
+    const float * residual;
+    float * out;
+} jfb_matmul_segment;
+#define JFB_MATMUL_MAX_SEGMENTS 4
 uint64_t jfb_matmul_tc_workspace_bytes(uint32_t rows, uint32_t cols, uint32_t n);
 jfb_status jfb_matmul_tc(const jfb_weight * weight, const jfb_q8k * x_q8, uint32_t n, uint32_t epilogue,
                          const float * bias, const float * residual, float * out, void * workspace,
                          uint64_t workspace_bytes, int32_t * error_flag, void * stream);
+/* The same with 1..JFB_MATMUL_MAX_SEGMENTS output segments (the last
+ * segment's row_end must be weight->rows). */
+jfb_status jfb_matmul_tc_segments(const jfb_weight * weight, const jfb_q8k * x_q8, uint32_t n,
+                                  const jfb_matmul_segment * segments, uint32_t segment_count, void * workspace,
+                                  uint64_t workspace_bytes, int32_t * error_flag, void * stream);
+
+/* A view of rows [row_begin, row_begin + rows) of a K-quant weight: the same
+ * device planes offset to that row range (planes are row-major), no copy. */
+jfb_status jfb_weight_row_view(const jfb_weight * weight, uint32_t row_begin, uint32_t rows, jfb_weight * view);
 
 /* NEOX rotary embedding of q and k plus the F16 KV-cache append
  * (ggml_rope_ext NEOX + ggml_set_rows, qwen2_architecture.cpp:400-424,

@@ -245,6 +245,41 @@ DeviceModel::DeviceModel(const std::string & package_path, std::uint32_t layer_s
         require_shape(p + "ffn_down.weight", {f, h});
     }
 
+    // Fusion groups: a layer's Q/K/V and gate/up stacked by rows into one
+    // matrix when they share a K-quant type, so a tensor-core launch covers
+    // the group; the members become row views of it.
+    struct Group {
+        std::string name;
+        std::vector<std::string> members;
+        std::uint32_t type = 0, cols = 0, rows = 0;
+        std::uint64_t raw_bytes = 0, offset = 0;
+    };
+    std::vector<Group> groups;
+    std::unordered_map<std::string, std::size_t> grouped;  // member -> group
+    auto is_kq = [](std::uint32_t t) { return t == JF_TENSOR_Q4_K || t == JF_TENSOR_Q6_K || t == JF_TENSOR_Q2_K; };
+    for (std::uint32_t l = layer_start_; l < layer_end_; ++l) {
+        const std::string p = "blk." + std::to_string(l) + ".";
+        for (const auto & [gname, members] : std::vector<std::pair<std::string, std::vector<std::string>>>{
+                 {p + "attn_qkv", {p + "attn_q.weight", p + "attn_k.weight", p + "attn_v.weight"}},
+                 {p + "ffn_gate_up", {p + "ffn_gate.weight", p + "ffn_up.weight"}}}) {
+            Group g;
+            g.name = gname;
+            g.members = members;
+            bool ok = true;
+            for (const std::string & m : members) {
+                const jf_tensor_view & v = require(m);
+                if (!is_kq(v.type) || (g.type != 0 && (v.type != g.type || v.shape[0] != g.cols))) ok = false;
+                g.type = v.type;
+                g.cols = static_cast<std::uint32_t>(v.shape[0]);
+                g.rows += static_cast<std::uint32_t>(v.shape[1]);
+                g.raw_bytes += v.size;
+            }
+            if (!ok) continue;
+            for (const std::string & m : members) grouped[m] = groups.size();
+            groups.push_back(g);
+        }
+    }
+
     // One device arena for the whole stage; matrices in the planar layout.
     struct Placement {
         const jf_tensor_view * view;
@@ -254,7 +289,13 @@ DeviceModel::DeviceModel(const std::string & package_path, std::uint32_t layer_s
     std::vector<Placement> placements;
     std::uint64_t cursor = 0, max_raw = 0;
     std::unordered_map<std::string, std::size_t> index;
+    for (Group & g : groups) {
+        g.offset = cursor;
+        cursor = align256(cursor + jfb_weight_device_bytes(g.type, g.rows, g.cols));
+        max_raw = std::max<std::uint64_t>(max_raw, g.raw_bytes);
+    }
     for (const auto & [name, v] : views) {
+        if (grouped.count(name) != 0) continue;
         const bool matrix = v.rank == 2;
         std::uint64_t bytes;
         if (matrix) {
@@ -290,6 +331,30 @@ DeviceModel::DeviceModel(const std::string & package_path, std::uint32_t layer_s
         jfb_check(jfb_weight_repack(pl.view->type, static_cast<std::uint32_t>(pl.view->shape[1]),
                                     static_cast<std::uint32_t>(pl.view->shape[0]), staging, dst, &w, stream_));
         matrices[name] = w;
+        cuda_check(cudaStreamSynchronize(stream_), "repack native tensor");  // staging is reused
+    }
+    std::unordered_map<std::string, jfb_weight> fused;
+    for (const Group & g : groups) {
+        std::uint64_t at = 0;
+        for (const std::string & m : g.members) {
+            const jf_tensor_view & v = require(m);
+            cuda_check(cudaMemcpyAsync(static_cast<std::uint8_t *>(staging) + at, v.data, v.size, cudaMemcpyHostToDevice,
+                                       stream_),
+                       "upload native tensor");
+            at += v.size;
+        }
+        jfb_weight w{};
+        jfb_check(jfb_weight_repack(g.type, g.rows, g.cols, staging, static_cast<std::uint8_t *>(arena_) + g.offset, &w,
+                                    stream_));
+        fused[g.name] = w;
+        std::uint32_t row = 0;
+        for (const std::string & m : g.members) {
+            const std::uint32_t rows = static_cast<std::uint32_t>(require(m).shape[1]);
+            jfb_weight view{};
+            jfb_check(jfb_weight_row_view(&w, row, rows, &view));
+            matrices[m] = view;
+            row += rows;
+        }
         cuda_check(cudaStreamSynchronize(stream_), "repack native tensor");  // staging is reused
     }
     cuda_check(cudaStreamSynchronize(stream_), "upload native weights");
@@ -337,6 +402,8 @@ DeviceModel::DeviceModel(const std::string & package_path, std::uint32_t layer_s
         w.k_bias = vec(p + "attn_k.bias");
         w.v_bias = vec(p + "attn_v.bias");
         w.ffn_norm = vec(p + "ffn_norm.weight");
+        if (const auto it = fused.find(p + "attn_qkv"); it != fused.end()) w.qkv = it->second;
+        if (const auto it = fused.find(p + "ffn_gate_up"); it != fused.end()) w.gate_up = it->second;
         layer_weights_.push_back(w);
     }
 }
@@ -498,7 +565,9 @@ void Qwen2Stage::ensure_scratch(std::uint32_t rows, std::uint32_t seqs, std::uin
     std::uint64_t tc = 0;
     for (std::uint32_t li = 0; li < m_.layers(); ++li) {
         const LayerWeights & lw = m_.layer(li);
-        for (const jfb_weight * x : {&lw.q, &lw.k, &lw.v, &lw.o, &lw.gate, &lw.up, &lw.down}) tc = std::max(tc, tc_need(*x, R));
+        for (const jfb_weight * x : {&lw.q, &lw.k, &lw.v, &lw.o, &lw.gate, &lw.up, &lw.down, &lw.qkv, &lw.gate_up}) {
+            if (x->type != 0) tc = std::max(tc, tc_need(*x, R));
+        }
     }
     if (m_.last_stage()) tc = std::max(tc, tc_need(m_.output(), S));
     if (tc > 0) {
@@ -602,10 +671,21 @@ void Qwen2Stage::forward(std::span<const SequenceRows> seqs, const ForwardIo & i
         cuda_check(cudaEventRecord(t.stop, st), "record timing event");
         timed_.push_back(t);
     };
+    auto use_tc = [&](const jfb_weight & w, std::uint32_t n) {
+        return w.type != 0 && matmul_path_ != 1 && tc_workspace_ != nullptr && jfb_matmul_tc_supported(&w) &&
+               (matmul_path_ == 2 || n >= kTensorCoreMinRows);
+    };
+    // one tensor-core launch over a stacked weight, one output segment per member
+    auto mm_fused = [&](const jfb_weight & w, std::uint32_t n, const jfb_matmul_segment * segs, std::uint32_t count,
+                        double bytes) {
+        timed(0, bytes, [&] {
+            jfb_check(jfb_matmul_tc_segments(&w, &q8_, n, segs, count, tc_workspace_, tc_workspace_bytes_, tc_error_dev_,
+                                             st));
+        });
+    };
     auto mm = [&](const jfb_weight & w, const float * xf, std::uint32_t n, std::uint32_t ep, const float * bias,
                   const float * residual, float * out) {
-        const bool tc = matmul_path_ != 1 && tc_workspace_ != nullptr && jfb_matmul_tc_supported(&w) &&
-                        (matmul_path_ == 2 || n >= kTensorCoreMinRows);
+        const bool tc = use_tc(w, n);
         timed(0, matmul_bytes(w, n, ep), [&] {
             if (tc) {
                 jfb_check(jfb_matmul_tc(&w, &q8_, n, ep, bias, residual, out, tc_workspace_, tc_workspace_bytes_,
@@ -627,9 +707,20 @@ void Qwen2Stage::forward(std::span<const SequenceRows> seqs, const ForwardIo & i
         const bool attn_f32 = !needs_q8(w.q) || !needs_q8(w.k) || !needs_q8(w.v);
         jfb_check(jfb_rmsnorm_quant(hidden_, nullptr, w.attn_norm, R, std::uint32_t(h), hp.rms_epsilon,
                                     attn_f32 ? xf_ : nullptr, attn_q8 ? &q8_ : nullptr, st));
-        mm(w.q, xf_, R, JFB_EPILOGUE_BIAS, w.q_bias, nullptr, q_);
-        mm(w.k, xf_, R, JFB_EPILOGUE_BIAS, w.k_bias, nullptr, k_);
-        mm(w.v, xf_, R, JFB_EPILOGUE_BIAS, w.v_bias, nullptr, v_);
+        if (use_tc(w.qkv, R)) {
+            const std::uint32_t qr = w.q.rows, kr = w.k.rows, vr = w.v.rows;
+            const jfb_matmul_segment segs[3] = {{qr, JFB_EPILOGUE_BIAS, w.q_bias, nullptr, q_},
+                                                {qr + kr, JFB_EPILOGUE_BIAS, w.k_bias, nullptr, k_},
+                                                {qr + kr + vr, JFB_EPILOGUE_BIAS, w.v_bias, nullptr, v_}};
+            mm_fused(w.qkv, R, segs, 3,
+                     matmul_bytes(w.q, R, JFB_EPILOGUE_BIAS) + matmul_bytes(w.k, R, JFB_EPILOGUE_BIAS) +
+                         matmul_bytes(w.v, R, JFB_EPILOGUE_BIAS));
+            launches_ -= 2;
+        } else {
+            mm(w.q, xf_, R, JFB_EPILOGUE_BIAS, w.q_bias, nullptr, q_);
+            mm(w.k, xf_, R, JFB_EPILOGUE_BIAS, w.k_bias, nullptr, k_);
+            mm(w.v, xf_, R, JFB_EPILOGUE_BIAS, w.v_bias, nullptr, v_);
+        }
         jfb_check(jfb_rope_kv_append(q_, k_, v_, R, seq_d, pos_d, hp.head_count, hp.kv_head_count, hp.head_dim(),
                                      hp.rope_dimension_count, m_.rope_table(), hp.info.context_length, slots_d, li, st));
         const bool o_q8 = needs_q8(w.o);
@@ -642,8 +733,16 @@ void Qwen2Stage::forward(std::span<const SequenceRows> seqs, const ForwardIo & i
         const bool ffn_f32 = !needs_q8(w.gate) || !needs_q8(w.up);
         jfb_check(jfb_rmsnorm_quant(hidden_, nullptr, w.ffn_norm, R, std::uint32_t(h), hp.rms_epsilon,
                                     ffn_f32 ? xf_ : nullptr, ffn_q8 ? &q8_ : nullptr, st));
-        mm(w.gate, xf_, R, JFB_EPILOGUE_STORE, nullptr, nullptr, gate_);
-        mm(w.up, xf_, R, JFB_EPILOGUE_STORE, nullptr, nullptr, up_);
+        if (use_tc(w.gate_up, R)) {
+            const jfb_matmul_segment segs[2] = {{w.gate.rows, JFB_EPILOGUE_STORE, nullptr, nullptr, gate_},
+                                                {w.gate.rows + w.up.rows, JFB_EPILOGUE_STORE, nullptr, nullptr, up_}};
+            mm_fused(w.gate_up, R, segs, 2,
+                     matmul_bytes(w.gate, R, JFB_EPILOGUE_STORE) + matmul_bytes(w.up, R, JFB_EPILOGUE_STORE));
+            launches_ -= 1;
+        } else {
+            mm(w.gate, xf_, R, JFB_EPILOGUE_STORE, nullptr, nullptr, gate_);
+            mm(w.up, xf_, R, JFB_EPILOGUE_STORE, nullptr, nullptr, up_);
+        }
         const bool down_q8 = needs_q8(w.down);
         jfb_check(jfb_swiglu_quant(gate_, up_, R, std::uint32_t(f), down_q8 ? nullptr : xf_, down_q8 ? &q8_ : nullptr, st));
         mm(w.down, xf_, R, JFB_EPILOGUE_RESIDUAL, nullptr, hidden_, hidden_);

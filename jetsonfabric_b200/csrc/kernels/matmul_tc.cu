@@ -393,10 +393,13 @@ struct TcParams {
     uint32_t tiles_m;
     uint32_t tiles;
     uint64_t work;          // tiles * blocks
-    uint32_t epilogue;
-    const float * bias;
-    const float * residual;
-    float * out;            // [n][rows]
+    // output segments: rows [seg_end[k-1], seg_end[k]) -> seg_out[k] [n][rows of k]
+    uint32_t nseg;
+    uint32_t seg_end[JFB_MATMUL_MAX_SEGMENTS];
+    uint32_t seg_epilogue[JFB_MATMUL_MAX_SEGMENTS];
+    const float * seg_bias[JFB_MATMUL_MAX_SEGMENTS];
+    const float * seg_residual[JFB_MATMUL_MAX_SEGMENTS];
+    float * seg_out[JFB_MATMUL_MAX_SEGMENTS];
     double * partial;       // [2 * gridDim.x][kBN][kRows]
     uint32_t * counters;    // [tiles][kEpilogueWarps]
     int * error;
@@ -984,15 +987,25 @@ __global__ void __launch_bounds__(kThreads, 1) mmq_tc_kernel(const __grid_consta
                 }
             }
             if (row < p.w.rows) {
+                // this row's output segment
+                int k = 0;
+#pragma unroll
+                for (int j = 0; j < JFB_MATMUL_MAX_SEGMENTS - 1; ++j) k += (j < int(p.nseg) - 1 && row >= p.seg_end[j]) ? 1 : 0;
+                const uint32_t seg_begin_row = k == 0 ? 0u : p.seg_end[k - 1];
+                const uint32_t ld = p.seg_end[k] - seg_begin_row, r = row - seg_begin_row;
+                const uint32_t ep = p.seg_epilogue[k];
+                float * out = p.seg_out[k];
+                const float * bias = p.seg_bias[k];
+                const float * residual = p.seg_residual[k];
 #pragma unroll
                 for (int t = 0; t < kCols; ++t) {
                     const uint32_t tok = tok0 + col0 + t;
                     if (tok >= p.n) break;
-                    const uint64_t at = uint64_t(tok) * p.w.rows + row;
+                    const uint64_t at = uint64_t(tok) * ld + r;
                     float v = __double2float_rn(sum[t]);
-                    if (p.epilogue == JFB_EPILOGUE_BIAS) v = __fadd_rn(v, p.bias[row]);
-                    else if (p.epilogue == JFB_EPILOGUE_RESIDUAL) v = __fadd_rn(v, p.residual[at]);
-                    p.out[at] = v;
+                    if (ep == JFB_EPILOGUE_BIAS) v = __fadd_rn(v, bias[r]);
+                    else if (ep == JFB_EPILOGUE_RESIDUAL) v = __fadd_rn(v, residual[at]);
+                    out[at] = v;
                 }
             }
         }
@@ -1153,18 +1166,31 @@ extern "C" int jfb_matmul_tc_supported(const jfb_weight * w) {
     return w != nullptr && is_kquant(w->type) && w->rows > 0 && w->cols >= kQK && w->cols % kQK == 0 ? 1 : 0;
 }
 
-extern "C" jfb_status jfb_matmul_tc(const jfb_weight * weight, const jfb_q8k * x_q8, uint32_t n, uint32_t epilogue,
-                                    const float * bias, const float * residual, float * out, void * workspace,
-                                    uint64_t workspace_size, int32_t * error_flag, void * stream) {
-    if (weight == nullptr || x_q8 == nullptr || out == nullptr) {
-        return status_error(JFB_STATUS_INVALID_ARGUMENT, "weight, activations and output are required");
+extern "C" jfb_status jfb_matmul_tc_segments(const jfb_weight * weight, const jfb_q8k * x_q8, uint32_t n,
+                                             const jfb_matmul_segment * segments, uint32_t segment_count,
+                                             void * workspace, uint64_t workspace_size, int32_t * error_flag,
+                                             void * stream) {
+    if (weight == nullptr || x_q8 == nullptr || segments == nullptr) {
+        return status_error(JFB_STATUS_INVALID_ARGUMENT, "weight, activations and output segments are required");
     }
     if (!jfb_matmul_tc_supported(weight)) {
         return status_error(JFB_STATUS_UNSUPPORTED, "jfb_matmul_tc needs a Q4_K, Q6_K or Q2_K weight");
     }
-    if (epilogue > JFB_EPILOGUE_RESIDUAL || (epilogue == JFB_EPILOGUE_BIAS && bias == nullptr) ||
-        (epilogue == JFB_EPILOGUE_RESIDUAL && residual == nullptr)) {
-        return status_error(JFB_STATUS_INVALID_ARGUMENT, "matmul epilogue operands are missing");
+    if (segment_count == 0 || segment_count > JFB_MATMUL_MAX_SEGMENTS) {
+        return status_error(JFB_STATUS_INVALID_ARGUMENT, "1 to %d output segments are supported", JFB_MATMUL_MAX_SEGMENTS);
+    }
+    uint32_t prev = 0;
+    for (uint32_t k = 0; k < segment_count; ++k) {
+        const jfb_matmul_segment & g = segments[k];
+        if (g.out == nullptr || g.row_end <= prev || g.epilogue > JFB_EPILOGUE_RESIDUAL ||
+            (g.epilogue == JFB_EPILOGUE_BIAS && g.bias == nullptr) ||
+            (g.epilogue == JFB_EPILOGUE_RESIDUAL && g.residual == nullptr)) {
+            return status_error(JFB_STATUS_INVALID_ARGUMENT, "matmul output segment %u is invalid", k);
+        }
+        prev = g.row_end;
+    }
+    if (prev != weight->rows) {
+        return status_error(JFB_STATUS_INVALID_ARGUMENT, "output segments must end at the weight's %u rows", weight->rows);
     }
     if (n == 0) return status_ok();
     if (x_q8->qs == nullptr || x_q8->d == nullptr || x_q8->bsums == nullptr) {
@@ -1197,10 +1223,15 @@ extern "C" jfb_status jfb_matmul_tc(const jfb_weight * weight, const jfb_q8k * x
     p.tiles_m = pl.tiles_m;
     p.tiles = pl.tiles;
     p.work = pl.work;
-    p.epilogue = epilogue;
-    p.bias = bias;
-    p.residual = residual;
-    p.out = out;
+    p.nseg = segment_count;
+    for (uint32_t k = 0; k < JFB_MATMUL_MAX_SEGMENTS; ++k) {
+        const bool used = k < segment_count;
+        p.seg_end[k] = used ? segments[k].row_end : weight->rows;
+        p.seg_epilogue[k] = used ? segments[k].epilogue : JFB_EPILOGUE_STORE;
+        p.seg_bias[k] = used ? segments[k].bias : nullptr;
+        p.seg_residual[k] = used ? segments[k].residual : nullptr;
+        p.seg_out[k] = used ? segments[k].out : nullptr;
+    }
     p.partial = static_cast<double *>(workspace);
     p.counters = reinterpret_cast<uint32_t *>(static_cast<uint8_t *>(workspace) + partial_bytes());
     p.error = error_flag;
@@ -1210,4 +1241,18 @@ extern "C" jfb_status jfb_matmul_tc(const jfb_weight * weight, const jfb_q8k * x
     case JF_TENSOR_Q6_K: return launch<JF_TENSOR_Q6_K>(p, weight->cols, pl.grid, s);
     default: return launch<JF_TENSOR_Q2_K>(p, weight->cols, pl.grid, s);
     }
+}
+
+extern "C" jfb_status jfb_matmul_tc(const jfb_weight * weight, const jfb_q8k * x_q8, uint32_t n, uint32_t epilogue,
+                                    const float * bias, const float * residual, float * out, void * workspace,
+                                    uint64_t workspace_size, int32_t * error_flag, void * stream) {
+    if (weight == nullptr || x_q8 == nullptr || out == nullptr) {
+        return status_error(JFB_STATUS_INVALID_ARGUMENT, "weight, activations and output are required");
+    }
+    if (epilogue > JFB_EPILOGUE_RESIDUAL || (epilogue == JFB_EPILOGUE_BIAS && bias == nullptr) ||
+        (epilogue == JFB_EPILOGUE_RESIDUAL && residual == nullptr)) {
+        return status_error(JFB_STATUS_INVALID_ARGUMENT, "matmul epilogue operands are missing");
+    }
+    const jfb_matmul_segment seg{weight->rows, epilogue, bias, residual, out};
+    return jfb_matmul_tc_segments(weight, x_q8, n, &seg, 1, workspace, workspace_size, error_flag, stream);
 }

@@ -162,6 +162,28 @@ extern "C" uint64_t jfb_weight_device_bytes(uint32_t type, uint32_t rows, uint32
     return align_up(p.bytes[0], kPlaneAlign) + align_up(p.bytes[1], kPlaneAlign) + align_up(p.bytes[2] + tail, kPlaneAlign);
 }
 
+extern "C" jfb_status jfb_weight_row_view(const jfb_weight * weight, uint32_t row_begin, uint32_t rows,
+                                          jfb_weight * view) {
+    if (weight == nullptr || view == nullptr || !is_kquant(weight->type)) {
+        return status_error(JFB_STATUS_INVALID_ARGUMENT, "row views need a K-quant weight");
+    }
+    if (rows == 0 || uint64_t(row_begin) + rows > weight->rows) {
+        return status_error(JFB_STATUS_INVALID_ARGUMENT, "row view [%u, %u) is outside the weight's %u rows", row_begin,
+                            row_begin + rows, weight->rows);
+    }
+    uint32_t b[3];
+    plane_block_bytes(weight->type, &b[0], &b[1], &b[2]);
+    const uint64_t blocks_before = uint64_t(row_begin) * (weight->cols / kQK);
+    *view = *weight;
+    view->rows = rows;
+    for (int i = 0; i < 3; ++i) {
+        view->plane[i] = weight->plane[i] == nullptr
+                             ? nullptr
+                             : static_cast<const uint8_t *>(weight->plane[i]) + blocks_before * b[i];
+    }
+    return status_ok();
+}
+
 static jfb_status check_weight_shape(uint32_t type, uint32_t rows, uint32_t cols) {
     if (rows == 0 || cols == 0) return status_error(JFB_STATUS_INVALID_ARGUMENT, "weight shape must be positive");
     if (type != JF_TENSOR_F32 && type != JF_TENSOR_F16 && !is_kquant(type)) {

@@ -22,6 +22,11 @@ class Q8K(C.Structure):
     _fields_ = [("qs", C.c_void_p), ("d", C.c_void_p), ("bsums", C.c_void_p)]
 
 
+class Segment(C.Structure):
+    _fields_ = [("row_end", C.c_uint32), ("epilogue", C.c_uint32), ("bias", C.c_void_p), ("residual", C.c_void_p),
+                ("out", C.c_void_p)]
+
+
 class KvSlot(C.Structure):
     _fields_ = [("k", C.c_void_p), ("v", C.c_void_p), ("capacity", C.c_uint32), ("reserved", C.c_uint32)]
 
@@ -46,6 +51,9 @@ def _bind():
         "jfb_swiglu_quant": ([_VP, _VP, C.c_uint32, C.c_uint32, _VP, C.POINTER(Q8K), _VP], Status),
         "jfb_matmul": ([C.POINTER(Weight), C.POINTER(Q8K), _VP, C.c_uint32, C.c_uint32, _VP, _VP, _VP, _VP], Status),
         "jfb_matmul_tc_supported": ([C.POINTER(Weight)], C.c_int),
+        "jfb_matmul_tc_segments": ([C.POINTER(Weight), C.POINTER(Q8K), C.c_uint32, C.POINTER(Segment), C.c_uint32, _VP,
+                                    C.c_uint64, _VP, _VP], Status),
+        "jfb_weight_row_view": ([C.POINTER(Weight), C.c_uint32, C.c_uint32, C.POINTER(Weight)], Status),
         "jfb_matmul_tc_workspace_bytes": ([C.c_uint32, C.c_uint32, C.c_uint32], C.c_uint64),
         "jfb_matmul_tc": ([C.POINTER(Weight), C.POINTER(Q8K), C.c_uint32, C.c_uint32, _VP, _VP, _VP, _VP, C.c_uint64,
                            _VP, _VP], Status),
@@ -142,6 +150,23 @@ def matmul_tc(w: DeviceWeight, n: int, out, x_q8: Q8Buffer, workspace, epilogue=
     size = workspace.numel() if workspace_bytes is None else workspace_bytes
     check(_bind().jfb_matmul_tc(C.byref(w.desc), C.byref(x_q8.desc), n, epilogue, ptr(bias), ptr(residual), ptr(out),
                                 ptr(workspace), size, ptr(error_flag), stream_ptr(stream)))
+
+
+def matmul_tc_segments(w: DeviceWeight, n: int, x_q8: Q8Buffer, segments, workspace, error_flag=None, stream=None):
+    """jfb_matmul_tc_segments; `segments` is a list of (row_end, epilogue, bias, residual, out)."""
+    arr = (Segment * len(segments))(*[Segment(r, e, ptr(b), ptr(res), ptr(o)) for r, e, b, res, o in segments])
+    check(_bind().jfb_matmul_tc_segments(C.byref(w.desc), C.byref(x_q8.desc), n, arr, len(segments), ptr(workspace),
+                                         workspace.numel(), ptr(error_flag), stream_ptr(stream)))
+
+
+class WeightView:
+    """Rows [row_begin, row_begin + rows) of a DeviceWeight (jfb_weight_row_view); keeps the parent alive."""
+
+    def __init__(self, parent: DeviceWeight, row_begin: int, rows: int):
+        self.parent = parent
+        self.desc = Weight()
+        check(_bind().jfb_weight_row_view(C.byref(parent.desc), row_begin, rows, C.byref(self.desc)))
+        self.rows, self.cols, self.type = rows, parent.cols, parent.type
 
 
 def argmax(logits, out):

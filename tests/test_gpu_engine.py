@@ -219,3 +219,28 @@ def test_generate_reports_latency(E, small_q4k_package):
         assert r.time_to_first_token_ms > 0 and r.inter_token_latency_ms > 0 and r.kv_cache_bytes > 0
         r2 = eng.generate([1, 2, 3, 4], 8)
         assert r2.sampled_tokens == r.sampled_tokens
+
+
+def test_wide_batched_decode_matches_oracle(E, small_q4k_package):
+    """Ten sessions decoding in one batch (10 rows: the tensor-core path with
+    the stacked Q/K/V and gate/up launches) give the oracle's tokens."""
+    rng = np.random.default_rng(21)
+    prompts = [rng.integers(0, 1024, n).tolist() for n in (6, 11, 3, 9, 14, 5, 8, 12, 7, 10)]
+    steps = 10
+    oracle = ob.OracleStage(small_q4k_package)
+    ref = []
+    for p in prompts:
+        s = oracle.session(len(p) + steps)
+        toks = [s.forward(True, tokens=p)["token"]]
+        for _ in range(steps - 1):
+            toks.append(s.forward(False, tokens=[toks[-1]])["token"])
+        ref.append(toks)
+    with E.NativeEngine(small_q4k_package, "cuda") as eng:
+        sessions = [eng.create_session(len(p) + steps) for p in prompts]
+        cur = [r.sampled_token for r in eng.prefill_stage_batch(sessions, prompts)]
+        got = [[t] for t in cur]
+        for _ in range(steps - 1):
+            cur = [r.sampled_token for r in eng.decode_stage_batch(sessions, cur)]
+            for g, t in zip(got, cur):
+                g.append(t)
+        assert got == ref

@@ -195,3 +195,40 @@ def test_tc_rejects_bad_arguments(K):
     f32 = K.DeviceWeight(jfm.JF_TENSOR_F32, 8, 256, np.zeros(8 * 256, np.float32).tobytes())
     with pytest.raises(NativeExecutionError):
         K.matmul_tc(f32, n, out, q8, torch.zeros(need, dtype=torch.uint8, device="cuda"))
+
+
+@pytest.mark.parametrize("jf_type", KQ)
+def test_tc_segments_over_stacked_rows(K, jf_type):
+    """One launch over a weight stacking three matrices (as the engine stacks
+    Q/K/V) writes each member's rows to its own output with its own bias;
+    row views of the stacked weight through both matmul paths agree."""
+    cols, n = 2048, 24
+    parts = [(300, 31), (128, 32), (200, 33)]
+    raws = [random_blocks(jf_type, r, cols, seed) for r, seed in parts]
+    total = sum(r for r, _ in parts)
+    w = K.DeviceWeight(jf_type, total, cols, b"".join(raws))
+    x = activations(n, cols, 17)
+    q8 = K.Q8Buffer(n, cols)
+    K.quantize_q8k(torch.from_numpy(x).cuda(), q8)
+    ws = torch.zeros(K.matmul_tc_workspace_bytes(total, cols, n), dtype=torch.uint8, device="cuda")
+    rng = np.random.default_rng(5)
+    outs, biases, segs, end = [], [], [], 0
+    for r, _ in parts:
+        end += r
+        bias = torch.from_numpy(rng.normal(0, 0.1, r).astype(np.float32)).cuda()
+        out = torch.empty((n, r), dtype=torch.float32, device="cuda")
+        outs.append(out)
+        biases.append(bias)
+        segs.append((end, K.EPILOGUE_BIAS, bias, None, out))
+    K.matmul_tc_segments(w, n, q8, segs, ws)
+    torch.cuda.synchronize()
+    row = 0
+    for (r, _), raw, out, bias in zip(parts, raws, outs, biases):
+        ref = oracle_matmul(jf_type, raw, r, cols, x) + bias.cpu().numpy()
+        assert np.array_equal(bits(out), bits(ref))
+        view = K.WeightView(w, row, r)
+        core = torch.empty((n, r), dtype=torch.float32, device="cuda")
+        K.matmul(view, n, core, x_q8=q8, epilogue=K.EPILOGUE_BIAS, bias=bias)
+        torch.cuda.synchronize()
+        assert np.array_equal(bits(core), bits(ref))
+        row += r
