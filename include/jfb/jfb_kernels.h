@@ -54,6 +54,15 @@ typedef struct jfb_q8k {
     int8_t * qs;        /* [rows][cols] */
     float * d;          /* [rows][cols/256] */
     int16_t * bsums;    /* [rows][cols/16] */
+    /* Operands of jfb_matmul_tc, written by every quantizer of this library
+     * when non-NULL (all three or none): the same codes and partial sums as
+     * f16 numbers (both are exact: |q| <= 127, |bsum| <= 2032) and the block
+     * scales transposed, so the tensor cores load them without conversion. */
+    uint16_t * qs_f16;     /* [rows][cols] */
+    uint16_t * bsums_f16;  /* [rows][cols/16] */
+    float * d_t;           /* [cols/256][d_stride]: d_t[b * d_stride + r] = d[r][b] */
+    uint32_t d_stride;     /* row stride of d_t in floats: >= rows, a multiple of 4 */
+    uint32_t reserved;
 } jfb_q8k;
 
 /* Per-sequence KV cache: token-major F16 rows for every resident layer,
@@ -133,8 +142,10 @@ jfb_status jfb_matmul(const jfb_weight * weight, const jfb_q8k * x_q8, const flo
  * The epilogue applies the per-block float terms exactly as the CPU rounds
  * them and sums them in double. The kernel is persistent: one CTA per SM walks
  * a contiguous range of (tile, block) work (stream-K, tiles of 128 weight rows
- * x 32 activation rows). A tile shared by several CTAs is finished by the last
- * contributor, which sums the double partials in CTA order.
+ * x 32 activation rows for n <= 32, x 64 above). A tile shared by several CTAs
+ * is finished by the last contributor, which sums the double partials in CTA
+ * order. x_q8 must carry the tensor-core operands (qs_f16, bsums_f16, d_t),
+ * all 16-byte aligned, with d_stride >= n.
  *
  * The workspace holds the partials and the per-tile arrival counters at
  * offsets that do not depend on the shape, so one workspace (sized for the

@@ -507,7 +507,8 @@ void Qwen2Stage::free_scratch() {
     for (void * p : {static_cast<void *>(hidden_), static_cast<void *>(xf_), static_cast<void *>(q_),
                      static_cast<void *>(k_), static_cast<void *>(v_), static_cast<void *>(attn_),
                      static_cast<void *>(gate_), static_cast<void *>(up_), static_cast<void *>(q8_.qs),
-                     static_cast<void *>(q8_.d), static_cast<void *>(q8_.bsums), attn_scratch_,
+                     static_cast<void *>(q8_.d), static_cast<void *>(q8_.bsums), static_cast<void *>(q8_.qs_f16),
+                     static_cast<void *>(q8_.bsums_f16), static_cast<void *>(q8_.d_t), attn_scratch_,
                      static_cast<void *>(logits_), static_cast<void *>(tokens_dev_),
                      static_cast<void *>(error_flag_), meta_dev_, tc_workspace_}) {
         if (p != nullptr) cudaFree(p);
@@ -549,6 +550,12 @@ void Qwen2Stage::ensure_scratch(std::uint32_t rows, std::uint32_t seqs, std::uin
     alloc(&q8_.qs, std::uint64_t(R) * wide);
     alloc(&q8_.d, std::uint64_t(R) * (wide / 256 + 1) * 4);
     alloc(&q8_.bsums, std::uint64_t(R) * (wide / 16 + 1) * 2);
+    // the tensor-core operands every quantizer also writes: f16 codes and
+    // partial sums, d transposed [blocks][d_stride]
+    q8_.d_stride = (R + 3) / 4 * 4;
+    alloc(&q8_.qs_f16, std::uint64_t(R) * wide * 2);
+    alloc(&q8_.bsums_f16, std::uint64_t(R) * (wide / 16 + 1) * 2);
+    alloc(&q8_.d_t, std::uint64_t(q8_.d_stride) * (wide / 256 + 1) * 4);
     attn_scratch_bytes_ = jfb_attention_scratch_bytes(R, hp.head_count, hp.head_dim(), K);
     alloc(&attn_scratch_, attn_scratch_bytes_);
     if (m_.last_stage()) alloc(&logits_, std::uint64_t(S) * m_.vocabulary() * 4);

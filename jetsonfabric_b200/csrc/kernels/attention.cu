@@ -246,8 +246,7 @@ __global__ void __launch_bounds__(256) combine_kernel(const int32_t * __restrict
     __syncthreads();
     for (uint32_t c = 0; c < width / kQK; ++c) {
         const float y = out[uint64_t(r) * width + c * kQK + threadIdx.x];
-        const uint64_t block = uint64_t(r) * (width / kQK) + c;
-        q8k_block_256(y, q8.qs + block * kQK, q8.d + block, q8.bsums + block * 16, keys_s);
+        q8k_block_256(y, q8_dest(q8, r, c, width / kQK), keys_s);
     }
 }
 
@@ -465,8 +464,8 @@ __global__ void __launch_bounds__(kFusedThreads, 1) fused_kernel(const float * _
     const uint32_t blocks_per_row = heads * D / kQK;
 #pragma unroll 1
     for (int c = 0; c < HPC * D / kQK; ++c) {
-        const uint64_t block = uint64_t(r) * blocks_per_row + (uint64_t(h0) * D) / kQK + c;
-        q8k_block_256(outs[c * kQK + threadIdx.x], q8.qs + block * kQK, q8.d + block, q8.bsums + block * 16, q8_keys);
+        const uint32_t blk = uint32_t((uint64_t(h0) * D) / kQK) + uint32_t(c);
+        q8k_block_256(outs[c * kQK + threadIdx.x], q8_dest(q8, r, blk, blocks_per_row), q8_keys);
     }
 }
 
@@ -531,6 +530,10 @@ extern "C" jfb_status jfb_attention(const float * q, uint32_t n, const int32_t *
     if (out_q8 != nullptr && (heads * head_dim) % kQK != 0) {
         return status_error(JFB_STATUS_INVALID_ARGUMENT, "Q8_K attention output needs a width multiple of 256");
     }
+    if (out_q8 != nullptr) {
+        const jfb_status tc = check_q8_tensor_core(out_q8, n);
+        if (tc.code != JFB_STATUS_OK) return tc;
+    }
     if (scratch_bytes < jfb_attention_scratch_bytes(n, heads, head_dim, max_keys)) {
         return status_error(JFB_STATUS_INVALID_ARGUMENT, "attention scratch is too small");
     }
@@ -540,7 +543,7 @@ extern "C" jfb_status jfb_attention(const float * q, uint32_t n, const int32_t *
         return status_error(JFB_STATUS_INVALID_ARGUMENT, "attention grid too large");
     }
     cudaStream_t s = as_stream(stream);
-    const jfb_q8k q8_fused = out_q8 != nullptr ? *out_q8 : jfb_q8k{nullptr, nullptr, nullptr};
+    const jfb_q8k q8_fused = out_q8 != nullptr ? *out_q8 : jfb_q8k{};
     if ((head_dim == 64 || head_dim == 128) && max_keys <= kFusedMaxKeys) {
         const int hpc = fused_heads_per_cta(n, heads, kv_heads);
         const uint32_t keys_cap = (max_keys + 3) / 4 * 4;
@@ -559,7 +562,7 @@ extern "C" jfb_status jfb_attention(const float * q, uint32_t n, const int32_t *
                                                                   scale, splits, sc);
     stats_kernel<<<dim3(n, heads), kThreads, 0, s>>>(pos, heads, splits, sc);
     pv_kernel<<<dim3(n, kv_heads, splits), kThreads, 0, s>>>(seq, pos, heads, kv_heads, head_dim, slots, layer, splits, sc);
-    const jfb_q8k q8 = out_q8 != nullptr ? *out_q8 : jfb_q8k{nullptr, nullptr, nullptr};
+    const jfb_q8k q8 = out_q8 != nullptr ? *out_q8 : jfb_q8k{};
     combine_kernel<<<n, 256, 0, s>>>(pos, heads, head_dim, splits, sc, out, q8, out_q8 != nullptr);
     return launch_status("jfb_attention");
 }

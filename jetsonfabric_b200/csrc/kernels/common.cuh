@@ -42,6 +42,25 @@ inline jfb_status launch_status(const char * what) {
 
 inline cudaStream_t as_stream(void * s) { return static_cast<cudaStream_t>(s); }
 
+// The tensor-core operands of a Q8_K buffer: all three planes or none,
+// 16-byte aligned, d_t wide enough for `rows` rows.
+inline jfb_status check_q8_tensor_core(const jfb_q8k * q8, uint32_t rows) {
+    const int present = (q8->qs_f16 != nullptr) + (q8->bsums_f16 != nullptr) + (q8->d_t != nullptr);
+    if (present == 0) return status_ok();
+    if (present != 3) {
+        return status_error(JFB_STATUS_INVALID_ARGUMENT, "Q8_K tensor-core planes must be given all together");
+    }
+    if ((reinterpret_cast<uintptr_t>(q8->qs_f16) & 15u) != 0 || (reinterpret_cast<uintptr_t>(q8->bsums_f16) & 15u) != 0 ||
+        (reinterpret_cast<uintptr_t>(q8->d_t) & 15u) != 0) {
+        return status_error(JFB_STATUS_INVALID_ARGUMENT, "Q8_K tensor-core planes must be 16-byte aligned");
+    }
+    if (q8->d_stride % 4 != 0 || q8->d_stride < rows) {
+        return status_error(JFB_STATUS_INVALID_ARGUMENT, "Q8_K d_stride %u must be a multiple of 4 and >= %u rows",
+                            q8->d_stride, rows);
+    }
+    return status_ok();
+}
+
 inline bool is_kquant(uint32_t type) {
     return type == JF_TENSOR_Q4_K || type == JF_TENSOR_Q6_K || type == JF_TENSOR_Q2_K;
 }
@@ -128,8 +147,36 @@ __device__ __forceinline__ unsigned long long warp_max_u64(unsigned long long v)
 // q = round-half-even(iscale * x) capped at 127, d = 1/iscale, bsums over 16.
 // `shared` must hold 8 unsigned long long + 16 int. Every thread of the block
 // must call it.
-__device__ __forceinline__ void q8k_block_256(float x, int8_t * qs, float * d, int16_t * bsums,
-                                              unsigned long long * shared_keys) {
+// Where one Q8_K block of a jfb_q8k goes: row r, block b of nb per row.
+struct Q8Dest {
+    int8_t * qs;
+    float * d;
+    int16_t * bsums;
+    uint16_t * qs_f16;     // nullptr when the tensor-core operands are not kept
+    uint16_t * bsums_f16;
+    float * d_t;
+};
+
+__device__ __forceinline__ Q8Dest q8_dest(const jfb_q8k & q8, uint64_t r, uint32_t b, uint32_t nb) {
+    const uint64_t block = r * nb + b;
+    Q8Dest o;
+    o.qs = q8.qs + block * kQK;
+    o.d = q8.d + block;
+    o.bsums = q8.bsums + block * 16;
+    const bool tc = q8.qs_f16 != nullptr;
+    o.qs_f16 = tc ? q8.qs_f16 + block * kQK : nullptr;
+    o.bsums_f16 = tc ? q8.bsums_f16 + block * 16 : nullptr;
+    o.d_t = tc ? q8.d_t + uint64_t(b) * q8.d_stride + r : nullptr;
+    return o;
+}
+
+// f16 bits of a small integer (|v| < 2048: exact).
+__device__ __forceinline__ uint16_t int_to_half_bits(int v) { return __half_as_ushort(__int2half_rn(v)); }
+
+__device__ __forceinline__ void q8k_block_256(float x, const Q8Dest & dst, unsigned long long * shared_keys) {
+    int8_t * qs = dst.qs;
+    float * d = dst.d;
+    int16_t * bsums = dst.bsums;
     const int t = threadIdx.x;
     unsigned long long key = warp_max_u64(amax_key(fabsf(x), t));
     if ((t & 31) == 0) shared_keys[t >> 5] = key;
@@ -158,12 +205,19 @@ __device__ __forceinline__ void q8k_block_256(float x, int8_t * qs, float * d, i
         dval = __fdiv_rn(1.0f, iscale);
     }
     qs[t] = static_cast<int8_t>(q);
+    if (dst.qs_f16 != nullptr) dst.qs_f16[t] = int_to_half_bits(q);
     // bsums: 16 consecutive values -> half-warp segments
     int s = q;
 #pragma unroll
     for (int o = 8; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-    if ((t & 15) == 0) bsums[t >> 4] = static_cast<int16_t>(s);
-    if (t == 0) *d = dval;
+    if ((t & 15) == 0) {
+        bsums[t >> 4] = static_cast<int16_t>(s);
+        if (dst.bsums_f16 != nullptr) dst.bsums_f16[t >> 4] = int_to_half_bits(s);
+    }
+    if (t == 0) {
+        *d = dval;
+        if (dst.d_t != nullptr) *dst.d_t = dval;
+    }
     __syncthreads();  // shared_keys / winner_value reuse safety
 }
 
@@ -171,12 +225,15 @@ __device__ __forceinline__ void q8k_block_256(float x, int8_t * qs, float * d, i
 // elements 8l..8l+7 in v[]. Identical arithmetic to q8k_block_256 (the amax
 // key picks the signed value of largest magnitude, first on ties), with
 // shuffles only, so any number of warps of a CTA quantize blocks
-// independently. qs must be 8-byte aligned.
+// independently. qs must be 8-byte aligned and qs_f16 16-byte aligned.
 struct Vals8 {
     float v[8];
 };
 
-__device__ __forceinline__ void q8k_block_warp(const Vals8 vals, int8_t * qs, float * d, int16_t * bsums) {
+__device__ __forceinline__ void q8k_block_warp(const Vals8 vals, const Q8Dest & dst) {
+    int8_t * qs = dst.qs;
+    float * d = dst.d;
+    int16_t * bsums = dst.bsums;
     const int lane = threadIdx.x & 31;
     unsigned long long key = 0;
 #pragma unroll
@@ -215,9 +272,23 @@ __device__ __forceinline__ void q8k_block_warp(const Vals8 vals, int8_t * qs, fl
 #pragma unroll
     for (int j = 0; j < 8; ++j) s += q[j];
     *reinterpret_cast<uint2 *>(qs + 8 * lane) = make_uint2(lo, hi);
+    if (dst.qs_f16 != nullptr) {
+        uint32_t h[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            h[j] = uint32_t(int_to_half_bits(q[2 * j])) | (uint32_t(int_to_half_bits(q[2 * j + 1])) << 16);
+        }
+        *reinterpret_cast<uint4 *>(dst.qs_f16 + 8 * lane) = make_uint4(h[0], h[1], h[2], h[3]);
+    }
     s += __shfl_xor_sync(0xffffffffu, s, 1);  // 16-value group = lanes 2g, 2g + 1
-    if ((lane & 1) == 0) bsums[lane >> 1] = static_cast<int16_t>(s);
-    if (lane == 0) *d = dval;
+    if ((lane & 1) == 0) {
+        bsums[lane >> 1] = static_cast<int16_t>(s);
+        if (dst.bsums_f16 != nullptr) dst.bsums_f16[lane >> 1] = int_to_half_bits(s);
+    }
+    if (lane == 0) {
+        *d = dval;
+        if (dst.d_t != nullptr) *dst.d_t = dval;
+    }
 }
 
 }  // namespace jfb

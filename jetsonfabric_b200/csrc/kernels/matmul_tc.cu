@@ -23,42 +23,48 @@
 //   Q2_K  A = scale*code <= 15*3 = 45: one accumulator.
 //   mins  One K = 16 MMA per block of the mins (<= 63) with the Q8_K partial
 //         sums (|bsum| <= 16*127): at most 16*63*2032 < 2^24.
-// The epilogue rounds every block term exactly as the CPU does and adds it to
-// a per-(row, token) double sum, as the CUDA-core kernel does.
+// The epilogue rounds every block term exactly as the CPU does (the products
+// with packed f32x2 multiplies, which round each lane like the scalar ones,
+// the final difference with scalar non-contractible subtractions) and adds it
+// to a per-(row, token) double sum, as the CUDA-core kernel does.
+//
+// Operands. The quantizers of this library also write the Q8_K codes and
+// 16-value partial sums as f16 numbers and the block scales d transposed
+// (jfb_q8k.qs_f16, bsums_f16, d_t). The activation operand therefore arrives
+// by TMA already in the tensor cores' layout and is never converted here: the
+// codes as 128-byte swizzled K-major boxes (SWIZZLE_128B, 64 codes per row),
+// the partial sums as two 8-wide no-swizzle boxes that form the canonical
+// K-major core-matrix layout, and each unit's activation scales as one row of
+// d_t. Only the weights are converted: every weight code becomes its exact
+// f16 product in tensor memory (the A operand, lane = weight row).
 //
 // Schedule. Persistent stream-K: grid G = min(SMs, W) and CTA c walks the
 // contiguous work range [c*W/G, (c+1)*W/G) of W = tiles * blocks units. A tile
-// is 128 weight rows x 32 activation rows; a unit is one 256-block of K. When
-// a tile's K range spans several CTAs, each epilogue warp writes its double
-// partials and the last warp to arrive (a per-tile, per-warp counter) adds
-// all contributors' partials in CTA order, so the result does not depend on
-// timing and no CTA ever waits for another.
+// is 128 weight rows x BN activation rows (BN = 32 for n <= 32, else 64); a
+// unit is one 256-block of K. When a tile's K range spans several CTAs, each
+// epilogue warp writes its double partials and the last warp to arrive (a
+// per-tile, per-warp counter) adds all contributors' partials in CTA order, so
+// the result does not depend on timing and no CTA ever waits for another.
 //
-// Warp roles (18 warps, 576 threads):
-//   warps 0-7   epilogue: warp w owns TMEM lanes 32(w % 4)..+31 (weight rows)
-//               and token columns 16(w / 4)..+15;
-//   warps 8-15  converters: per stage (half a block, 128 K values) thread
-//               (m, part) turns 64 raw values of weight row m into f16
-//               products and writes them to tensor memory (tcgen05.st): the A
-//               operand lives in TMEM (lane = weight row, each 32-bit column
-//               a pair of consecutive K values), so it never takes shared
-//               memory bandwidth. All converters also turn the activation
-//               codes (and, once per block, the mins and partial sums) into
-//               f16 B tiles in shared memory, in the canonical no-swizzle
-//               K-major layout (core matrices of 8 rows x 16 bytes; LBO = 128 B
-//               between the two K-halves of one 16-wide MMA step, SBO between
-//               8-row groups);
-//   warp 16     TMEM allocation and the single-thread tcgen05.mma issue;
-//   warp 17     one thread issuing the 2D TMA loads (cp.async.bulk.tensor, no
-//               multicast) of the raw weight rows, activation codes and
-//               partial sums into a ring of raw stages, several stages ahead
-//               of the converters, completing on mbarrier transaction counts.
-// Accumulators are double-buffered in TMEM, so the MMAs of block i+1 overlap
-// the epilogue of block i. The epilogue stages its per-block scales (weight
-// d/dmin of its row, activation d of its lane's token) with cp.async several
-// blocks ahead. Every mbarrier wait is bounded by a 2 s
-// global-timer limit: on expiry the kernel records an error code, every role
-// stops, in-flight MMAs and TMA loads are drained and TMEM is released.
+// Warp roles (BN = 32: 18 warps; BN = 64: 14 warps):
+//   epilogue    8 warps: warp w owns TMEM lanes 32(w % 4)..+31 (weight rows)
+//               and token columns (BN/2)(w / 4)..+BN/2-1;
+//   converters  8 warps for BN = 32 (two threads per weight row, 64 values
+//               each per half-block), 4 for BN = 64 (one thread per row):
+//               weight codes -> exact f16 products in TMEM (tcgen05.st), the
+//               mins -> a K = 16 shared-memory tile, and each row's block
+//               scale word -> the epilogue ring;
+//   MMA         one thread: TMEM allocation and the tcgen05.mma chain of each
+//               half-block; its commits free the A stage, the raw stage (which
+//               holds B) and hand the accumulator to the epilogue;
+//   TMA         one thread: the 2D loads (cp.async.bulk.tensor, no multicast)
+//               of the raw stages (weights, scale bytes, f16 codes, f16
+//               partial sums) and of each unit's activation scales, several
+//               units ahead, completing on mbarrier transaction counts.
+// Accumulators are double-buffered in TMEM, so the MMAs of unit i+1 overlap
+// the epilogue of unit i. Every mbarrier wait is bounded by a 2 s global-timer
+// limit: on expiry the kernel records an error code, every role stops,
+// in-flight MMAs and TMA loads are drained and TMEM is released.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -73,25 +79,19 @@
 namespace jfb {
 namespace {
 
-constexpr int kThreads = 576;
-constexpr int kEpilogueThreads = 256;   // warps 0-7
-constexpr int kEpilogueWarps = 8;
-constexpr int kConverterThreads = 256;  // warps 8-15
-constexpr int kMmaWarp = 16;
-constexpr int kTmaWarp = 17;
 constexpr int kRows = 128;             // MMA M: weight rows per tile
-constexpr int kBN = 32;                // MMA N: activation rows per tile
-constexpr int kKStage = 128;           // K values per pipeline stage
-constexpr uint32_t kSbo = 2048;        // 8-row group stride of a 128-wide K tile
-constexpr uint32_t kSbo16 = 256;       // same for the K = 16 mins tiles
-constexpr uint32_t kBBytes = kBN * kKStage * 2;       // 8 KB
+constexpr int kKStage = 128;           // K values per pipeline stage (half a block)
+constexpr uint32_t kSbo16 = 256;       // 8-row group stride of the K = 16 mins tile
 constexpr uint32_t kA2Bytes = kRows * 16 * 2;         // 4 KB
-constexpr uint32_t kB2Bytes = kBN * 16 * 2;           // 1 KB
 constexpr uint32_t kMaxSmem = 232448;                 // sm_100 opt-in limit per block
-constexpr uint32_t kTailBytes = 1024;                 // barriers, TMEM slot, flags, activation scales
-constexpr uint64_t kWaitNs = 2000000000ull;            // bound of every pipeline wait
-constexpr uint32_t kSuspendNs = 1000000;               // longest single suspension of a waiting thread
-constexpr uint32_t kSlotDoubles = kRows * kBN;        // one partial tile
+constexpr uint32_t kTailBytes = 1024;                 // barriers, TMEM slot, flags
+constexpr uint64_t kWaitNs = 2000000000ull;           // bound of every pipeline wait
+constexpr uint32_t kSuspendNs = 1000000;              // longest single suspension of a waiting thread
+constexpr uint32_t kTmemCols = 512;                   // one CTA per SM owns all of TMEM
+constexpr int kEpiRing = 4;                           // units of epilogue scales staged ahead
+constexpr uint32_t kEpiSlotBytes = 1024;              // [128] weight scale words, then [BN] activation d
+constexpr uint32_t kEpiDaOff = 512;
+constexpr int kMaxBN = 64;
 
 enum : int {
     kErrWaitEmpty = 1,
@@ -100,11 +100,13 @@ enum : int {
     kErrWaitAccFull = 4,
     kErrWaitRawEmpty = 5,
     kErrWaitRawFull = 6,
+    kErrWaitEpiEmpty = 7,
+    kErrWaitEpiFull = 8,
+    kErrSmemAlign = 9,
 };
 
-// Raw stage (TMA destination, per half-block): the weight boxes W0 (and W1)
-// of 128 rows, the scale/header box of 128 x 16 bytes, the activation codes
-// (32 x 128 bytes) and, for types with mins, the Q8_K partial sums (32 x 32).
+// Per type: A planes (Q6_K: hi and lo), accumulators per unit, raw weight
+// bytes per row and half-block (W0, W1) and plane-0 bytes per block.
 template <uint32_t TYPE>
 struct TypeTraits;
 template <>
@@ -112,7 +114,7 @@ struct TypeTraits<JF_TENSOR_Q4_K> {
     static constexpr int kPlanes = 1, kAcc = 3;  // D(half 0), D(half 1), mins
     static constexpr bool kMins = true;
     static constexpr uint32_t kW0 = 64, kW1 = 0;  // bytes per row: codes of the half-block
-    static constexpr uint32_t kBlockBytes = 128;  // plane-0 bytes per block
+    static constexpr uint32_t kBlockBytes = 128;
 };
 template <>
 struct TypeTraits<JF_TENSOR_Q6_K> {
@@ -129,53 +131,56 @@ struct TypeTraits<JF_TENSOR_Q2_K> {
     static constexpr uint32_t kBlockBytes = 64;
 };
 
-template <uint32_t TYPE>
-struct RawLayout {
-    using T = TypeTraits<TYPE>;
-    static constexpr uint32_t kW0Off = 0;
-    static constexpr uint32_t kW1Off = kW0Off + kRows * T::kW0;
-    static constexpr uint32_t kScOff = kW1Off + kRows * T::kW1;
-    static constexpr uint32_t kActOff = kScOff + kRows * 16;
-    static constexpr uint32_t kBsOff = kActOff + kBN * 128;
-    static constexpr uint32_t kBytes = kBsOff + (T::kMins ? kBN * 32 : 0);  // also the TMA transaction size
+// Warp roles for BN activation rows per tile.
+template <int BN>
+struct Roles {
+    static constexpr int kEpiWarps = 8;       // 4 TMEM lane quarters x 2 column halves
+    static constexpr int kCols = BN / 2;      // token columns per epilogue thread
+    static constexpr int kConvWarps = BN == 32 ? 8 : 4;
+    static constexpr int kConvThreads = kConvWarps * 32;
+    static constexpr int kParts = kConvThreads / kRows;  // converter threads per weight row
+    static constexpr int kScaleWriterWarps = 4;          // the part-0 converter warps
+    static constexpr int kMmaWarp = kEpiWarps + kConvWarps;
+    static constexpr int kTmaWarp = kMmaWarp + 1;
+    static constexpr int kWarps = kTmaWarp + 1;
+    static constexpr int kThreads = kWarps * 32;
+    // registers per thread: each of the SM's 4 sub-partitions has 16 K
+    // registers for the warps w with w % 4 == its index, allocated in
+    // multiples of 8 per thread
+    static constexpr int kRegs = (16384 / (((kWarps + 3) / 4) * 32)) / 8 * 8;
+    static constexpr uint32_t kSlotDoubles = uint32_t(kRows) * BN;  // one partial tile
 };
 
-// Operand stage in shared memory: the f16 B tile (activation codes) and, for
-// types with mins, the K = 16 mins (A2) and partial-sum (B2) tiles. The A
-// operand of a stage lives in TMEM.
-template <uint32_t TYPE>
-__host__ __device__ constexpr uint32_t stage_bytes() {
-    return kBBytes + (TypeTraits<TYPE>::kMins ? kA2Bytes + kB2Bytes : 0);
-}
-template <uint32_t TYPE>
-__host__ __device__ constexpr uint32_t acc_columns() {  // both accumulator buffers
-    return 2 * TypeTraits<TYPE>::kAcc * kBN;
-}
-template <uint32_t TYPE>
-__host__ __device__ constexpr uint32_t a_columns() {  // one stage of A: 64 columns per plane
-    return TypeTraits<TYPE>::kPlanes * (kKStage / 2);
-}
-// Operand stages: as many A stages as fit next to the accumulators in the
-// 512 TMEM columns, at most 4.
-template <uint32_t TYPE>
-__host__ __device__ constexpr int stage_count() {
-    return int((512 - acc_columns<TYPE>()) / a_columns<TYPE>()) < 4 ? int((512 - acc_columns<TYPE>()) / a_columns<TYPE>())
-                                                                      : 4;
-}
-constexpr int kScaleRing = 4;  // blocks of epilogue scales staged ahead
-constexpr uint32_t kScaleBytes = kEpilogueWarps * kScaleRing * (32 + 32) * 4;
-template <uint32_t TYPE>
-__host__ __device__ constexpr int raw_count() {
-    return int((kMaxSmem - kTailBytes - kScaleBytes - stage_count<TYPE>() * stage_bytes<TYPE>()) / RawLayout<TYPE>::kBytes) < 10
-               ? int((kMaxSmem - kTailBytes - kScaleBytes - stage_count<TYPE>() * stage_bytes<TYPE>()) / RawLayout<TYPE>::kBytes)
-               : 10;
-}
-template <uint32_t TYPE>
-__host__ __device__ constexpr uint32_t smem_bytes() {
-    return stage_count<TYPE>() * stage_bytes<TYPE>() + raw_count<TYPE>() * RawLayout<TYPE>::kBytes + kScaleBytes +
-           kTailBytes;
-}
-constexpr uint32_t kTmemCols = 512;  // one CTA per SM owns all of TMEM
+// Shared and tensor memory of one (type, BN):
+//   raw stage (one TMA transaction per half-block): the f16 codes as two
+//   swizzled 64-code boxes [BN][128 B], the weight boxes W0 (and W1) of 128
+//   rows, the scale/header box [128][16 B] and, for types with mins in half 0,
+//   the f16 partial sums as two boxes [BN][16 B];
+//   operand stage: the K = 16 mins tile of A (types with mins);
+//   epilogue ring: per unit the weight rows' scale words and the activation d.
+template <uint32_t TYPE, int BN>
+struct Layout {
+    using T = TypeTraits<TYPE>;
+    static constexpr uint32_t kBOff = 0;
+    static constexpr uint32_t kBHalf = uint32_t(BN) * 128;
+    static constexpr uint32_t kW0Off = 2 * kBHalf;
+    static constexpr uint32_t kW1Off = kW0Off + kRows * T::kW0;
+    static constexpr uint32_t kScOff = kW1Off + kRows * T::kW1;
+    static constexpr uint32_t kB2Off = kScOff + kRows * 16;
+    static constexpr uint32_t kB2Bytes = T::kMins ? uint32_t(BN) * 32 : 0;
+    static constexpr uint32_t kTx0 = kB2Off + kB2Bytes;  // transaction bytes of half 0
+    static constexpr uint32_t kTx1 = kB2Off;             // half 1 (no partial sums)
+    static constexpr uint32_t kRawBytes = (kTx0 + 1023) / 1024 * 1024;
+    static constexpr uint32_t kAccCols = 2 * T::kAcc * uint32_t(BN);  // both accumulator buffers
+    static constexpr uint32_t kACols = T::kPlanes * (kKStage / 2);    // one A stage: 64 columns per plane
+    static constexpr int kNsFit = int((kTmemCols - kAccCols) / kACols);
+    static constexpr int NS = kNsFit < 4 ? kNsFit : 4;
+    static constexpr uint32_t kOpBytes = T::kMins ? kA2Bytes : 0;
+    static constexpr uint32_t kFixed = uint32_t(NS) * kOpBytes + kEpiRing * kEpiSlotBytes + kTailBytes;
+    static constexpr int kNrFit = int((kMaxSmem - kFixed) / kRawBytes);
+    static constexpr int NR = kNrFit < 12 ? kNrFit : 12;
+    static constexpr uint32_t kSmem = uint32_t(NR) * kRawBytes + kFixed;
+};
 
 // ---- PTX wrappers -------------------------------------------------------------
 
@@ -274,6 +279,21 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint3
     return d;
 }
 
+// K-major operand in the 128-byte swizzled layout that a SWIZZLE_128B TMA
+// box writes (rows of 64 f16 = 128 bytes, 16-byte chunk c of row r stored at
+// chunk c ^ (r % 8), 8-row groups 1024 bytes apart). The atom must be
+// 1024-byte aligned; a K step of 16 values inside it advances the start
+// address by 32 bytes. Layout type 2 (bits 61-63) is SWIZZLE_128B.
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
+    uint64_t d = 0;
+    d |= uint64_t((addr & 0x3FFFF) >> 4);
+    d |= uint64_t(1) << 16;          // leading byte offset: unused for swizzled K-major
+    d |= uint64_t(1024 >> 4) << 32;  // stride byte offset: 8 rows x 128 bytes
+    d |= uint64_t(1) << 46;
+    d |= uint64_t(2) << 61;
+    return d;
+}
+
 // Instruction descriptor of kind::f16: D = f32, A = B = f16, both K-major.
 __host__ __device__ constexpr uint32_t instr_desc(uint32_t m, uint32_t n) {
     return (1u << 4) | ((n >> 3) << 17) | ((m >> 4) << 24);
@@ -310,16 +330,6 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t * v) {
 }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
-// 4-byte asynchronous global -> shared copy (completes at cp_async_wait).
-__device__ __forceinline__ void cp_async4(void * dst, const void * src) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-
 __device__ __forceinline__ void mma_commit(uint64_t * bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                  : "memory");
@@ -351,8 +361,6 @@ __device__ __forceinline__ uint2 scaled4(uint32_t w, __half2 scale, __half2 nbia
     return make_uint2(h2_bits(lo), h2_bits(hi));
 }
 
-__device__ __forceinline__ __half2 h2_int(int v) { return __half2half2(__int2half_rn(v)); }
-
 // f16 pair (V, V) of an exactly representable integer constant.
 template <int V>
 __device__ __forceinline__ __half2 h2_int_const() {
@@ -360,34 +368,15 @@ __device__ __forceinline__ __half2 h2_int_const() {
     return __float2half2_rn(f);
 }
 
-__device__ __forceinline__ uint32_t byte_at(const uint4 & v, int i) {
-    const uint32_t w = i < 4 ? v.x : i < 8 ? v.y : i < 12 ? v.z : v.w;
-    return (w >> (8 * (i & 3))) & 0xffu;
-}
-
-// 6-bit scale and min of Q4_K sub-block j from the 12 packed bytes at hdr[4..16).
-__device__ __forceinline__ void q4k_scale_min_hdr(const uint4 & hdr, int j, int & sc, int & m) {
-    auto s = [&](int k) { return int(byte_at(hdr, 4 + k)); };
-    if (j < 4) {
-        sc = s(j) & 63;
-        m = s(j + 4) & 63;
-    } else {
-        sc = (s(j + 4) & 0x0f) | ((s(j - 4) >> 6) << 4);
-        m = (s(j + 4) >> 4) | ((s(j) >> 6) << 4);
-    }
-}
-
 // Tensor maps of one launch: weight boxes W0/W1 and the scale box (128 rows
-// each), the activation codes (32 x 128 bytes) and partial sums (32 x 32).
+// each), the f16 codes (64 x BN, 128-byte swizzle), the f16 partial sums
+// (8 x BN) and the transposed activation scales (BN x 1).
 struct TcMaps {
-    CUtensorMap w0, w1, sc, act, bsums;
+    CUtensorMap w0, w1, sc, qs, b2, dt;
 };
 
 struct TcParams {
     jfb_weight w;
-    const int8_t * qs;      // Q8_K codes [n][cols]
-    const float * da;       // [n][blocks]
-    const int16_t * bsums;  // [n][cols/16]
     uint32_t n;
     uint32_t blocks;        // cols / 256
     uint32_t tiles_m;
@@ -400,8 +389,8 @@ struct TcParams {
     const float * seg_bias[JFB_MATMUL_MAX_SEGMENTS];
     const float * seg_residual[JFB_MATMUL_MAX_SEGMENTS];
     float * seg_out[JFB_MATMUL_MAX_SEGMENTS];
-    double * partial;       // [2 * gridDim.x][kBN][kRows]
-    uint32_t * counters;    // [tiles][kEpilogueWarps]
+    double * partial;       // [2 * gridDim.x][BN][kRows]
+    uint32_t * counters;    // [tiles][epilogue warps]
     int * error;
 };
 
@@ -458,9 +447,8 @@ __device__ __forceinline__ uint32_t scale_word(const uint4 & scv, int h, int par
 // values per 32-bit column. h and part only move byte offsets and shift
 // amounts, so every register-array index below is a compile-time constant and
 // one body serves all four (h, part) cases. Warp-collective (tcgen05.st).
-template <uint32_t TYPE>
+template <uint32_t TYPE, class RL>
 __device__ __forceinline__ void convert_a(const uint8_t * r, int h, int part, uint32_t a_col, int m) {
-    using RL = RawLayout<TYPE>;
     const uint4 scv = *reinterpret_cast<const uint4 *>(r + RL::kScOff + m * 16);
     const uint32_t col = a_col + 32 * part;
     if constexpr (TYPE == JF_TENSOR_Q4_K) {
@@ -583,9 +571,9 @@ __device__ __forceinline__ void convert_a(const uint8_t * r, int h, int part, ui
 // K = 16 f16 operand row (Q4_K: the 6-bit min of each 32-value sub-block,
 // twice; Q2_K: the high nibble of each scale byte), from the raw scale row of
 // tile row m. The two parts of a row write the two 16-byte core columns.
-template <uint32_t TYPE>
+template <uint32_t TYPE, class RL>
 __device__ __forceinline__ void convert_mins(const uint8_t * r, int part, uint8_t * tile, int m) {
-    const uint4 meta = *reinterpret_cast<const uint4 *>(r + RawLayout<TYPE>::kScOff + m * 16);
+    const uint4 meta = *reinterpret_cast<const uint4 *>(r + RL::kScOff + m * 16);
     uint32_t h2[4];
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
@@ -609,30 +597,56 @@ __device__ __forceinline__ void convert_mins(const uint8_t * r, int part, uint8_
     *reinterpret_cast<uint4 *>(tile + (m >> 3) * kSbo16 + part * 128 + (m & 7) * 16) = make_uint4(h2[0], h2[1], h2[2], h2[3]);
 }
 
-template <uint32_t TYPE>
-__global__ void __launch_bounds__(kThreads, 1) mmq_tc_kernel(const __grid_constant__ TcMaps maps, TcParams p) {
+// Packed f32x2 arithmetic (sm_100): each lane is rounded exactly as the
+// scalar __fmul_rn / __fadd_rn / __fmaf_rn would round it. A packed product
+// that feeds an addition can still be fused with it by the compiler (measured:
+// the __fmul2_rn / __fadd2_rn intrinsics are), so every rounding-sensitive
+// difference of two products below is a scalar __fsub_rn, which never is.
+__device__ __forceinline__ float2 f2(float a, float b) { return make_float2(a, b); }
+
+__device__ __forceinline__ float2 mul2_rn(float2 a, float2 b) {
+    float2 d;
+    asm("{\n\t.reg .b64 a, b, d;\n\tmov.b64 a, {%2, %3};\n\tmov.b64 b, {%4, %5};\n\t"
+        "mul.rn.f32x2 d, a, b;\n\tmov.b64 {%0, %1}, d;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
+}
+
+__device__ __forceinline__ float2 fma2_rn(float2 a, float2 b, float2 c) {
+    float2 d;
+    asm("{\n\t.reg .b64 a, b, c, d;\n\tmov.b64 a, {%2, %3};\n\tmov.b64 b, {%4, %5};\n\t"
+        "mov.b64 c, {%6, %7};\n\tfma.rn.f32x2 d, a, b, c;\n\tmov.b64 {%0, %1}, d;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+    return d;
+}
+
+template <uint32_t TYPE, int BN>
+__global__ void __launch_bounds__(Roles<BN>::kThreads) __maxnreg__(Roles<BN>::kRegs) mmq_tc_kernel(const __grid_constant__ TcMaps maps, TcParams p) {
     using T = TypeTraits<TYPE>;
-    using RL = RawLayout<TYPE>;
-    constexpr int NS = stage_count<TYPE>();
-    constexpr int NR = raw_count<TYPE>();
-    constexpr uint32_t kStage = stage_bytes<TYPE>();
-    constexpr uint32_t kBOff = 0;
-    constexpr uint32_t kA2Off = kBOff + kBBytes;
-    constexpr uint32_t kB2Off = kA2Off + kA2Bytes;
-    constexpr uint32_t kAccCols = acc_columns<TYPE>();
-    constexpr uint32_t kACols = a_columns<TYPE>();
+    using L = Layout<TYPE, BN>;
+    using R = Roles<BN>;
+    constexpr int NS = L::NS;
+    constexpr int NR = L::NR;
+    constexpr uint32_t kAccCols = L::kAccCols;
+    constexpr uint32_t kACols = L::kACols;
 
     extern __shared__ __align__(1024) uint8_t smem[];
-    uint8_t * raw = smem + NS * kStage;                    // [NR][RL::kBytes]
-    uint8_t * scales = raw + NR * RL::kBytes;              // epilogue scale rings
-    uint8_t * tail = scales + kScaleBytes;
-    uint64_t * full = reinterpret_cast<uint64_t *>(tail);  // [NS]
-    uint64_t * empty = full + NS;                          // [NS]
-    uint64_t * raw_full = empty + NS;                      // [NR]
-    uint64_t * raw_empty = raw_full + NR;                  // [NR]
+    uint8_t * raw = smem;                                   // [NR][kRawBytes], 1024-byte aligned
+    uint8_t * ops = raw + NR * L::kRawBytes;                // [NS][kOpBytes]
+    uint8_t * ering = ops + NS * L::kOpBytes;               // [kEpiRing][kEpiSlotBytes]
+    uint8_t * tail = ering + kEpiRing * kEpiSlotBytes;
+    uint64_t * full = reinterpret_cast<uint64_t *>(tail);  // [NS] A stage written (converters)
+    uint64_t * empty = full + NS;                          // [NS] A stage consumed (MMA commit)
+    uint64_t * raw_full = empty + NS;                      // [NR] TMA landed
+    uint64_t * raw_empty = raw_full + NR;                  // [NR] converters + MMA done with it
     uint64_t * acc_full = raw_empty + NR;                  // [2]
     uint64_t * acc_empty = acc_full + 2;                   // [2]
-    uint64_t * drain = acc_empty + 2;                      // [1]
+    uint64_t * epi_full = acc_empty + 2;                   // [kEpiRing] weight scale words (converters)
+    uint64_t * epi_tx = epi_full + kEpiRing;               // [kEpiRing] activation d landed (TMA)
+    uint64_t * epi_empty = epi_tx + kEpiRing;              // [kEpiRing]
+    uint64_t * drain = epi_empty + kEpiRing;               // [1]
     uint32_t * tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
     volatile int * abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
@@ -644,22 +658,30 @@ __global__ void __launch_bounds__(kThreads, 1) mmq_tc_kernel(const __grid_consta
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < NS; ++s) {
-            mbar_init(&full[s], kConverterThreads);
+            mbar_init(&full[s], R::kConvWarps);
             mbar_init(&empty[s], 1);
         }
         for (int s = 0; s < NR; ++s) {
             mbar_init(&raw_full[s], 1);
-            mbar_init(&raw_empty[s], kConverterThreads);
+            mbar_init(&raw_empty[s], R::kConvWarps + 1);
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(&acc_full[a], 1);
-            mbar_init(&acc_empty[a], kEpilogueThreads);
+            mbar_init(&acc_empty[a], R::kEpiWarps);
+        }
+        for (int e = 0; e < kEpiRing; ++e) {
+            mbar_init(&epi_full[e], R::kScaleWriterWarps);
+            mbar_init(&epi_tx[e], 1);
+            mbar_init(&epi_empty[e], R::kEpiWarps);
         }
         mbar_init(drain, 1);
-        *abort_flag = 0;
+        // the swizzled boxes need a 1024-byte aligned ring; stop before any load otherwise
+        const bool aligned = (smem_u32(smem) & 1023u) == 0;
+        *abort_flag = aligned ? 0 : 1;
+        if (!aligned && p.error != nullptr) *reinterpret_cast<volatile int *>(p.error) = kErrSmemAlign;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    if (warp == kMmaWarp) {
+    if (warp == R::kMmaWarp) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                      "r"(kTmemCols));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
@@ -669,32 +691,49 @@ __global__ void __launch_bounds__(kThreads, 1) mmq_tc_kernel(const __grid_consta
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp == kTmaWarp) {
-        // ---------------- TMA loads of the raw stages (one thread) ----------------
+    if (warp == R::kTmaWarp) {
+        // ---------------- TMA loads (one thread) ----------------
         if (lane == 0) {
-            uint32_t rs = 0, rph = 0;
-            uint64_t issued = 0;
+            uint32_t rs = 0, rph = 0, es = 0, eph = 0;
+            uint64_t issued = 0, e_issued = 0;
             bool ok = true;
             Cursor cur;
             cur.init(w_begin, nb, p.tiles_m);
             for (uint64_t w = w_begin; w < w_end && ok && !*abort_flag; ++w, cur.next(nb, p.tiles_m)) {
                 const uint32_t b = cur.b;
-                const int32_t y_w = int32_t(cur.tm * kRows), y_a = int32_t(cur.tn * kBN);
+                const int32_t y_w = int32_t(cur.tm * kRows), y_a = int32_t(cur.tn * BN);
+                // the unit's activation scales d[tokens][b] (one row of d_t)
+                if (!mbar_wait(&epi_empty[es], eph ^ 1u, abort_flag, p.error, kErrWaitEpiEmpty)) break;
+                mbar_arrive_expect_tx(&epi_tx[es], uint32_t(BN) * 4);
+                tma_load_2d(ering + es * kEpiSlotBytes + kEpiDaOff, &maps.dt, y_a, int32_t(b), &epi_tx[es]);
+                ++e_issued;
+                if (++es == kEpiRing) {
+                    es = 0;
+                    eph ^= 1u;
+                }
                 for (int h = 0; h < 2; ++h) {
                     if (!mbar_wait(&raw_empty[rs], rph ^ 1u, abort_flag, p.error, kErrWaitRawEmpty)) {
                         ok = false;
                         break;
                     }
-                    uint8_t * r = raw + rs * RL::kBytes;
-                    mbar_arrive_expect_tx(&raw_full[rs], RL::kBytes);
+                    uint8_t * r = raw + rs * L::kRawBytes;
+                    mbar_arrive_expect_tx(&raw_full[rs], h == 0 ? L::kTx0 : L::kTx1);
+                    // x coordinates: f16 elements (codes: multiples of 64; partial sums: of 8), bytes for the
+                    // weight planes (multiples of 16): all 16-byte aligned
+                    const int32_t x_codes = int32_t(b * kQK + 128 * h);
+                    tma_load_2d(r + L::kBOff, &maps.qs, x_codes, y_a, &raw_full[rs]);
+                    tma_load_2d(r + L::kBOff + L::kBHalf, &maps.qs, x_codes + 64, y_a, &raw_full[rs]);
                     const int32_t x_blk = int32_t(b * T::kBlockBytes);
-                    tma_load_2d(r + RL::kW0Off, &maps.w0, x_blk + int32_t(T::kW0 * h), y_w, &raw_full[rs]);
+                    tma_load_2d(r + L::kW0Off, &maps.w0, x_blk + int32_t(T::kW0 * h), y_w, &raw_full[rs]);
                     if constexpr (T::kW1 > 0) {
-                        tma_load_2d(r + RL::kW1Off, &maps.w1, x_blk + 128 + int32_t(T::kW1 * h), y_w, &raw_full[rs]);
+                        tma_load_2d(r + L::kW1Off, &maps.w1, x_blk + 128 + int32_t(T::kW1 * h), y_w, &raw_full[rs]);
                     }
-                    tma_load_2d(r + RL::kScOff, &maps.sc, int32_t(b * 16), y_w, &raw_full[rs]);
-                    tma_load_2d(r + RL::kActOff, &maps.act, int32_t(b * kQK + 128 * h), y_a, &raw_full[rs]);
-                    if constexpr (T::kMins) tma_load_2d(r + RL::kBsOff, &maps.bsums, int32_t(b * 32), y_a, &raw_full[rs]);
+                    tma_load_2d(r + L::kScOff, &maps.sc, int32_t(b * 16), y_w, &raw_full[rs]);
+                    if (T::kMins && h == 0) {
+                        tma_load_2d(r + L::kB2Off, &maps.b2, int32_t(b * 16), y_a, &raw_full[rs]);
+                        tma_load_2d(r + L::kB2Off + uint32_t(BN) * 16, &maps.b2, int32_t(b * 16 + 8), y_a,
+                                    &raw_full[rs]);
+                    }
                     ++issued;
                     if (++rs == NR) {
                         rs = 0;
@@ -703,25 +742,44 @@ __global__ void __launch_bounds__(kThreads, 1) mmq_tc_kernel(const __grid_consta
                 }
             }
             // a stopped kernel must not exit with loads still landing in its
-            // shared memory: wait (bounded) for the last issue of every stage
+            // shared memory: wait (bounded) for the last issue of every slot
             if (*abort_flag) {
                 volatile int no_abort = 0;
                 for (uint64_t j = issued > uint64_t(NR) ? issued - NR : 0; j < issued; ++j) {
                     (void) mbar_wait(&raw_full[j % NR], uint32_t((j / NR) & 1u), &no_abort, nullptr, 0);
                 }
+                for (uint64_t j = e_issued > uint64_t(kEpiRing) ? e_issued - kEpiRing : 0; j < e_issued; ++j) {
+                    (void) mbar_wait(&epi_tx[j % kEpiRing], uint32_t((j / kEpiRing) & 1u), &no_abort, nullptr, 0);
+                }
             }
         }
         __syncwarp();
-    } else if (warp >= kEpilogueWarps && warp < kMmaWarp) {
+    } else if (warp >= R::kEpiWarps && warp < R::kMmaWarp) {
         // ---------------- converters ----------------
-        const int pt = threadIdx.x - kEpilogueThreads;
-        const int m = pt & (kRows - 1), part = pt >> 7;  // part is uniform per warp
-        const uint32_t lane_base = uint32_t((warp & 3) * 32) << 16;  // this warp's TMEM lane quarter
-        const __half2 act_nbias = h2_int(-1152);  // codes arrive as q + 128 after the sign flip
-        const __half2 one = h2_int(1);
-        uint32_t stage = 0, phase = 0, rs = 0, rph = 0;
-        for (uint64_t w = w_begin; w < w_end; ++w) {
+        const int cw = warp - R::kEpiWarps;
+        const int quarter = warp & 3;                 // TMEM lane quarter of this warp
+        const int part = cw >> 2;                     // uniform per warp (always 0 with one thread per row)
+        const int m = quarter * 32 + lane;
+        const bool scale_writer = part == 0;
+        const uint32_t lane_base = uint32_t(quarter * 32) << 16;
+        const uint8_t * p2 = static_cast<const uint8_t *>(p.w.plane[2]);
+        uint32_t stage = 0, phase = 0, rs = 0, rph = 0, es = 0, eph = 0;
+        Cursor cur;
+        cur.init(w_begin, nb, p.tiles_m);
+        for (uint64_t w = w_begin; w < w_end; ++w, cur.next(nb, p.tiles_m)) {
             if (__any_sync(0xffffffffu, *abort_flag != 0)) break;
+            // the epilogue's weight scale word of this row and block: Q4_K takes
+            // it from the header bytes of the raw stage; Q6_K and Q2_K read
+            // plane 2 here, early, so the load overlaps the conversion
+            uint32_t dword = 0;
+            if constexpr (TYPE != JF_TENSOR_Q4_K) {
+                const uint32_t row = cur.tm * kRows + uint32_t(m);
+                if (scale_writer && row < p.w.rows) {
+                    const uint64_t block = uint64_t(row) * nb + cur.b;
+                    dword = TYPE == JF_TENSOR_Q6_K ? uint32_t(__ldg(reinterpret_cast<const uint16_t *>(p2) + block))
+                                                   : __ldg(reinterpret_cast<const uint32_t *>(p2) + block);
+                }
+            }
             bool ok = true;
             for (int h = 0; h < 2; ++h) {
                 // the whole warp proceeds or stops together (TMEM stores are warp-collective)
@@ -732,44 +790,44 @@ __global__ void __launch_bounds__(kThreads, 1) mmq_tc_kernel(const __grid_consta
                     break;
                 }
                 tc_fence_after();
-                const uint8_t * r = raw + rs * RL::kBytes;
-                uint8_t * st = smem + stage * kStage;
-                convert_a<TYPE>(r, h, part, tmem + lane_base + kAccCols + stage * kACols, m);
-                if (T::kMins && h == 0) convert_mins<TYPE>(r, part, st + kA2Off, m);
-                // activation codes: one token t and 16 codes (chunk pair c16) per
-                // thread. The raw tile arrives 128-byte swizzled (16-byte chunk c
-                // of token row t at chunk c ^ (t & 7)), so the 8 lanes that share
-                // c16 read 8 different bank groups; they also write 128
-                // contiguous bytes of the B tile.
-                {
-                    const int t_low = pt & 7, c16 = (pt >> 3) & 7, t = ((pt >> 6) << 3) | t_low;
-                    const uint4 v = *reinterpret_cast<const uint4 *>(r + RL::kActOff + t * 128 + ((c16 ^ t_low) << 4));
-                    const uint2 a = scaled4(v.x ^ 0x80808080u, one, act_nbias);
-                    const uint2 b = scaled4(v.y ^ 0x80808080u, one, act_nbias);
-                    const uint2 c = scaled4(v.z ^ 0x80808080u, one, act_nbias);
-                    const uint2 d = scaled4(v.w ^ 0x80808080u, one, act_nbias);
-                    uint8_t * dst = st + kBOff + (t >> 3) * kSbo + (2 * c16) * 128 + (t & 7) * 16;
-                    *reinterpret_cast<uint4 *>(dst) = make_uint4(a.x, a.y, b.x, b.y);
-                    *reinterpret_cast<uint4 *>(dst + 128) = make_uint4(c.x, c.y, d.x, d.y);
-                }
-                if (T::kMins && h == 0 && pt < kBN * 2) {
-                    const int t = pt >> 1, c = pt & 1;
-                    const uint4 v = *reinterpret_cast<const uint4 *>(r + RL::kBsOff + t * 32 + 16 * c);
-                    const uint32_t rw[4] = {v.x, v.y, v.z, v.w};
-                    uint32_t hv[4];
-#pragma unroll
-                    for (int k = 0; k < 4; ++k) {
-                        hv[k] = h2_bits(__halves2half2(__int2half_rn(int(int16_t(rw[k] & 0xffffu))),
-                                                       __int2half_rn(int(int16_t(rw[k] >> 16)))));
+                const uint8_t * r = raw + rs * L::kRawBytes;
+                const uint32_t a_col = tmem + lane_base + kAccCols + stage * kACols;
+                uint8_t * op = ops + stage * L::kOpBytes;
+                if constexpr (R::kParts == 2) {
+                    convert_a<TYPE, L>(r, h, part, a_col, m);
+                    if (T::kMins && h == 0) convert_mins<TYPE, L>(r, part, op, m);
+                } else {
+#pragma unroll 1
+                    for (int pt = 0; pt < 2; ++pt) {
+                        convert_a<TYPE, L>(r, h, pt, a_col, m);
+                        if (T::kMins && h == 0) convert_mins<TYPE, L>(r, pt, op, m);
                     }
-                    *reinterpret_cast<uint4 *>(st + kB2Off + (t >> 3) * kSbo16 + c * 128 + (t & 7) * 16) =
-                        make_uint4(hv[0], hv[1], hv[2], hv[3]);
+                }
+                if (h == 0) {
+                    if (scale_writer) {
+                        if constexpr (TYPE == JF_TENSOR_Q4_K) dword = *reinterpret_cast<const uint32_t *>(r + L::kScOff + m * 16);
+                        const bool free_slot = mbar_wait(&epi_empty[es], eph ^ 1u, abort_flag, p.error, kErrWaitEpiEmpty);
+                        if (!__all_sync(0xffffffffu, free_slot)) {
+                            ok = false;
+                            break;
+                        }
+                        reinterpret_cast<uint32_t *>(ering + es * kEpiSlotBytes)[m] = dword;
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&epi_full[es]);
+                    }
+                    if (++es == kEpiRing) {
+                        es = 0;
+                        eph ^= 1u;
+                    }
                 }
                 tmem_wait_st();
                 tc_fence_before();
-                fence_proxy_async();
-                mbar_arrive(&full[stage]);
-                mbar_arrive(&raw_empty[rs]);
+                if (T::kMins && h == 0) fence_proxy_async();  // the mins tile is read by the tensor cores
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(&full[stage]);
+                    mbar_arrive(&raw_empty[rs]);
+                }
                 if (++stage == NS) {
                     stage = 0;
                     phase ^= 1u;
@@ -781,46 +839,55 @@ __global__ void __launch_bounds__(kThreads, 1) mmq_tc_kernel(const __grid_consta
             }
             if (!ok) break;
         }
-    } else if (warp == kMmaWarp) {
+    } else if (warp == R::kMmaWarp) {
         // ---------------- MMA issue (one thread) ----------------
         if (lane == 0) {
-            constexpr uint32_t idesc = instr_desc(kRows, kBN);
-            uint32_t stage = 0, phase = 0, i = 0;
+            constexpr uint32_t idesc = instr_desc(kRows, BN);
+            uint32_t stage = 0, phase = 0, rs = 0, rph = 0, i = 0;
             bool ok = true;
             for (uint64_t w = w_begin; w < w_end && ok && !*abort_flag; ++w, ++i) {
                 const uint32_t acc = i & 1u, use = i >> 1;
                 if (!mbar_wait(&acc_empty[acc], (use & 1u) ^ 1u, abort_flag, p.error, kErrWaitAccEmpty)) break;
                 tc_fence_after();
-                const uint32_t d = tmem + acc * (T::kAcc * kBN);
+                const uint32_t d = tmem + acc * (T::kAcc * BN);
                 for (int h = 0; h < 2; ++h) {
-                    if (!mbar_wait(&full[stage], phase, abort_flag, p.error, kErrWaitFull)) {
+                    if (!mbar_wait(&full[stage], phase, abort_flag, p.error, kErrWaitFull) ||
+                        !mbar_wait(&raw_full[rs], rph, abort_flag, p.error, kErrWaitRawFull)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t st = smem_u32(smem + stage * kStage);
+                    const uint32_t braw = smem_u32(raw + rs * L::kRawBytes);
                     const uint32_t a = tmem + kAccCols + stage * kACols;
 #pragma unroll
                     for (int ks = 0; ks < kKStage / 16; ++ks) {
-                        const uint64_t bdesc = smem_desc(st + kBOff + ks * 256, 128, kSbo);
+                        const uint64_t bdesc =
+                            smem_desc_sw128(braw + L::kBOff + uint32_t(ks >> 2) * L::kBHalf + uint32_t(ks & 3) * 32);
                         if constexpr (TYPE == JF_TENSOR_Q4_K) {
-                            mma_f16_ts(d + h * kBN, a + ks * 8, bdesc, idesc, ks > 0 ? 1u : 0u);
+                            mma_f16_ts(d + h * BN, a + ks * 8, bdesc, idesc, ks > 0 ? 1u : 0u);
                         } else if constexpr (TYPE == JF_TENSOR_Q6_K) {
                             const uint32_t accum = (h > 0 || ks > 0) ? 1u : 0u;
                             mma_f16_ts(d, a + ks * 8, bdesc, idesc, accum);
-                            mma_f16_ts(d + kBN, a + 64 + ks * 8, bdesc, idesc, accum);
+                            mma_f16_ts(d + BN, a + 64 + ks * 8, bdesc, idesc, accum);
                         } else {
                             mma_f16_ts(d, a + ks * 8, bdesc, idesc, (h > 0 || ks > 0) ? 1u : 0u);
                         }
                     }
                     if (T::kMins && h == 0) {
-                        mma_f16(d + (T::kAcc - 1) * kBN, smem_desc(st + kA2Off, 128, kSbo16),
-                                smem_desc(st + kB2Off, 128, kSbo16), idesc, 0u);
+                        // A2 [128 x 16]: core matrices 128 B apart along K, 8-row groups kSbo16 apart;
+                        // B2 [BN x 16]: the two 8-wide boxes BN*16 B apart, 8-row groups 128 B apart
+                        mma_f16(d + (T::kAcc - 1) * BN, smem_desc(smem_u32(ops + stage * L::kOpBytes), 128, kSbo16),
+                                smem_desc(braw + L::kB2Off, uint32_t(BN) * 16, 128), idesc, 0u);
                     }
-                    mma_commit(&empty[stage]);  // frees the stage once these MMAs are done
+                    mma_commit(&empty[stage]);   // the A stage is free once these MMAs are done
+                    mma_commit(&raw_empty[rs]);  // and so is the raw stage that holds B
                     if (++stage == NS) {
                         stage = 0;
                         phase ^= 1u;
+                    }
+                    if (++rs == NR) {
+                        rs = 0;
+                        rph ^= 1u;
                     }
                 }
                 if (ok) mma_commit(&acc_full[acc]);
@@ -832,111 +899,90 @@ __global__ void __launch_bounds__(kThreads, 1) mmq_tc_kernel(const __grid_consta
         }
         __syncwarp();
     } else {
-        // ---------------- epilogue (warps 0-3) ----------------
-        constexpr int kCols = kBN / 2;  // token columns of this thread
-        const int m = (warp & 3) * 32 + lane;  // TMEM lane quarter of the warp = its 32 weight rows
+        // ---------------- epilogue ----------------
+        constexpr int kCols = R::kCols;  // token columns of this thread
+        const int quarter = warp & 3;
+        const int m = quarter * 32 + lane;  // the warp's TMEM lane quarter = its 32 weight rows
         const int col0 = (warp >> 2) * kCols;
-        const uint32_t lane_base = uint32_t((warp & 3) * 32) << 16;
-        // scale rings of this warp: [kScaleRing][32] weight scale words (own row), [kScaleRing][32] activation d
-        uint32_t * dring = reinterpret_cast<uint32_t *>(scales) + warp * kScaleRing * 64;
-        float * aring = reinterpret_cast<float *>(dring + kScaleRing * 32);
-        const uint8_t * p1 = static_cast<const uint8_t *>(p.w.plane[1]);
-        const uint8_t * p2 = static_cast<const uint8_t *>(p.w.plane[2]);
+        const uint32_t lane_base = uint32_t(quarter * 32) << 16;
         const uint32_t first_tile = uint32_t(w_begin / nb);
-        Cursor ahead;  // the unit whose scales are staged next
-        ahead.init(w_begin, nb, p.tiles_m);
-        // stage unit w (at cursor `ahead`) into ring slot `slot` (one commit group per unit, possibly empty)
-        auto stage_scales = [&](uint64_t w, int slot) {
-            if (w < w_end) {
-                const uint32_t b = ahead.b;
-                const uint32_t row = ahead.tm * kRows + uint32_t(m), tok = ahead.tn * kBN + lane;
-                if (row < p.w.rows) {
-                    const uint64_t block = uint64_t(row) * nb + b;
-                    const uint8_t * src = TYPE == JF_TENSOR_Q4_K ? p1 + block * 16        // d | dmin << 16
-                                          : TYPE == JF_TENSOR_Q6_K ? p2 + ((block * 2) & ~uint64_t(3))  // word holding d
-                                                                   : p2 + block * 4;      // d | dmin << 16
-                    cp_async4(&dring[slot * 32 + lane], src);
-                } else {
-                    dring[slot * 32 + lane] = 0;
-                }
-                if (tok < p.n) cp_async4(&aring[slot * 32 + lane], p.da + uint64_t(tok) * nb + b);
-                else aring[slot * 32 + lane] = 0.0f;
-                ahead.next(nb, p.tiles_m);
-            }
-            cp_async_commit();
-        };
-#pragma unroll
-        for (int k = 0; k < kScaleRing; ++k) stage_scales(w_begin + k, k);
         double sum[kCols];
         uint64_t seg_begin = w_begin;
-        uint32_t i = 0;
+        uint32_t i = 0, es = 0, eph = 0;
         Cursor cur;
         cur.init(w_begin, nb, p.tiles_m);
         for (uint64_t w = w_begin; w < w_end; ++w, ++i, cur.next(nb, p.tiles_m)) {
             // warp-uniform stop: the warp collectives below need every lane
             if (__any_sync(0xffffffffu, *abort_flag != 0)) break;
             const uint32_t tile = cur.tile;
-            const uint32_t row = cur.tm * kRows + uint32_t(m), tok0 = cur.tn * kBN;
+            const uint32_t row = cur.tm * kRows + uint32_t(m), tok0 = cur.tn * BN;
             if (w == seg_begin) {
 #pragma unroll
                 for (int t = 0; t < kCols; ++t) sum[t] = 0.0;
             }
-            const int slot = int(i % kScaleRing);
-            cp_async_wait<kScaleRing - 1>();  // unit i's group is complete
-            __syncwarp();
-            float dw, dmin = 0.0f;
-            {
-                const uint32_t word = dring[slot * 32 + lane];
-                if constexpr (TYPE == JF_TENSOR_Q6_K) {
-                    const uint32_t odd = ((row & nb) + cur.b) & 1u;  // parity of block row * nb + b
-                    dw = half_bits_to_float(uint16_t(odd ? word >> 16 : word & 0xffffu));
-                } else {
-                    dw = half_bits_to_float(uint16_t(word & 0xffffu));
-                    dmin = half_bits_to_float(uint16_t(word >> 16));
-                }
-            }
-            const float * da_s = aring + slot * 32;
-
             const uint32_t acc = i & 1u, use = i >> 1;
             // the whole warp proceeds or stops together
-            const bool ready = mbar_wait(&acc_full[acc], use & 1u, abort_flag, p.error, kErrWaitAccFull);
+            const bool ready = mbar_wait(&epi_full[es], eph, abort_flag, p.error, kErrWaitEpiFull) &&
+                               mbar_wait(&epi_tx[es], eph, abort_flag, p.error, kErrWaitEpiFull) &&
+                               mbar_wait(&acc_full[acc], use & 1u, abort_flag, p.error, kErrWaitAccFull);
             if (!__all_sync(0xffffffffu, ready)) break;
             tc_fence_after();
-            const uint32_t base = tmem + lane_base + acc * (T::kAcc * kBN) + col0;
+            const uint8_t * slot = ering + es * kEpiSlotBytes;
+            const uint32_t word = reinterpret_cast<const uint32_t *>(slot)[m];
+            const float dw = half_bits_to_float(uint16_t(word & 0xffffu));
+            const float dmin = half_bits_to_float(uint16_t(word >> 16));  // unused for Q6_K
+            const float2 dw2 = f2(dw, dw), dmin2 = f2(dmin, dmin);
+            const float * da_s = reinterpret_cast<const float *>(slot + kEpiDaOff) + col0;
+            const uint32_t base = tmem + lane_base + acc * (T::kAcc * BN) + col0;
 #pragma unroll
             for (int ch = 0; ch < kCols / 8; ++ch) {
                 uint32_t r0[8], r1[8], r2[8];
                 tmem_ld8(base + 8 * ch, r0);
-                tmem_ld8(base + kBN + 8 * ch, r1);
-                if constexpr (T::kAcc == 3) tmem_ld8(base + 2 * kBN + 8 * ch, r2);
+                tmem_ld8(base + BN + 8 * ch, r1);
+                if constexpr (T::kAcc == 3) tmem_ld8(base + 2 * BN + 8 * ch, r2);
+                const float4 da0 = *reinterpret_cast<const float4 *>(da_s + 8 * ch);
+                const float4 da1 = *reinterpret_cast<const float4 *>(da_s + 8 * ch + 4);
                 tmem_wait_ld();
                 if (ch == kCols / 8 - 1) {
+                    // the accumulators and the ring slot may be reused now
                     tc_fence_before();
-                    mbar_arrive(&acc_empty[acc]);  // the accumulators may be overwritten now
-                }
-                const float4 da0 = *reinterpret_cast<const float4 *>(da_s + col0 + 8 * ch);
-                const float4 da1 = *reinterpret_cast<const float4 *>(da_s + col0 + 8 * ch + 4);
-                const float das[8] = {da0.x, da0.y, da0.z, da0.w, da1.x, da1.y, da1.z, da1.w};
-#pragma unroll
-                for (int k = 0; k < 8; ++k) {
-                    const float da = das[k];
-                    float c;
-                    if constexpr (TYPE == JF_TENSOR_Q4_K) {
-                        const float isum = __fadd_rn(__uint_as_float(r0[k]), __uint_as_float(r1[k]));
-                        c = __fsub_rn(__fmul_rn(__fmul_rn(dw, da), isum),
-                                      __fmul_rn(__fmul_rn(dmin, da), __uint_as_float(r2[k])));
-                    } else if constexpr (TYPE == JF_TENSOR_Q6_K) {
-                        const float isum = __fmaf_rn(16.0f, __uint_as_float(r0[k]), __uint_as_float(r1[k]));
-                        c = __fmul_rn(__fmul_rn(dw, da), isum);
-                    } else {
-                        c = __fsub_rn(__fmul_rn(__fmul_rn(dw, da), __uint_as_float(r0[k])),
-                                      __fmul_rn(__fmul_rn(dmin, da), __uint_as_float(r1[k])));
+                    __syncwarp();
+                    if (lane == 0) {
+                        mbar_arrive(&acc_empty[acc]);
+                        mbar_arrive(&epi_empty[es]);
                     }
-                    sum[8 * ch + k] += double(c);
+                }
+                const float2 das[4] = {f2(da0.x, da0.y), f2(da0.z, da0.w), f2(da1.x, da1.y), f2(da1.z, da1.w)};
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const float2 da = das[k];
+                    const float2 a0 = f2(__uint_as_float(r0[2 * k]), __uint_as_float(r0[2 * k + 1]));
+                    const float2 a1 = f2(__uint_as_float(r1[2 * k]), __uint_as_float(r1[2 * k + 1]));
+                    float2 c;
+                    if constexpr (TYPE == JF_TENSOR_Q4_K) {
+                        // c = (dw*da)*RN(D0 + D1) - (dmin*da)*msum
+                        const float2 a2 = f2(__uint_as_float(r2[2 * k]), __uint_as_float(r2[2 * k + 1]));
+                        const float2 isum = f2(__fadd_rn(a0.x, a1.x), __fadd_rn(a0.y, a1.y));
+                        const float2 t1 = mul2_rn(mul2_rn(dw2, da), isum);
+                        const float2 t2 = mul2_rn(mul2_rn(dmin2, da), a2);
+                        c = f2(__fsub_rn(t1.x, t2.x), __fsub_rn(t1.y, t2.y));
+                    } else if constexpr (TYPE == JF_TENSOR_Q6_K) {
+                        // 16*Dhi is exact, so the fused form rounds once, like RN(isum)
+                        const float2 isum = fma2_rn(f2(16.0f, 16.0f), a0, a1);
+                        c = mul2_rn(mul2_rn(dw2, da), isum);
+                    } else {
+                        const float2 t1 = mul2_rn(mul2_rn(dw2, da), a0);
+                        const float2 t2 = mul2_rn(mul2_rn(dmin2, da), a1);
+                        c = f2(__fsub_rn(t1.x, t2.x), __fsub_rn(t1.y, t2.y));
+                    }
+                    sum[8 * ch + 2 * k] += double(c.x);
+                    sum[8 * ch + 2 * k + 1] += double(c.y);
                 }
             }
-            __syncwarp();  // every lane is done with slot `slot` before it is refilled
-            stage_scales(w + kScaleRing, slot);
+            if (++es == kEpiRing) {
+                es = 0;
+                eph ^= 1u;
+            }
 
             // a segment ends where the CTA's range or the tile's K range ends
             if (w + 1 != w_end && cur.b + 1 != nb) continue;
@@ -944,7 +990,7 @@ __global__ void __launch_bounds__(kThreads, 1) mmq_tc_kernel(const __grid_consta
             seg_begin = w + 1;
             if (!complete) {
                 const uint32_t slot_p = 2 * blockIdx.x + (tile == first_tile ? 0 : 1);
-                double * part = p.partial + uint64_t(slot_p) * kSlotDoubles;
+                double * part = p.partial + uint64_t(slot_p) * R::kSlotDoubles;
 #pragma unroll
                 for (int t = 0; t < kCols; ++t) part[(col0 + t) * kRows + m] = sum[t];
                 __threadfence();
@@ -953,7 +999,7 @@ __global__ void __launch_bounds__(kThreads, 1) mmq_tc_kernel(const __grid_consta
                 const uint32_t hi = cta_of(uint64_t(tile + 1) * nb - 1, p.work, g);
                 uint32_t arrived = 0;
                 if (lane == 0) {
-                    uint32_t * counter = p.counters + uint64_t(tile) * kEpilogueWarps + warp;
+                    uint32_t * counter = p.counters + uint64_t(tile) * R::kEpiWarps + warp;
                     arrived = atomicAdd(counter, 1u) + 1;
                     if (arrived == hi - lo + 1) *counter = 0;  // every contributor is in
                 }
@@ -966,8 +1012,8 @@ __global__ void __launch_bounds__(kThreads, 1) mmq_tc_kernel(const __grid_consta
                 // eight tokens at a time, with the loads of several
                 // contributors in flight together.
                 const uint64_t lo_slot = 2 * uint64_t(lo) + (range_start(lo, p.work, g) == uint64_t(tile) * nb ? 0 : 1);
-                const double * lo_src = p.partial + lo_slot * kSlotDoubles + col0 * kRows + m;
-                const double * rest = p.partial + 2 * uint64_t(lo + 1) * kSlotDoubles + col0 * kRows + m;
+                const double * lo_src = p.partial + lo_slot * R::kSlotDoubles + col0 * kRows + m;
+                const double * rest = p.partial + 2 * uint64_t(lo + 1) * R::kSlotDoubles + col0 * kRows + m;
 #pragma unroll
                 for (int t0 = 0; t0 < kCols; t0 += 8) {
                     double acc8[8];
@@ -975,7 +1021,7 @@ __global__ void __launch_bounds__(kThreads, 1) mmq_tc_kernel(const __grid_consta
                     for (int k = 0; k < 8; ++k) acc8[k] = 0.0 + __ldcg(lo_src + (t0 + k) * kRows);
 #pragma unroll 4
                     for (uint32_t c = 0; c < hi - lo; ++c) {
-                        const double * src = rest + uint64_t(2 * c) * kSlotDoubles;
+                        const double * src = rest + uint64_t(2 * c) * R::kSlotDoubles;
                         double v[8];
 #pragma unroll
                         for (int k = 0; k < 8; ++k) v[k] = __ldcg(src + (t0 + k) * kRows);
@@ -1009,12 +1055,11 @@ __global__ void __launch_bounds__(kThreads, 1) mmq_tc_kernel(const __grid_consta
                 }
             }
         }
-        cp_async_wait<0>();  // no copy may land after the kernel ends
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if (warp == kMmaWarp) {
+    if (warp == R::kMmaWarp) {
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
     }
 }
@@ -1033,26 +1078,31 @@ int sm_count() {
     return cached[dev];
 }
 
+// Activation rows per tile: 32 for decode-sized calls, 64 above (each weight
+// conversion then feeds twice the tokens).
+uint32_t tile_tokens(uint32_t n) { return n <= 32 ? 32u : 64u; }
+
 struct Plan {
-    uint32_t tiles_m, tiles, grid;
+    uint32_t bn, tiles_m, tiles, grid;
     uint64_t work;
 };
 
 Plan make_plan(uint32_t rows, uint32_t cols, uint32_t n) {
     Plan pl;
+    pl.bn = tile_tokens(n);
     pl.tiles_m = (rows + kRows - 1) / kRows;
-    pl.tiles = pl.tiles_m * ((n + kBN - 1) / kBN);
+    pl.tiles = pl.tiles_m * ((n + pl.bn - 1) / pl.bn);
     pl.work = uint64_t(pl.tiles) * (cols / kQK);
     pl.grid = uint32_t(std::min<uint64_t>(pl.work, uint64_t(sm_count())));
     return pl;
 }
 
-// Workspace: partial slots for the largest grid this device runs (two per
-// SM), then the arrival counters. Both offsets are the same for every shape,
-// so calls of different shapes can share one workspace on a stream.
-uint64_t partial_bytes() { return uint64_t(2) * uint64_t(sm_count()) * kSlotDoubles * sizeof(double); }
+// Workspace: partial slots for the largest grid and tile this device runs
+// (two per SM), then the arrival counters. Both offsets are the same for every
+// shape, so calls of different shapes can share one workspace on a stream.
+uint64_t partial_bytes() { return uint64_t(2) * uint64_t(sm_count()) * uint64_t(kRows) * kMaxBN * sizeof(double); }
 uint64_t workspace_bytes(const Plan & pl) {
-    return partial_bytes() + uint64_t(pl.tiles) * kEpilogueWarps * sizeof(uint32_t);
+    return partial_bytes() + uint64_t(pl.tiles) * Roles<32>::kEpiWarps * sizeof(uint32_t);
 }
 
 // ---- tensor maps ----------------------------------------------------------------
@@ -1071,14 +1121,16 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
     return fn;
 }
 
-// A tensor map is a pure function of its parameters, so encoded maps are
-// cached by the full parameter tuple (bounded; cleared when it grows large).
-bool byte_tensor_map(CUtensorMap & out, const void * base, uint64_t row_bytes, uint64_t rows, uint32_t box_bytes,
-                     uint32_t box_rows, bool swizzle128 = false) {
-    using Key = std::tuple<uintptr_t, uint64_t, uint64_t, uint32_t, uint32_t, bool>;
+// 2D tensor map of [rows][width] elements of `elem_bytes` bytes with a row
+// stride of `stride` elements. A tensor map is a pure function of its
+// parameters, so encoded maps are cached by the full parameter tuple
+// (bounded; cleared when it grows large).
+bool tensor_map_2d(CUtensorMap & out, const void * base, uint32_t elem_bytes, uint64_t width, uint64_t stride,
+                   uint64_t rows, uint32_t box_w, uint32_t box_rows, bool swizzle128 = false) {
+    using Key = std::tuple<uintptr_t, uint32_t, uint64_t, uint64_t, uint64_t, uint32_t, uint32_t, bool>;
     static std::mutex mu;
     static std::map<Key, CUtensorMap> cache;
-    const Key key{reinterpret_cast<uintptr_t>(base), row_bytes, rows, box_bytes, box_rows, swizzle128};
+    const Key key{reinterpret_cast<uintptr_t>(base), elem_bytes, width, stride, rows, box_w, box_rows, swizzle128};
     std::lock_guard<std::mutex> lock(mu);
     auto it = cache.find(key);
     if (it != cache.end()) {
@@ -1087,15 +1139,17 @@ bool byte_tensor_map(CUtensorMap & out, const void * base, uint64_t row_bytes, u
     }
     PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
     if (encode == nullptr) return false;
-    const cuuint64_t dims[2] = {row_bytes, rows};
-    const cuuint64_t strides[1] = {row_bytes};
-    const cuuint32_t box[2] = {box_bytes, box_rows};
+    const CUtensorMapDataType type = elem_bytes == 1   ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                                     : elem_bytes == 2 ? CU_TENSOR_MAP_DATA_TYPE_UINT16
+                                                       : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+    const cuuint64_t dims[2] = {width, rows};
+    const cuuint64_t strides[1] = {stride * elem_bytes};
+    const cuuint32_t box[2] = {box_w, box_rows};
     const cuuint32_t elem[2] = {1, 1};
     CUtensorMap map;
     std::memset(&map, 0, sizeof(map));
-    if (encode(&map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides, box, elem,
-               CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
-               CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+    if (encode(&map, type, 2, const_cast<void *>(base), dims, strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE,
+               swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS) {
         return false;
     }
@@ -1105,33 +1159,40 @@ bool byte_tensor_map(CUtensorMap & out, const void * base, uint64_t row_bytes, u
     return true;
 }
 
-template <uint32_t TYPE>
-jfb_status build_maps(TcMaps & maps, const TcParams & p, uint32_t cols) {
+template <uint32_t TYPE, int BN>
+jfb_status build_maps(TcMaps & maps, const TcParams & p, const jfb_q8k & x, uint32_t cols) {
     using T = TypeTraits<TYPE>;
-    const uint64_t nb = p.blocks;
-    bool ok = byte_tensor_map(maps.w0, p.w.plane[0], nb * T::kBlockBytes, p.w.rows, T::kW0, kRows) &&
-              byte_tensor_map(maps.w1, p.w.plane[0], nb * T::kBlockBytes, p.w.rows, T::kW1 > 0 ? T::kW1 : 16, kRows) &&
-              byte_tensor_map(maps.sc, p.w.plane[1], nb * 16, p.w.rows, 16, kRows) &&
-              byte_tensor_map(maps.act, p.qs, cols, p.n, 128, kBN, true) &&
-              byte_tensor_map(maps.bsums, p.bsums, uint64_t(cols) / 8, p.n, 32, kBN);
+    const uint64_t nb = p.blocks, wb = nb * T::kBlockBytes;
+    const bool ok = tensor_map_2d(maps.w0, p.w.plane[0], 1, wb, wb, p.w.rows, T::kW0, kRows) &&
+                    tensor_map_2d(maps.w1, p.w.plane[0], 1, wb, wb, p.w.rows, T::kW1 > 0 ? T::kW1 : 16, kRows) &&
+                    tensor_map_2d(maps.sc, p.w.plane[1], 1, nb * 16, nb * 16, p.w.rows, 16, kRows) &&
+                    tensor_map_2d(maps.qs, x.qs_f16, 2, cols, cols, p.n, 64, BN, true) &&
+                    tensor_map_2d(maps.b2, x.bsums_f16, 2, cols / 16, cols / 16, p.n, 8, BN) &&
+                    tensor_map_2d(maps.dt, x.d_t, 4, p.n, x.d_stride, nb, BN, 1);
     if (!ok) return status_error(JFB_STATUS_CUDA_ERROR, "jfb_matmul_tc: could not encode a TMA tensor map");
     return status_ok();
 }
 
-template <uint32_t TYPE>
-jfb_status launch(TcParams & p, uint32_t cols, uint32_t grid, cudaStream_t s) {
-    constexpr uint32_t bytes = smem_bytes<TYPE>();
+template <uint32_t TYPE, int BN>
+jfb_status launch(TcParams & p, const jfb_q8k & x, uint32_t cols, uint32_t grid, cudaStream_t s) {
+    using L = Layout<TYPE, BN>;
+    using R = Roles<BN>;
+    constexpr uint32_t bytes = L::kSmem;
     static_assert(bytes <= kMaxSmem, "shared memory budget");
-    static_assert(raw_count<TYPE>() >= 2, "raw pipeline depth");
-    static_assert(stage_count<TYPE>() >= 2, "operand pipeline depth");
-    static_assert(acc_columns<TYPE>() + stage_count<TYPE>() * a_columns<TYPE>() <= kTmemCols, "TMEM budget");
-    static_assert(RawLayout<TYPE>::kBytes % 1024 == 0 && RawLayout<TYPE>::kActOff % 1024 == 0,
-                  "raw stages and the swizzled activation box stay 1024-byte aligned");
-    static_assert(kConverterThreads == kBN * 8, "one converter thread per token and 16-code chunk");
+    static_assert(L::NR >= 4, "raw pipeline depth: two units");
+    static_assert(L::NS >= 2, "operand pipeline depth");
+    static_assert(L::kAccCols + L::NS * L::kACols <= kTmemCols, "TMEM budget");
+    static_assert(L::kRawBytes % 1024 == 0 && L::kBHalf % 1024 == 0, "swizzled boxes stay 1024-byte aligned");
+    static_assert(L::kOpBytes % 1024 == 0 && kEpiSlotBytes % 128 == 0, "TMA destinations stay 128-byte aligned");
+    static_assert(kEpiDaOff >= kRows * 4 && kEpiDaOff + BN * 4 <= kEpiSlotBytes, "epilogue slot layout");
+    static_assert(R::kConvWarps % 4 == 0 && R::kParts * kRows == R::kConvThreads, "converter lanes cover the rows");
+    static_assert(R::kEpiWarps * 32 * R::kCols == kRows * BN && R::kCols % 8 == 0, "epilogue threads cover the tile");
+    static_assert(BN <= kMaxBN, "partial slots are sized for kMaxBN");
+    static_assert(R::kEpiWarps == Roles<32>::kEpiWarps, "one counter layout for every tile width");
     TcMaps maps;
-    jfb_status st = build_maps<TYPE>(maps, p, cols);
+    jfb_status st = build_maps<TYPE, BN>(maps, p, x, cols);
     if (st.code != JFB_STATUS_OK) return st;
-    auto kernel = mmq_tc_kernel<TYPE>;
+    auto kernel = mmq_tc_kernel<TYPE, BN>;
     // the shared-memory opt-in is a per-device function attribute: set once
     static std::mutex mu;
     static bool attribute_set[64] = {};
@@ -1148,8 +1209,13 @@ jfb_status launch(TcParams & p, uint32_t cols, uint32_t grid, cudaStream_t s) {
             attribute_set[dev] = true;
         }
     }
-    kernel<<<grid, kThreads, bytes, s>>>(maps, p);
+    kernel<<<grid, R::kThreads, bytes, s>>>(maps, p);
     return launch_status("jfb_matmul_tc");
+}
+
+template <uint32_t TYPE>
+jfb_status launch_type(TcParams & p, const jfb_q8k & x, uint32_t cols, const Plan & pl, cudaStream_t s) {
+    return pl.bn == 32 ? launch<TYPE, 32>(p, x, cols, pl.grid, s) : launch<TYPE, 64>(p, x, cols, pl.grid, s);
 }
 
 }  // namespace
@@ -1193,16 +1259,19 @@ extern "C" jfb_status jfb_matmul_tc_segments(const jfb_weight * weight, const jf
         return status_error(JFB_STATUS_INVALID_ARGUMENT, "output segments must end at the weight's %u rows", weight->rows);
     }
     if (n == 0) return status_ok();
-    if (x_q8->qs == nullptr || x_q8->d == nullptr || x_q8->bsums == nullptr) {
-        return status_error(JFB_STATUS_INVALID_ARGUMENT, "Q8_K activation planes are required");
+    if (x_q8->qs_f16 == nullptr || x_q8->bsums_f16 == nullptr || x_q8->d_t == nullptr) {
+        return status_error(JFB_STATUS_INVALID_ARGUMENT,
+                            "jfb_matmul_tc needs the Q8_K tensor-core planes (qs_f16, bsums_f16, d_t)");
     }
-    if ((reinterpret_cast<uintptr_t>(x_q8->qs) & 15u) != 0 || (reinterpret_cast<uintptr_t>(x_q8->bsums) & 15u) != 0) {
-        return status_error(JFB_STATUS_INVALID_ARGUMENT, "Q8_K codes and partial sums must be 16-byte aligned");
-    }
+    jfb_status chk = check_q8_tensor_core(x_q8, n);
+    if (chk.code != JFB_STATUS_OK) return chk;
     for (int i = 0; i < 2; ++i) {
         if ((reinterpret_cast<uintptr_t>(weight->plane[i]) & 15u) != 0) {
             return status_error(JFB_STATUS_INVALID_ARGUMENT, "weight planes must be 16-byte aligned");
         }
+    }
+    if (weight->type != JF_TENSOR_Q4_K && weight->plane[2] == nullptr) {
+        return status_error(JFB_STATUS_INVALID_ARGUMENT, "Q6_K and Q2_K weights need their scale plane");
     }
     const Plan pl = make_plan(weight->rows, weight->cols, n);
     const uint64_t need = workspace_bytes(pl);
@@ -1215,9 +1284,6 @@ extern "C" jfb_status jfb_matmul_tc_segments(const jfb_weight * weight, const jf
     }
     TcParams p;
     p.w = *weight;
-    p.qs = x_q8->qs;
-    p.da = x_q8->d;
-    p.bsums = x_q8->bsums;
     p.n = n;
     p.blocks = weight->cols / kQK;
     p.tiles_m = pl.tiles_m;
@@ -1237,9 +1303,9 @@ extern "C" jfb_status jfb_matmul_tc_segments(const jfb_weight * weight, const jf
     p.error = error_flag;
     cudaStream_t s = as_stream(stream);
     switch (weight->type) {
-    case JF_TENSOR_Q4_K: return launch<JF_TENSOR_Q4_K>(p, weight->cols, pl.grid, s);
-    case JF_TENSOR_Q6_K: return launch<JF_TENSOR_Q6_K>(p, weight->cols, pl.grid, s);
-    default: return launch<JF_TENSOR_Q2_K>(p, weight->cols, pl.grid, s);
+    case JF_TENSOR_Q4_K: return launch_type<JF_TENSOR_Q4_K>(p, *x_q8, weight->cols, pl, s);
+    case JF_TENSOR_Q6_K: return launch_type<JF_TENSOR_Q6_K>(p, *x_q8, weight->cols, pl, s);
+    default: return launch_type<JF_TENSOR_Q2_K>(p, *x_q8, weight->cols, pl, s);
     }
 }
 

@@ -73,10 +73,7 @@ __global__ void __launch_bounds__(kThreads) rmsnorm_quant_kernel(
             y.v[j] = i < cols ? __fmul_rn(__fmul_rn(v[c][j], scale), w[i]) : 0.0f;
             if (out_f32 != nullptr && i < cols) out_f32[uint64_t(row) * cols + i] = y.v[j];
         }
-        if (quantize) {
-            const uint64_t block = uint64_t(row) * (cols / kQK) + blk;
-            q8k_block_warp(y, q8.qs + block * kQK, q8.d + block, q8.bsums + block * 16);
-        }
+        if (quantize) q8k_block_warp(y, q8_dest(q8, row, blk, cols / kQK));
     }
 }
 
@@ -88,8 +85,7 @@ __global__ void __launch_bounds__(kThreads) quantize_kernel(const float * __rest
     const float4 * src = reinterpret_cast<const float4 *>(x + uint64_t(row) * cols + blk * kQK + 8 * lane);
     const float4 a = src[0], b = src[1];
     const Vals8 y = {{a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w}};
-    const uint64_t block = uint64_t(row) * (cols / kQK) + blk;
-    q8k_block_warp(y, q8.qs + block * kQK, q8.d + block, q8.bsums + block * 16);
+    q8k_block_warp(y, q8_dest(q8, row, blk, cols / kQK));
 }
 
 // silu(g) * u with silu(g) = g / (1 + e^-g), each step rounded
@@ -115,17 +111,16 @@ __global__ void __launch_bounds__(kThreads) swiglu_quant_kernel(const float * __
         y.v[j] = in ? swiglu(gate[base + j], up[base + j]) : 0.0f;
         if (out_f32 != nullptr && in) out_f32[base + j] = y.v[j];
     }
-    if (quantize) {
-        const uint64_t block = uint64_t(row) * (cols / kQK) + blk;
-        q8k_block_warp(y, q8.qs + block * kQK, q8.d + block, q8.bsums + block * 16);
-    }
+    if (quantize) q8k_block_warp(y, q8_dest(q8, row, blk, cols / kQK));
 }
 
-jfb_status check_q8(const jfb_q8k * q8, uint32_t cols) {
+jfb_status check_q8(const jfb_q8k * q8, uint32_t n, uint32_t cols) {
     if (q8 == nullptr) return status_ok();
     if (q8->qs == nullptr || q8->d == nullptr || q8->bsums == nullptr) {
         return status_error(JFB_STATUS_INVALID_ARGUMENT, "Q8_K output planes are required");
     }
+    const jfb_status tc = check_q8_tensor_core(q8, n);
+    if (tc.code != JFB_STATUS_OK) return tc;
     if (cols % kQK != 0) return status_error(JFB_STATUS_INVALID_ARGUMENT, "Q8_K rows must be a multiple of 256");
     return status_ok();
 }
@@ -144,10 +139,10 @@ extern "C" jfb_status jfb_rmsnorm_quant(const float * x, const int32_t * row_ind
     if (cols == 0 || cols > uint32_t(kMaxRowChunks * kThreads)) {
         return status_error(JFB_STATUS_INVALID_ARGUMENT, "rmsnorm row length %u is outside 1..8192", cols);
     }
-    jfb_status s = check_q8(out_q8, cols);
+    jfb_status s = check_q8(out_q8, n, cols);
     if (s.code != JFB_STATUS_OK) return s;
     if (n == 0) return status_ok();
-    const jfb_q8k q8 = out_q8 != nullptr ? *out_q8 : jfb_q8k{nullptr, nullptr, nullptr};
+    const jfb_q8k q8 = out_q8 != nullptr ? *out_q8 : jfb_q8k{};
     rmsnorm_quant_kernel<<<n, kThreads, 0, as_stream(stream)>>>(x, row_index, norm_weight, cols, eps, out_f32, q8,
                                                                  out_q8 != nullptr);
     return launch_status("jfb_rmsnorm_quant");
@@ -155,7 +150,7 @@ extern "C" jfb_status jfb_rmsnorm_quant(const float * x, const int32_t * row_ind
 
 extern "C" jfb_status jfb_quantize_q8k(const float * x, uint32_t n, uint32_t cols, const jfb_q8k * out, void * stream) {
     if (x == nullptr || out == nullptr) return status_error(JFB_STATUS_INVALID_ARGUMENT, "input and output are required");
-    jfb_status s = check_q8(out, cols);
+    jfb_status s = check_q8(out, n, cols);
     if (s.code != JFB_STATUS_OK) return s;
     if (n == 0) return status_ok();
     if (n > 65535u) return status_error(JFB_STATUS_INVALID_ARGUMENT, "Q8_K rows above 65535 per call");
@@ -168,10 +163,10 @@ extern "C" jfb_status jfb_swiglu_quant(const float * gate, const float * up, uin
     if (gate == nullptr || up == nullptr || (out_f32 == nullptr && out_q8 == nullptr)) {
         return status_error(JFB_STATUS_INVALID_ARGUMENT, "swiglu needs gate, up and an output");
     }
-    jfb_status s = check_q8(out_q8, cols);
+    jfb_status s = check_q8(out_q8, n, cols);
     if (s.code != JFB_STATUS_OK) return s;
     if (n == 0 || cols == 0) return status_ok();
-    const jfb_q8k q8 = out_q8 != nullptr ? *out_q8 : jfb_q8k{nullptr, nullptr, nullptr};
+    const jfb_q8k q8 = out_q8 != nullptr ? *out_q8 : jfb_q8k{};
     if (n > 65535u) return status_error(JFB_STATUS_INVALID_ARGUMENT, "swiglu rows above 65535 per call");
     swiglu_quant_kernel<<<dim3((cols + 8 * kQK - 1) / (8 * kQK), n), kThreads, 0, as_stream(stream)>>>(
         gate, up, cols, out_f32, q8, out_q8 != nullptr);

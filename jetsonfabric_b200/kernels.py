@@ -19,7 +19,8 @@ class Weight(C.Structure):
 
 
 class Q8K(C.Structure):
-    _fields_ = [("qs", C.c_void_p), ("d", C.c_void_p), ("bsums", C.c_void_p)]
+    _fields_ = [("qs", C.c_void_p), ("d", C.c_void_p), ("bsums", C.c_void_p), ("qs_f16", C.c_void_p),
+                ("bsums_f16", C.c_void_p), ("d_t", C.c_void_p), ("d_stride", C.c_uint32), ("reserved", C.c_uint32)]
 
 
 class Segment(C.Structure):
@@ -111,12 +112,27 @@ class DeviceWeight:
 
 
 class Q8Buffer:
-    def __init__(self, rows: int, cols: int):
+    """Q8_K activations [rows][cols] on the device. With `tensor_core` (the
+    default) the buffer also keeps the operands of the tensor-core matmul that
+    every quantizer writes: the codes and partial sums as f16 and d
+    transposed with a row stride of rows rounded up to 4."""
+
+    def __init__(self, rows: int, cols: int, tensor_core: bool = True):
         import torch
         self.qs = torch.zeros((rows, cols), dtype=torch.int8, device="cuda")
         self.d = torch.zeros((rows, cols // 256), dtype=torch.float32, device="cuda")
         self.bsums = torch.zeros((rows, cols // 16), dtype=torch.int16, device="cuda")
-        self.desc = Q8K(self.qs.data_ptr(), self.d.data_ptr(), self.bsums.data_ptr())
+        self.qs_f16 = self.bsums_f16 = self.d_t = None
+        self.d_stride = 0
+        if tensor_core:
+            self.d_stride = (rows + 3) // 4 * 4
+            self.qs_f16 = torch.zeros((rows, cols), dtype=torch.float16, device="cuda")
+            self.bsums_f16 = torch.zeros((rows, cols // 16), dtype=torch.float16, device="cuda")
+            self.d_t = torch.zeros((cols // 256, self.d_stride), dtype=torch.float32, device="cuda")
+        self.desc = Q8K(self.qs.data_ptr(), self.d.data_ptr(), self.bsums.data_ptr(),
+                        None if self.qs_f16 is None else self.qs_f16.data_ptr(),
+                        None if self.bsums_f16 is None else self.bsums_f16.data_ptr(),
+                        None if self.d_t is None else self.d_t.data_ptr(), self.d_stride, 0)
 
 
 def rmsnorm_quant(x, weight, eps, out_f32=None, out_q8: Q8Buffer | None = None, row_index=None, rows=None):

@@ -46,9 +46,10 @@ void orc_set_threads(int threads) {
  * exp(x) by Cody-Waite argument reduction (x = n ln2 + r, ln2 split in a
  * short high part and a correction) and the degree-7 Taylor polynomial of
  * e^r in Horner form with fused multiply-adds, then an exact two-step scaling
- * by 2^n. Used for softmax and SiLU. The CUDA library implements the same
- * method in its own code, so both produce identical bits (fmaf, rintf and the
- * float multiplications are correctly rounded on both). */
+ * by 2^n. Used for softmax and SiLU. The device kernels evaluate this same
+ * restatement step for step (exp_cw in the kernels' common header), so both
+ * produce identical bits (fmaf, rintf and the float multiplications are
+ * correctly rounded on both). */
 static float bitsf(uint32_t u);
 static float pow2i(int e) { return bitsf((uint32_t) (e + 127) << 23); }  /* 2^e, -126 <= e <= 127 */
 

@@ -10,8 +10,9 @@ import shutil
 import sys
 from pathlib import Path
 
-SOURCE = Path(sys.argv[1] if len(sys.argv) > 1 else
-              "/root/reference/runtime/engines/native/tests/fixtures/jfm-v2-golden")
+if len(sys.argv) != 2:
+    sys.exit("usage: make_jfm_golden.py <reference checkout>/runtime/engines/native/tests/fixtures/jfm-v2-golden")
+SOURCE = Path(sys.argv[1])
 TARGET = Path(__file__).resolve().parent / "jfm-v2-golden"
 
 if __name__ == "__main__":

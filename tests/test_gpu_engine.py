@@ -7,7 +7,7 @@ Mirrors the reference's engine tests:
 - session lifecycle, duplicate prefill, decode, rollback, and the 0-1 / 1-2
   stage split that must also yield 7
   (runtime/adapters/native_stage_executor_test.cpp:85-235);
-and adds the quantized-model parity the north star asks for: greedy token
+and adds the quantized-model parity required of the engine: greedy token
 streams identical to the CPU oracle (the GGML-CPU restatement) with per-step
 logits within 2e-2 max-abs and 1e-3 relative (relative = L2 norm of the
 difference over L2 norm of the oracle logits). The engine reproduces the

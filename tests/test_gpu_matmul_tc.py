@@ -117,7 +117,8 @@ def bits(a) -> np.ndarray:
     (96, 2048, 5),      # one unit per CTA: every tile split across 8 CTAs
     (300, 2560, 32),    # 3 row tiles x 10 blocks, a full token tile
     (1000, 11008, 33),  # 8 x 2 tiles x 43 blocks over 148 CTAs: tiles straddle CTAs
-    (200, 1024, 100),   # 2 x 4 tiles, partial token tile
+    (200, 1024, 100),   # 2 x 2 tiles of 64 tokens, partial token tile
+    (520, 2048, 130),   # 5 x 3 tiles of 64 tokens
 ])
 def test_tc_matches_oracle_and_cuda_core(K, jf_type, rows, cols, n):
     raw = random_blocks(jf_type, rows, cols, 7 + rows + jf_type, extreme_rows=(0, rows - 1))
@@ -158,7 +159,8 @@ def test_tc_workspace_reuse_leaves_counters_zero(K):
     for _ in range(3):
         again, _, ws = run_tc(K, w, x, workspace=ws)
         assert np.array_equal(bits(again), bits(first))
-    partial_bytes = 2 * torch.cuda.get_device_properties(0).multi_processor_count * 128 * 32 * 8
+    # partial slots: two per SM, sized for the widest token tile (64)
+    partial_bytes = 2 * torch.cuda.get_device_properties(0).multi_processor_count * 128 * 64 * 8
     counters = ws[partial_bytes:].view(torch.int32)
     assert int(counters.abs().sum().item()) == 0
 
@@ -181,6 +183,30 @@ def test_tc_shapes_share_one_workspace(K):
             assert np.array_equal(bits(got), bits(ref))
 
 
+@pytest.mark.parametrize("n,cols", [(1, 256), (37, 2048), (130, 11008)])
+def test_quantizer_writes_tensor_core_operands(K, n, cols):
+    """Every quantizer also writes the codes and partial sums as f16 and d
+    transposed; the tensor-core matmul loads those instead of the int8 codes."""
+    x = torch.from_numpy(activations(n, cols, 11, constant_rows=(0,))).cuda()
+    q8 = K.Q8Buffer(n, cols)
+    K.quantize_q8k(x, q8)
+    torch.cuda.synchronize()
+    assert torch.equal(q8.qs_f16.float(), q8.qs.float())
+    assert torch.equal(q8.bsums_f16.float(), q8.bsums.float())
+    assert torch.equal(q8.d_t[:, :n], q8.d.t())
+    gate = torch.from_numpy(activations(n, cols, 12)).cuda()
+    K.swiglu_quant(gate, x, out_q8=q8)
+    torch.cuda.synchronize()
+    assert torch.equal(q8.qs_f16.float(), q8.qs.float())
+    assert torch.equal(q8.d_t[:, :n], q8.d.t())
+    if cols <= 8192:
+        norm_w = torch.from_numpy(np.random.default_rng(1).normal(1, 0.1, cols).astype(np.float32)).cuda()
+        K.rmsnorm_quant(x, norm_w, 1e-6, out_q8=q8)
+        torch.cuda.synchronize()
+        assert torch.equal(q8.bsums_f16.float(), q8.bsums.float())
+        assert torch.equal(q8.d_t[:, :n], q8.d.t())
+
+
 def test_tc_rejects_bad_arguments(K):
     from jetsonfabric_b200.engine import InvalidArgument, NativeExecutionError
     rows, cols, n = 128, 512, 4
@@ -192,6 +218,9 @@ def test_tc_rejects_bad_arguments(K):
     small = torch.zeros(need - 8, dtype=torch.uint8, device="cuda")
     with pytest.raises(InvalidArgument):
         K.matmul_tc(w, n, out, q8, small)
+    plain = K.Q8Buffer(n, cols, tensor_core=False)  # no f16 operands for the tensor cores
+    with pytest.raises(InvalidArgument):
+        K.matmul_tc(w, n, out, plain, torch.zeros(need, dtype=torch.uint8, device="cuda"))
     f32 = K.DeviceWeight(jfm.JF_TENSOR_F32, 8, 256, np.zeros(8 * 256, np.float32).tobytes())
     with pytest.raises(NativeExecutionError):
         K.matmul_tc(f32, n, out, q8, torch.zeros(need, dtype=torch.uint8, device="cuda"))
