@@ -13,9 +13,10 @@
 //     of the row, and p is rounded to f16 exactly as GGML does before P V;
 //   - exp is exp_cw (common.cuh), the same method the CPU oracle implements.
 //
-// Rows of up to 8192 keys with head_dim 64 or 128 take a single launch (see
-// the single-launch path below). Otherwise four launches over a
-// (row, kv head, 64-key chunk) grid:
+// Head dims 64 and 128 with at most 8 query heads per kv head take a single
+// launch on the FP64 tensor cores (see the single-launch path below) for rows
+// of up to 32768 keys (4096 with 8 rows per CTA). Otherwise four launches over
+// a (row, kv head, 64-key chunk) grid:
 //   1. scores x_j (and each chunk's maximum) -> scratch
 //   2. per (row, head): max over chunks, sum_j exp(x_j - max) in double
 //   3. P V partial sums per chunk in double -> scratch
@@ -24,6 +25,7 @@
 // share its kv head, so each K and V row is read once for G heads.
 #include "common.cuh"
 
+#include <algorithm>
 #include <mutex>
 
 namespace jfb {
@@ -70,6 +72,8 @@ __global__ void __launch_bounds__(kThreads) scores_kernel(const float * __restri
                                                         uint32_t layer, float scale, uint32_t splits, Scratch sc) {
     __shared__ float q_s[kMaxGroup * kMaxHeadDim];
     __shared__ float x_s[kMaxGroup][kChunk];
+    pdl_trigger();
+    pdl_wait();
     const uint32_t r = blockIdx.x, kvh = blockIdx.y, split = blockIdx.z;
     const uint32_t keys = uint32_t(pos[r]) + 1u;
     const uint32_t j0 = split * kChunk;
@@ -160,6 +164,8 @@ __device__ __forceinline__ double block_sum(double v, double * shared) {
 __global__ void __launch_bounds__(kThreads) stats_kernel(const int32_t * __restrict__ pos, uint32_t heads, uint32_t splits,
                                                        Scratch sc) {
     __shared__ double red[kThreads / 32];
+    pdl_trigger();
+    pdl_wait();
     const uint32_t r = blockIdx.x, h = blockIdx.y;
     const uint32_t keys = uint32_t(pos[r]) + 1u;
     const uint32_t used = (keys + kChunk - 1) / kChunk;
@@ -185,6 +191,8 @@ __global__ void __launch_bounds__(kThreads) pv_kernel(const int32_t * __restrict
                                                     const jfb_kv_slot * __restrict__ slots, uint32_t layer,
                                                     uint32_t splits, Scratch sc) {
     __shared__ float p_s[kMaxGroup][kChunk];
+    pdl_trigger();
+    pdl_wait();
     const uint32_t r = blockIdx.x, kvh = blockIdx.y, split = blockIdx.z;
     const uint32_t keys = uint32_t(pos[r]) + 1u;
     const uint32_t j0 = split * kChunk;
@@ -232,6 +240,8 @@ __global__ void __launch_bounds__(256) combine_kernel(const int32_t * __restrict
                                                     uint32_t splits, Scratch sc, float * __restrict__ out, jfb_q8k q8,
                                                     int quantize) {
     __shared__ unsigned long long keys_s[8];
+    pdl_trigger();
+    pdl_wait();
     const uint32_t r = blockIdx.x;
     const uint32_t D = head_dim, width = heads * D;
     const uint32_t used = (uint32_t(pos[r]) + kChunk) / kChunk;
@@ -250,260 +260,485 @@ __global__ void __launch_bounds__(256) combine_kernel(const int32_t * __restrict
     }
 }
 
-// ---- single-launch path -------------------------------------------------------
+// ---- single-launch path on the FP64 tensor cores -------------------------------
 //
-// One CTA per (row, kv head, group of HPC query heads) does the whole row:
-//   scores   16 lanes per key for D = 128 (each lane 8 dims, one 16-byte load
-//            of the K row, so a K row is one coalesced 256-byte read); each
-//            lane keeps its 8 dims of f16(q) for the HPC heads in registers
-//            as doubles and accumulates k*q with DFMA (the f16*f16 product is
-//            exact, so this equals adding the exact products in double); the
-//            lane partials are added by a shuffle tree;
-//   softmax  block reductions for the maximum and the double sum of exp;
-//   P V      each thread owns 4 dims x HPC heads in double over an interleaved
-//            share of the keys; the shares are added in a fixed order.
-// The exact semantics are those of the four-launch path above. Scores and
-// probabilities live in shared memory, so the row's key count is bounded by
-// kFusedMaxKeys; longer rows use the four-launch path.
-constexpr int kFusedThreads = 256;
-constexpr uint32_t kFusedMaxKeys = 8192;
+// Exactness needs every score and output as the double sum of exact f16*f16
+// products, rounded to float once. The FP64 MMA (mma.sync m8n8k4 .f64)
+// computes such sums eight query heads at a time: the 8 x 4 A fragment holds
+// f16(q) of the G <= 8 query heads that share a kv head (the rows beyond G
+// are zero), the 4 x 8 B fragment eight keys of the K cache, and the 8 x 8
+// accumulator the scores of those heads and keys. Every product is exact in
+// double and each MMA rounds its sums in double, so the float scores equal
+// the CPU's (the order of the additions changes only bits far below a float
+// ulp). P V is the same product with A = f16(p) and B = eight V columns.
+//
+// Operands. A K or V value (f16) becomes a double with integer operations:
+// its 15 magnitude bits shifted into a double's exponent and mantissa fields
+// give the value times 2^-1008 (f16 subnormals become double subnormals, also
+// exact), and q and p carry the factor 2^1008, so every product is the exact
+// f16 product. The dimension order inside the dot products is free, so lane
+// (g, t) of a warp (g = lane / 4, t = lane % 4) holds dimensions
+// [D/4 * t, D/4 * (t + 1)) of q and of key g of each 8-key group: one
+// contiguous load of the K row per lane.
+//
+// Work split. A CTA (8 warps) serves R query rows and one kv head: R = 8 rows
+// (a warp per row) for prefill-sized calls, R = 1 row (8 warps splitting its
+// keys) for decode-sized ones. The keys of a row are split into contiguous
+// ranges of at most KC over a thread-block cluster of C CTAs, which exchange
+// the softmax maximum, the double sums of exp and the P V partial sums
+// through distributed shared memory, each added in cluster-rank order.
+// Scores and probabilities stay in shared memory ([R][8][KC + 4] floats).
+constexpr int kDThreads = 256;
+constexpr int kDWarps = kDThreads / 32;
+constexpr uint32_t kDMaxKeysRow8 = 512;    // KC limit with 8 rows per CTA
+constexpr uint32_t kDMaxKeysRow1 = 4096;   // KC limit with 1 row per CTA
+constexpr uint32_t kDMaxCluster = 8;       // portable cluster size
 
-template <int HPC, int D>
-__host__ __device__ constexpr uint32_t fused_smem_bytes(uint32_t keys_cap) {
-    return (kFusedThreads / (D / 4)) * HPC * D * 8  // PV partials [S][HPC][D] double
-           + HPC * D * 4                             // output values of the CTA
-           + HPC * keys_cap * 4;                     // scores / probabilities [HPC][keys_cap]
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
 }
 
-template <int HPC, int D>
-__global__ void __launch_bounds__(kFusedThreads, 1) fused_kernel(const float * __restrict__ q, const int32_t * __restrict__ seq,
-                                                            const int32_t * __restrict__ pos, uint32_t heads,
-                                                            uint32_t kv_heads, const jfb_kv_slot * __restrict__ slots,
-                                                            uint32_t layer, float scale, uint32_t keys_cap,
-                                                            float * __restrict__ out, jfb_q8k q8, int quantize) {
-    constexpr int L = D / 8;                  // lanes per key in the score pass
-    constexpr int KPW = 32 / L;               // keys per warp step
-    constexpr int DT = D / 4;                 // threads per key share in the P V pass
-    constexpr int S = kFusedThreads / DT;     // key shares
-    constexpr int W = kFusedThreads / 32;
-    extern __shared__ __align__(16) uint8_t smem_raw[];
-    double * red = reinterpret_cast<double *>(smem_raw);   // [S][HPC][D]
-    float * outs = reinterpret_cast<float *>(red + S * HPC * D);  // [HPC * D]
-    float * xs = outs + HPC * D;                            // [HPC][keys_cap]
-    __shared__ float wmax[W][HPC];
-    __shared__ double wsum[W][HPC];
-    __shared__ float stat[HPC][2];  // max, 1 / sum
-    __shared__ unsigned long long q8_keys[8];
+__device__ __forceinline__ uint32_t cluster_ctas() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
+    return r;
+}
 
-    const uint32_t r = blockIdx.x;
-    const uint32_t G = heads / kv_heads, groups = G / HPC;
-    const uint32_t kvh = blockIdx.y / groups;
-    const uint32_t h0 = kvh * G + (blockIdx.y % groups) * HPC;  // first query head of this CTA
-    // keys beyond the caller's max_keys are ignored, as on the four-launch path
-    const uint32_t keys = min(uint32_t(pos[r]) + 1u, keys_cap), kvd = kv_heads * D;
-    const jfb_kv_slot slot = slots[seq[r]];
-    const uint16_t * kbase = slot.k + uint64_t(layer) * slot.capacity * kvd + kvh * D;
-    const uint16_t * vbase = slot.v + uint64_t(layer) * slot.capacity * kvd + kvh * D;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+// All threads of all CTAs of the cluster; release/acquire orders the shared
+// memory each CTA wrote before it for the reads of the others after it.
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
 
-    // ---- scores
-    {
-        const int sub = lane / L, li = lane % L;
-        double qr[HPC][8];
-#pragma unroll
-        for (int h = 0; h < HPC; ++h) {
-            const float * qh = q + uint64_t(r) * heads * D + uint64_t(h0 + h) * D + 8 * li;
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-                qr[h][e] = double(__half2float(__float2half_rn(qh[e])));
-                asm volatile("" : "+d"(qr[h][e]));  // keep in a register: no reload inside the key loop
-            }
-        }
-        float mx[HPC];
-#pragma unroll
-        for (int h = 0; h < HPC; ++h) mx[h] = -INFINITY;
-        constexpr int U = 8;  // key steps whose loads are in flight together
-        for (uint32_t jb = uint32_t(warp) * KPW; jb < keys; jb += W * KPW * U) {
-            uint4 raw[U];
-#pragma unroll
-            for (int u = 0; u < U; ++u) {
-                const uint32_t j = jb + uint32_t(u * W * KPW + sub);
-                raw[u] = j < keys ? __ldg(reinterpret_cast<const uint4 *>(kbase + uint64_t(j) * kvd + 8 * li))
-                                  : make_uint4(0, 0, 0, 0);
-            }
-#pragma unroll
-            for (int u = 0; u < U; ++u) {
-                const uint32_t j = jb + uint32_t(u * W * KPW + sub);
-                double acc[HPC];
-#pragma unroll
-                for (int h = 0; h < HPC; ++h) acc[h] = 0.0;
-                const uint32_t wv[4] = {raw[u].x, raw[u].y, raw[u].z, raw[u].w};
-#pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    const double kd = double(half_bits_to_float(uint16_t(wv[e / 2] >> (16 * (e & 1)))));
-#pragma unroll
-                    for (int h = 0; h < HPC; ++h) acc[h] = fma(kd, qr[h][e], acc[h]);
-                }
-#pragma unroll
-                for (int o = L / 2; o > 0; o >>= 1) {
-#pragma unroll
-                    for (int h = 0; h < HPC; ++h) acc[h] += __shfl_xor_sync(0xffffffffu, acc[h], o);
-                }
-                if (li == 0 && j < keys) {
-#pragma unroll
-                    for (int h = 0; h < HPC; ++h) {
-                        const float x = __fmul_rn(__double2float_rn(acc[h]), scale);
-                        xs[h * keys_cap + j] = x;
-                        mx[h] = fmaxf(mx[h], x);
-                    }
-                }
-            }
-        }
-#pragma unroll
-        for (int h = 0; h < HPC; ++h) {
-            const float m = warp_max(mx[h]);
-            if (lane == 0) wmax[warp][h] = m;
-        }
-    }
-    __syncthreads();
-    if (threadIdx.x < HPC) {
-        float m = -INFINITY;
-        for (int w = 0; w < W; ++w) m = fmaxf(m, wmax[w][threadIdx.x]);
-        stat[threadIdx.x][0] = m;
-    }
-    __syncthreads();
+__device__ __forceinline__ uint32_t dsmem_addr(const void * p, uint32_t rank) {
+    uint32_t out;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;"
+                 : "=r"(out)
+                 : "r"(static_cast<uint32_t>(__cvta_generic_to_shared(p))), "r"(rank));
+    return out;
+}
 
-    // ---- softmax: e = exp(x - max), 1 / double sum, p = f16(e * inv)
-    {
-        double sum[HPC];
-#pragma unroll
-        for (int h = 0; h < HPC; ++h) {
-            const float m = stat[h][0];
-            double acc = 0.0;
-            for (uint32_t j = threadIdx.x; j < keys; j += kFusedThreads) {
-                const float e = exp_cw(__fsub_rn(xs[h * keys_cap + j], m));
-                xs[h * keys_cap + j] = e;
-                acc += double(e);
-            }
-            sum[h] = warp_sum(acc);
-        }
-        if (lane == 0) {
-#pragma unroll
-            for (int h = 0; h < HPC; ++h) wsum[warp][h] = sum[h];
-        }
-    }
-    __syncthreads();
-    if (threadIdx.x < HPC) {
-        double t = 0.0;
-        for (int w = 0; w < W; ++w) t += wsum[w][threadIdx.x];
-        stat[threadIdx.x][1] = __double2float_rn(__ddiv_rn(1.0, t));  // t >= 1 (the maximum contributes 1)
-    }
-    __syncthreads();
-#pragma unroll
-    for (int h = 0; h < HPC; ++h) {
-        const float inv = stat[h][1];
-        for (uint32_t j = threadIdx.x; j < keys; j += kFusedThreads) {
-            xs[h * keys_cap + j] = __half2float(__float2half_rn(__fmul_rn(xs[h * keys_cap + j], inv)));
-        }
-    }
-    __syncthreads();
+__device__ __forceinline__ float dsmem_f32(uint32_t addr) {
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+    return v;
+}
 
-    // ---- P V
-    {
-        const int dq = threadIdx.x % DT, share = threadIdx.x / DT;
-        double acc[HPC][4];
-#pragma unroll
-        for (int h = 0; h < HPC; ++h) {
-#pragma unroll
-            for (int e = 0; e < 4; ++e) acc[h][e] = 0.0;
-        }
-        constexpr int U = 8;  // keys whose V loads are in flight together
-        for (uint32_t jb = uint32_t(share); jb < keys; jb += S * U) {
-            uint2 raw[U];
-#pragma unroll
-            for (int u = 0; u < U; ++u) {
-                const uint32_t j = jb + uint32_t(u * S);
-                raw[u] = j < keys ? __ldg(reinterpret_cast<const uint2 *>(vbase + uint64_t(j) * kvd + 4 * dq))
-                                  : make_uint2(0, 0);
-            }
-#pragma unroll
-            for (int u = 0; u < U; ++u) {
-                const uint32_t j = jb + uint32_t(u * S);
-                if (j >= keys) break;
-                const double v0 = double(half_bits_to_float(uint16_t(raw[u].x & 0xffffu)));
-                const double v1 = double(half_bits_to_float(uint16_t(raw[u].x >> 16)));
-                const double v2 = double(half_bits_to_float(uint16_t(raw[u].y & 0xffffu)));
-                const double v3 = double(half_bits_to_float(uint16_t(raw[u].y >> 16)));
-#pragma unroll
-                for (int h = 0; h < HPC; ++h) {
-                    const double pj = double(xs[h * keys_cap + j]);
-                    acc[h][0] = fma(v0, pj, acc[h][0]);
-                    acc[h][1] = fma(v1, pj, acc[h][1]);
-                    acc[h][2] = fma(v2, pj, acc[h][2]);
-                    acc[h][3] = fma(v3, pj, acc[h][3]);
-                }
-            }
-        }
-#pragma unroll
-        for (int h = 0; h < HPC; ++h) {
-#pragma unroll
-            for (int e = 0; e < 4; ++e) red[(share * HPC + h) * D + 4 * dq + e] = acc[h][e];
-        }
-    }
-    __syncthreads();
-    for (int i = threadIdx.x; i < HPC * D; i += kFusedThreads) {
-        double t = 0.0;
-#pragma unroll
-        for (int sh = 0; sh < S; ++sh) t += red[sh * HPC * D + i];
-        const float v = __double2float_rn(t);
-        outs[i] = v;
-        out[uint64_t(r) * heads * D + uint64_t(h0) * D + i] = v;
-    }
-    if (!quantize) return;
-    __syncthreads();
-    const uint32_t blocks_per_row = heads * D / kQK;
-#pragma unroll 1
-    for (int c = 0; c < HPC * D / kQK; ++c) {
-        const uint32_t blk = uint32_t((uint64_t(h0) * D) / kQK) + uint32_t(c);
-        q8k_block_256(outs[c * kQK + threadIdx.x], q8_dest(q8, r, blk, blocks_per_row), q8_keys);
-    }
+__device__ __forceinline__ double dsmem_f64(uint32_t addr) {
+    double v;
+    asm volatile("ld.shared::cluster.f64 %0, [%1];" : "=d"(v) : "r"(addr) : "memory");
+    return v;
+}
+
+// D (8 x 8) += A (8 x 4) B (4 x 8) in double; this lane's elements:
+// a = A[lane / 4][lane % 4], b = B[lane % 4][lane / 4],
+// d0, d1 = D[lane / 4][2 (lane % 4) + 0, 1].
+__device__ __forceinline__ void dmma(double & d0, double & d1, double a, double b) {
+    asm volatile("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0, %1}, {%2}, {%3}, {%0, %1};"
+                 : "+d"(d0), "+d"(d1)
+                 : "d"(a), "d"(b));
+}
+
+// The two f16 values of w as doubles times 2^-1008, exactly.
+__device__ __forceinline__ void h2_scaled_doubles(uint32_t w, double & lo, double & hi) {
+    const uint32_t h0 = ((w & 0x7fffu) << 10) | ((w & 0x8000u) << 16);
+    const uint32_t h1 = ((w >> 6) & 0x01fffc00u) | (w & 0x80000000u);
+    lo = __hiloint2double(static_cast<int>(h0), 0);
+    hi = __hiloint2double(static_cast<int>(h1), 0);
+}
+
+constexpr double kTwo1008 = 0x1p1008;  // 2^1008
+
+struct DmmaLayout {
+    uint32_t rows, kc, kcp;  // R, keys per CTA, row stride of the score array
+    uint32_t x_bytes;        // scores / probabilities, later the warps' P V partials and the output rows
+    uint32_t o_bytes;        // the CTA's P V partial sums [R][8][D] (read by the cluster)
+    uint32_t total;
+};
+
+__host__ __device__ inline DmmaLayout dmma_layout(uint32_t rows, uint32_t kc, uint32_t head_dim) {
+    DmmaLayout l;
+    l.rows = rows;
+    l.kc = kc;
+    l.kcp = kc + 4;  // == 4 mod 8: the 8 head rows of a P fragment load hit distinct banks
+    uint32_t x = rows * 8 * l.kcp * 4;
+    const uint32_t warp_partials = rows == 1 ? kDWarps * 8 * head_dim * 8 : 0;
+    const uint32_t out_rows = rows * 8 * head_dim * 4;
+    x = x > warp_partials ? x : warp_partials;
+    x = x > out_rows ? x : out_rows;
+    l.x_bytes = (x + 15) / 16 * 16;
+    l.o_bytes = rows * 8 * head_dim * 8;
+    // + wmax [8][8] f32, wsum [8][8] f64, lmax [8][8] f32, lsum [8][8] f64, gmax/ginv [8][8] f32 each,
+    // key counts [8] u32
+    l.total = l.x_bytes + l.o_bytes + 8 * 8 * (4 + 8 + 4 + 8 + 4 + 4) + 8 * 4;
+    return l;
 }
 
 template <int D>
-jfb_status launch_fused_d(int hpc, const float * q, uint32_t n, const int32_t * seq, const int32_t * pos, uint32_t heads,
-                          uint32_t kv_heads, const jfb_kv_slot * slots, uint32_t layer, float scale,
-                          uint32_t keys_cap, float * out, jfb_q8k q8, int quantize, cudaStream_t s) {
-    const dim3 grid(n, kv_heads * ((heads / kv_heads) / uint32_t(hpc)));
-    auto go = [&](auto kernel, uint32_t bytes) -> jfb_status {
-        const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(bytes));
-        if (e != cudaSuccess) {
-            return status_error(JFB_STATUS_CUDA_ERROR, "attention shared memory attribute: %s", cudaGetErrorString(e));
-        }
-        kernel<<<grid, kFusedThreads, bytes, s>>>(q, seq, pos, heads, kv_heads, slots, layer, scale, keys_cap, out, q8,
-                                                  quantize);
-        return launch_status("jfb_attention");
+__global__ void __launch_bounds__(kDThreads, 1) dmma_attention_kernel(
+    const float * __restrict__ q, const int32_t * __restrict__ seq, const int32_t * __restrict__ pos, uint32_t n,
+    uint32_t heads, uint32_t kv_heads, const jfb_kv_slot * __restrict__ slots, uint32_t layer, float scale,
+    uint32_t keys_cap, uint32_t R, uint32_t KC, float * __restrict__ out, jfb_q8k q8, int quantize) {
+    constexpr int KS = D / 4;  // k-steps of a score (dimensions per lane)
+    constexpr int NT = D / 8;  // n-tiles of P V (dimensions per lane)
+    extern __shared__ __align__(16) uint8_t smem_raw[];
+    const DmmaLayout lay = dmma_layout(R, KC, D);
+    float * xs = reinterpret_cast<float *>(smem_raw);                                // [R][8][kcp]
+    double * wpart = reinterpret_cast<double *>(smem_raw);                           // [8 warps][8][D] (R = 1)
+    float * orow = reinterpret_cast<float *>(smem_raw);                              // [R][8][D] final values
+    double * octa = reinterpret_cast<double *>(smem_raw + lay.x_bytes);              // [R][8][D]
+    float * wmax = reinterpret_cast<float *>(smem_raw + lay.x_bytes + lay.o_bytes);  // [8][8]
+    double * wsum = reinterpret_cast<double *>(wmax + 64);                          // [8][8]
+    float * lmax = reinterpret_cast<float *>(wsum + 64);                            // [8][8] per (row, head)
+    double * lsum = reinterpret_cast<double *>(lmax + 64);                          // [8][8]
+    float * gmax = reinterpret_cast<float *>(lsum + 64);                            // [8][8]
+    float * ginv = gmax + 64;                                                       // [8][8]
+
+    const uint32_t C = cluster_ctas(), crank = cluster_rank();
+    const uint32_t tile = blockIdx.x / C, kvh = blockIdx.y;
+    const uint32_t G = heads / kv_heads, h0 = kvh * G, kvd = kv_heads * D;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int gq = lane >> 2, tq = lane & 3;
+    const uint32_t S = kDWarps / R;                    // warps per row
+    const uint32_t row_local = uint32_t(warp) / S, slice = uint32_t(warp) % S;
+    const uint32_t kc0 = crank * KC;
+
+    // keys of row `rl` of the tile that fall in this CTA's range [kc0, kc0 + KC)
+    auto row_keys = [&](uint32_t rl) -> uint32_t {
+        const uint32_t r = tile * R + rl;
+        if (r >= n) return 0u;
+        const uint32_t keys = min(uint32_t(pos[r]) + 1u, keys_cap);
+        return keys > kc0 ? min(keys - kc0, KC) : 0u;
     };
-    switch (hpc) {
-    case 4: return go(fused_kernel<4, D>, fused_smem_bytes<4, D>(keys_cap));
-    case 3: return go(fused_kernel<3, D>, fused_smem_bytes<3, D>(keys_cap));
-    case 2: return go(fused_kernel<2, D>, fused_smem_bytes<2, D>(keys_cap));
-    default: return go(fused_kernel<1, D>, fused_smem_bytes<1, D>(keys_cap));
+
+    pdl_trigger();
+    // positions, sequence ids and KV slots are per-call metadata, written
+    // before the first kernel of the call: read them before waiting for the
+    // previous kernel (whose output is q and the appended K/V rows)
+    uint32_t * nk_s = reinterpret_cast<uint32_t *>(ginv + 64);  // [8] keys of each tile row in this CTA
+    if (threadIdx.x < R) nk_s[threadIdx.x] = row_keys(threadIdx.x);
+    const uint32_t r = tile * R + row_local;
+    const uint32_t nk = row_keys(row_local);
+    const uint32_t ng = (nk + 7) / 8;                  // 8-key groups of the row in this CTA
+    const uint32_t gs = (ng + S - 1) / S;               // groups per warp of the row
+    const uint32_t g_begin = min(ng, slice * gs), g_end = min(ng, g_begin + gs);
+    const jfb_kv_slot slot = r < n ? slots[seq[r]] : jfb_kv_slot{};
+    const uint16_t * kbase = slot.k + uint64_t(layer) * slot.capacity * kvd + kvh * D;
+    const uint16_t * vbase = slot.v + uint64_t(layer) * slot.capacity * kvd + kvh * D;
+    float * xrow = xs + row_local * 8 * lay.kcp;
+    pdl_wait();
+
+    // ---- scores of this warp's key groups. Four independent accumulator
+    // chains per score (k-steps of each residue mod 4) keep several FP64 MMAs
+    // in flight; the next group's K row is loaded while this one is summed.
+    float mx = -INFINITY;  // this lane's maximum for head gq
+    if (g_begin < g_end) {
+        double qa[KS];
+        {
+            const bool live = uint32_t(gq) < G;
+            const float * qh = q + uint64_t(r) * heads * D + uint64_t(h0 + (live ? gq : 0)) * D + KS * tq;
+#pragma unroll
+            for (int k = 0; k < KS; ++k) {
+                qa[k] = live ? double(__half2float(__float2half_rn(qh[k]))) * kTwo1008 : 0.0;
+            }
+        }
+        auto load_k = [&](uint32_t g, uint4 (&raw)[KS / 8]) {
+            const uint32_t key = 8 * g + uint32_t(gq);  // this lane's K row (relative to kc0)
+#pragma unroll
+            for (int c = 0; c < KS / 8; ++c) {
+                raw[c] = key < nk ? __ldg(reinterpret_cast<const uint4 *>(kbase + uint64_t(kc0 + key) * kvd + KS * tq) + c)
+                                  : make_uint4(0, 0, 0, 0);
+            }
+        };
+        auto score_group = [&](uint32_t g, const uint4 (&cur)[KS / 8]) {
+            double acc[4][2];
+#pragma unroll
+            for (int a = 0; a < 4; ++a) acc[a][0] = acc[a][1] = 0.0;
+#pragma unroll
+            for (int c = 0; c < KS / 8; ++c) {
+                const uint32_t w[4] = {cur[c].x, cur[c].y, cur[c].z, cur[c].w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    double b0, b1;
+                    h2_scaled_doubles(w[e], b0, b1);
+                    const int k0 = 8 * c + 2 * e;
+                    dmma(acc[k0 & 3][0], acc[k0 & 3][1], qa[k0], b0);
+                    dmma(acc[(k0 + 1) & 3][0], acc[(k0 + 1) & 3][1], qa[k0 + 1], b1);
+                }
+            }
+            const double d0 = (acc[0][0] + acc[1][0]) + (acc[2][0] + acc[3][0]);
+            const double d1 = (acc[0][1] + acc[1][1]) + (acc[2][1] + acc[3][1]);
+            // d0, d1: scores of head gq for keys 8g + 2tq + {0, 1} (relative to kc0)
+            const uint32_t j = 8 * g + 2 * uint32_t(tq);
+            const float x0 = j < nk ? __fmul_rn(__double2float_rn(d0), scale) : -INFINITY;
+            const float x1 = j + 1 < nk ? __fmul_rn(__double2float_rn(d1), scale) : -INFINITY;
+            if (uint32_t(gq) < G) {
+                xrow[gq * lay.kcp + j] = x0;
+                xrow[gq * lay.kcp + j + 1] = x1;
+            }
+            mx = fmaxf(mx, fmaxf(x0, x1));
+        };
+        // K rows of three groups in flight per warp (a ring of register buffers)
+        uint4 kb[3][KS / 8];
+        load_k(g_begin, kb[0]);
+        if (g_begin + 1 < g_end) load_k(g_begin + 1, kb[1]);
+        for (uint32_t g = g_begin; g < g_end; g += 3) {
+#pragma unroll
+            for (int u = 0; u < 3; ++u) {
+                if (g + u >= g_end) break;
+                if (g + u + 2 < g_end) load_k(g + u + 2, kb[(u + 2) % 3]);
+                score_group(g + u, kb[u]);
+            }
+        }
     }
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    if (tq == 0) wmax[warp * 8 + gq] = mx;
+    __syncthreads();
+    if (threadIdx.x < R * 8) {  // (row, head) maximum over the row's warps
+        const uint32_t rl = threadIdx.x / 8, h = threadIdx.x % 8;
+        float m = -INFINITY;
+        for (uint32_t s = 0; s < S; ++s) m = fmaxf(m, wmax[(rl * S + s) * 8 + h]);
+        lmax[threadIdx.x] = m;
+    }
+    cluster_sync_all();
+    if (threadIdx.x < R * 8) {  // maximum over the cluster
+        float m = -INFINITY;
+        for (uint32_t c = 0; c < C; ++c) m = fmaxf(m, dsmem_f32(dsmem_addr(lmax + threadIdx.x, c)));
+        gmax[threadIdx.x] = m;
+    }
+    __syncthreads();
+
+    // ---- e = exp(x - max) and its double sum per (row, head); zero the key
+    // tail up to the next multiple of 8 (read by the P V k-steps)
+    for (uint32_t pr = uint32_t(warp); pr < R * 8; pr += kDWarps) {
+        const uint32_t rl = pr / 8, h = pr % 8;
+        double acc = 0.0;
+        if (h < G) {
+            const uint32_t keys = nk_s[rl];
+            float * xr = xs + (rl * 8 + h) * lay.kcp;
+            const float m = gmax[pr];
+            for (uint32_t j = uint32_t(lane); j < (keys + 7) / 8 * 8; j += 32) {
+                if (j < keys) {
+                    const float e = exp_cw(__fsub_rn(xr[j], m));
+                    xr[j] = e;
+                    acc += double(e);
+                } else {
+                    xr[j] = 0.0f;
+                }
+            }
+        }
+        acc = warp_sum(acc);
+        if (lane == 0) lsum[pr] = acc;
+    }
+    cluster_sync_all();
+    if (threadIdx.x < R * 8) {  // total in cluster-rank order; 1 / total as the CPU rounds it
+        double t = 0.0;
+        for (uint32_t c = 0; c < C; ++c) t += dsmem_f64(dsmem_addr(lsum + threadIdx.x, c));
+        ginv[threadIdx.x] = t > 0.0 ? __double2float_rn(__ddiv_rn(1.0, t)) : 0.0f;
+    }
+    __syncthreads();
+    for (uint32_t pr = uint32_t(warp); pr < R * 8; pr += kDWarps) {
+        const uint32_t rl = pr / 8, h = pr % 8;
+        if (h >= G) continue;
+        const uint32_t keys = nk_s[rl];
+        float * xr = xs + (rl * 8 + h) * lay.kcp;
+        const float inv = ginv[pr];
+        for (uint32_t j = uint32_t(lane); j < keys; j += 32) xr[j] = __half2float(__float2half_rn(__fmul_rn(xr[j], inv)));
+    }
+    __syncthreads();
+
+    // ---- P V over this warp's keys: o[t][i] = O[head gq][dim 16 (2 tq + i) + t]
+    double o[NT][2];
+#pragma unroll
+    for (int t = 0; t < NT; ++t) o[t][0] = o[t][1] = 0.0;
+    {
+        const uint32_t k_begin = 8 * g_begin, k_end = 8 * g_end;  // multiples of 8, within the zeroed tail
+        const float * prow = xrow + gq * lay.kcp;
+        const bool live = uint32_t(gq) < G;
+        auto load_v = [&](uint32_t kk, uint4 (&raw)[NT / 8]) {
+            const uint32_t j = kk + uint32_t(tq);  // this lane's V row (relative to kc0)
+#pragma unroll
+            for (int c = 0; c < NT / 8; ++c) {
+                raw[c] = j < nk ? __ldg(reinterpret_cast<const uint4 *>(vbase + uint64_t(kc0 + j) * kvd + NT * gq) + c)
+                                : make_uint4(0, 0, 0, 0);
+            }
+        };
+        auto pv_step = [&](uint32_t kk, const uint4 (&cur)[NT / 8]) {
+            const double a = live ? double(prow[kk + uint32_t(tq)]) * kTwo1008 : 0.0;
+#pragma unroll
+            for (int c = 0; c < NT / 8; ++c) {
+                const uint32_t w[4] = {cur[c].x, cur[c].y, cur[c].z, cur[c].w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    double b0, b1;
+                    h2_scaled_doubles(w[e], b0, b1);
+                    dmma(o[8 * c + 2 * e][0], o[8 * c + 2 * e][1], a, b0);
+                    dmma(o[8 * c + 2 * e + 1][0], o[8 * c + 2 * e + 1][1], a, b1);
+                }
+            }
+        };
+        // V rows of three key steps in flight per warp
+        uint4 vb[3][NT / 8];
+        if (k_begin < k_end) load_v(k_begin, vb[0]);
+        if (k_begin + 4 < k_end) load_v(k_begin + 4, vb[1]);
+        for (uint32_t kk = k_begin; kk < k_end; kk += 12) {
+#pragma unroll
+            for (int u = 0; u < 3; ++u) {
+                const uint32_t k = kk + 4 * uint32_t(u);
+                if (k >= k_end) break;
+                if (k + 8 < k_end) load_v(k + 8, vb[(u + 2) % 3]);
+                pv_step(k, vb[u]);
+            }
+        }
+    }
+    __syncthreads();  // every warp is done with the probabilities: the score array is reused below
+
+    // ---- the CTA's partial sums [R][8][D]
+    if (R == 1) {
+        double * wp = wpart + uint64_t(warp) * 8 * D + gq * D;
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+#pragma unroll
+            for (int i = 0; i < 2; ++i) wp[NT * (2 * tq + i) + t] = o[t][i];
+        }
+        __syncthreads();
+        for (uint32_t e = threadIdx.x; e < 8 * D; e += kDThreads) {
+            double t = 0.0;
+            for (int w = 0; w < kDWarps; ++w) t += wpart[uint64_t(w) * 8 * D + e];  // warp (slice) order
+            octa[e] = t;
+        }
+    } else {
+        double * op = octa + uint64_t(row_local) * 8 * D + gq * D;
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+#pragma unroll
+            for (int i = 0; i < 2; ++i) op[NT * (2 * tq + i) + t] = o[t][i];
+        }
+    }
+    cluster_sync_all();
+
+    // ---- rank 0 adds the cluster's partials in rank order, writes the rows
+    // and quantizes them to Q8_K
+    if (crank == 0) {
+        const uint32_t width = G * D;
+        for (uint32_t e = threadIdx.x; e < R * 8 * D; e += kDThreads) {
+            const uint32_t rl = e / (8 * D), h = (e / D) % 8, d = e % D;
+            const uint32_t rr = tile * R + rl;
+            if (h >= G || rr >= n) continue;
+            double t = 0.0;
+            for (uint32_t c = 0; c < C; ++c) t += dsmem_f64(dsmem_addr(octa + e, c));
+            const float v = __double2float_rn(t);
+            orow[rl * width + h * D + d] = v;
+            out[uint64_t(rr) * heads * D + uint64_t(h0) * D + h * D + d] = v;
+        }
+        if (quantize) {
+            __syncthreads();
+            const uint32_t per_row = width / kQK;  // Q8_K blocks of this kv head's heads
+            for (uint32_t b = uint32_t(warp); b < R * per_row; b += kDWarps) {
+                const uint32_t rl = b / per_row, blk = b % per_row;
+                const uint32_t rr = tile * R + rl;
+                if (rr >= n) continue;
+                const float * src = orow + rl * width + blk * kQK + 8 * lane;
+                const float4 a = *reinterpret_cast<const float4 *>(src);
+                const float4 c = *reinterpret_cast<const float4 *>(src + 4);
+                const Vals8 y = {{a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w}};
+                q8k_block_warp(y, q8_dest(q8, rr, (h0 * D) / kQK + blk, heads * D / kQK));
+            }
+        }
+    }
+    cluster_sync_all();  // no CTA leaves while another may still read its shared memory
 }
 
-// Query heads per CTA of the single-launch path: the largest of 4, 3, 2, 1
-// dividing the group, halved while that leaves the GPU without a full wave.
-int fused_heads_per_cta(uint32_t n, uint32_t heads, uint32_t kv_heads) {
-    const uint32_t G = heads / kv_heads;
-    int hpc = 1;
-    for (int c = 4; c >= 1; --c) {
-        if (G % uint32_t(c) == 0) {
-            hpc = c;
-            break;
+struct DmmaPlan {
+    bool ok;
+    uint32_t rows, kc, cluster, tiles;
+    DmmaLayout layout;
+};
+
+DmmaPlan dmma_plan(uint32_t n, uint32_t heads, uint32_t kv_heads, uint32_t head_dim, uint32_t max_keys, int sms) {
+    DmmaPlan pl{};
+    pl.ok = false;
+    if ((head_dim != 64 && head_dim != 128) || heads / kv_heads > 8 || n == 0) return pl;
+    pl.rows = uint64_t(n) * kv_heads >= uint64_t(8) * uint64_t(sms) ? 8u : 1u;
+    const uint32_t kc_max = pl.rows == 8 ? kDMaxKeysRow8 : kDMaxKeysRow1;
+    const uint32_t c_min = (max_keys + kc_max - 1) / kc_max;
+    if (c_min > kDMaxCluster) return pl;
+    pl.tiles = (n + pl.rows - 1) / pl.rows;
+    uint32_t c = c_min;
+    if (pl.rows == 1) {  // about one CTA per SM for decode-sized calls
+        const uint64_t ctas = uint64_t(pl.tiles) * kv_heads;
+        const uint32_t want = uint32_t(std::min<uint64_t>(kDMaxCluster, std::max<uint64_t>(1, uint64_t(sms) / ctas)));
+        c = std::max(c, want);
+    }
+    c = std::min(c, std::max(1u, (max_keys + 7) / 8));  // no CTA without keys at all
+    pl.cluster = std::max(c, c_min);
+    pl.kc = ((max_keys + pl.cluster - 1) / pl.cluster + 7) / 8 * 8;
+    if (pl.kc > kc_max) return pl;
+    pl.layout = dmma_layout(pl.rows, pl.kc, head_dim);
+    if (uint64_t(pl.tiles) * pl.cluster > 0x7fffffffu || kv_heads > 65535u) return pl;
+    pl.ok = true;
+    return pl;
+}
+
+template <int D>
+jfb_status launch_dmma(const DmmaPlan & pl, const float * q, uint32_t n, const int32_t * seq, const int32_t * pos,
+                       uint32_t heads, uint32_t kv_heads, const jfb_kv_slot * slots, uint32_t layer, float scale,
+                       uint32_t keys_cap, float * out, jfb_q8k q8, int quantize, cudaStream_t s) {
+    auto kernel = dmma_attention_kernel<D>;
+    static std::mutex mu;
+    static uint32_t attribute_bytes[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        if (attribute_bytes[dev] < pl.layout.total) {
+            // the largest layout of any plan: one attribute for every later call
+            const uint32_t bytes = std::max<uint32_t>(pl.layout.total, dmma_layout(8, kDMaxKeysRow8, D).total);
+            cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(bytes));
+            if (e != cudaSuccess) {
+                return status_error(JFB_STATUS_CUDA_ERROR, "attention shared memory attribute: %s", cudaGetErrorString(e));
+            }
+            attribute_bytes[dev] = bytes;
         }
     }
-    while (hpc % 2 == 0 && uint64_t(n) * kv_heads * (G / uint32_t(hpc)) < 148) hpc /= 2;
-    return hpc;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(pl.tiles * pl.cluster, kv_heads, 1);
+    cfg.blockDim = dim3(kDThreads, 1, 1);
+    cfg.dynamicSmemBytes = pl.layout.total;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = pl.cluster;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (pdl_enabled()) {
+        attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[1].val.programmaticStreamSerializationAllowed = 1;
+        cfg.numAttrs = 2;
+    }
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, q, seq, pos, n, heads, kv_heads, slots, layer, scale, keys_cap,
+                                             pl.rows, pl.kc, out, q8, quantize);
+    if (e != cudaSuccess) return status_error(JFB_STATUS_CUDA_ERROR, "jfb_attention: %s", cudaGetErrorString(e));
+    return launch_status("jfb_attention");
+}
+
+int device_sms() {
+    static std::mutex mu;
+    static int cached[64] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+    std::lock_guard<std::mutex> lock(mu);
+    if (cached[dev] == 0) {
+        int v = 0;
+        if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0) v = 148;
+        cached[dev] = v;
+    }
+    return cached[dev];
 }
 
 }  // namespace
@@ -543,27 +778,33 @@ extern "C" jfb_status jfb_attention(const float * q, uint32_t n, const int32_t *
         return status_error(JFB_STATUS_INVALID_ARGUMENT, "attention grid too large");
     }
     cudaStream_t s = as_stream(stream);
-    const jfb_q8k q8_fused = out_q8 != nullptr ? *out_q8 : jfb_q8k{};
-    if ((head_dim == 64 || head_dim == 128) && max_keys <= kFusedMaxKeys) {
-        const int hpc = fused_heads_per_cta(n, heads, kv_heads);
-        const uint32_t keys_cap = (max_keys + 3) / 4 * 4;
-        const bool fused_q8 = out_q8 != nullptr && (uint32_t(hpc) * head_dim) % kQK == 0;
+    const DmmaPlan plan = dmma_plan(n, heads, kv_heads, head_dim, max_keys, device_sms());
+    if (plan.ok) {
+        const bool fused_q8 = out_q8 != nullptr && ((heads / kv_heads) * head_dim) % kQK == 0;
+        const jfb_q8k q8_fused = fused_q8 ? *out_q8 : jfb_q8k{};
         const float fscale = 1.0f / sqrtf(float(head_dim));
-        jfb_status st = head_dim == 64 ? launch_fused_d<64>(hpc, q, n, seq, pos, heads, kv_heads, slots, layer, fscale,
-                                                            keys_cap, out, q8_fused, fused_q8 ? 1 : 0, s)
-                                       : launch_fused_d<128>(hpc, q, n, seq, pos, heads, kv_heads, slots, layer, fscale,
-                                                             keys_cap, out, q8_fused, fused_q8 ? 1 : 0, s);
+        jfb_status st = head_dim == 64 ? launch_dmma<64>(plan, q, n, seq, pos, heads, kv_heads, slots, layer, fscale,
+                                                         max_keys, out, q8_fused, fused_q8 ? 1 : 0, s)
+                                       : launch_dmma<128>(plan, q, n, seq, pos, heads, kv_heads, slots, layer, fscale,
+                                                          max_keys, out, q8_fused, fused_q8 ? 1 : 0, s);
         if (st.code != JFB_STATUS_OK || out_q8 == nullptr || fused_q8) return st;
         return jfb_quantize_q8k(out, n, heads * head_dim, out_q8, stream);
     }
     const Scratch sc = carve(scratch, n, heads, head_dim, splits);
     const float scale = 1.0f / sqrtf(float(head_dim));
-    scores_kernel<<<dim3(n, kv_heads, splits), kThreads, 0, s>>>(q, seq, pos, heads, kv_heads, head_dim, slots, layer,
-                                                                  scale, splits, sc);
-    stats_kernel<<<dim3(n, heads), kThreads, 0, s>>>(pos, heads, splits, sc);
-    pv_kernel<<<dim3(n, kv_heads, splits), kThreads, 0, s>>>(seq, pos, heads, kv_heads, head_dim, slots, layer, splits, sc);
+    cudaError_t e = launch_k(scores_kernel, dim3(n, kv_heads, splits), dim3(kThreads), 0, s, q, seq, pos, heads, kv_heads,
+                             head_dim, slots, layer, scale, splits, sc);
+    if (e == cudaSuccess) e = launch_k(stats_kernel, dim3(n, heads), dim3(kThreads), 0, s, pos, heads, splits, sc);
+    if (e == cudaSuccess) {
+        e = launch_k(pv_kernel, dim3(n, kv_heads, splits), dim3(kThreads), 0, s, seq, pos, heads, kv_heads, head_dim, slots,
+                     layer, splits, sc);
+    }
     const jfb_q8k q8 = out_q8 != nullptr ? *out_q8 : jfb_q8k{};
-    combine_kernel<<<n, 256, 0, s>>>(pos, heads, head_dim, splits, sc, out, q8, out_q8 != nullptr);
+    if (e == cudaSuccess) {
+        e = launch_k(combine_kernel, dim3(n), dim3(256), 0, s, pos, heads, head_dim, splits, sc, out, q8,
+                     out_q8 != nullptr ? 1 : 0);
+    }
+    if (e != cudaSuccess) return status_error(JFB_STATUS_CUDA_ERROR, "jfb_attention: %s", cudaGetErrorString(e));
     return launch_status("jfb_attention");
 }
 

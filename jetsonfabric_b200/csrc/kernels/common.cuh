@@ -9,6 +9,8 @@
 #include <cstdarg>
 #include <cstdint>
 #include <cstdio>
+#include <cstdlib>
+#include <utility>
 
 #include "jetsonfabric/engine.h"
 #include "jfb/jfb_kernels.h"
@@ -61,11 +63,52 @@ inline jfb_status check_q8_tensor_core(const jfb_q8k * q8, uint32_t rows) {
     return status_ok();
 }
 
+// ---- programmatic dependent launch ---------------------------------------------
+//
+// The kernels of the per-step path are launched with programmatic stream
+// serialization (off with JFB_PDL=0): a kernel may start while its predecessor
+// in the stream drains, runs its prologue (barriers, tensor memory, weight
+// loads, per-call metadata), and calls pdl_wait() before it touches anything
+// an earlier kernel writes. Every such kernel also calls pdl_trigger() on
+// entry, which lets the next kernel start as soon as all of its CTAs run.
+// Without the launch attribute both instructions return at once.
+inline bool pdl_enabled() {
+    static const bool on = [] {
+        const char * e = std::getenv("JFB_PDL");
+        return e == nullptr || e[0] != '0';
+    }();
+    return on;
+}
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                            Args &&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    if (pdl_enabled()) {
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+    }
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 inline bool is_kquant(uint32_t type) {
     return type == JF_TENSOR_Q4_K || type == JF_TENSOR_Q6_K || type == JF_TENSOR_Q2_K;
 }
 
 // ---- device helpers --------------------------------------------------------
+
+// Wait until the kernels before this one in the stream have completed and
+// their writes are visible (programmatic dependent launch).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Allow the next kernel in the stream to start launching.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 __device__ __forceinline__ float half_bits_to_float(uint16_t h) {
     return __half2float(__ushort_as_half(h));

@@ -256,6 +256,8 @@ __device__ __forceinline__ void lane_block(const jfb_weight & w, uint64_t block,
 template <uint32_t TYPE>
 __global__ void __launch_bounds__(kWarps * 32) mmv_kquant_kernel(jfb_weight w, ActView a, uint32_t n, float * out,
                                                                Epilogue ep) {
+    pdl_trigger();
+    pdl_wait();
     const uint32_t row = blockIdx.x * kWarps + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     const uint32_t t0 = blockIdx.y * kGroup;
@@ -284,6 +286,8 @@ __global__ void __launch_bounds__(kWarps * 32) mmv_kquant_kernel(jfb_weight w, A
 template <bool HALF>
 __global__ void __launch_bounds__(kWarps * 32) mmv_float_kernel(jfb_weight w, const float * __restrict__ x, uint32_t n,
                                                               float * out, Epilogue ep) {
+    pdl_trigger();
+    pdl_wait();
     const uint32_t row = blockIdx.x * kWarps + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     const uint32_t t0 = blockIdx.y * kGroup;
@@ -332,18 +336,22 @@ extern "C" jfb_status jfb_matmul(const jfb_weight * weight, const jfb_q8k * x_q8
         }
         if (w.cols % kQK != 0) return status_error(JFB_STATUS_INVALID_ARGUMENT, "K-quant columns must be a multiple of 256");
         const ActView a{x_q8->qs, x_q8->d, x_q8->bsums, w.cols};
+        cudaError_t e;
         switch (w.type) {
-        case JF_TENSOR_Q4_K: mmv_kquant_kernel<JF_TENSOR_Q4_K><<<grid, kWarps * 32, 0, s>>>(w, a, n, out, ep); break;
-        case JF_TENSOR_Q6_K: mmv_kquant_kernel<JF_TENSOR_Q6_K><<<grid, kWarps * 32, 0, s>>>(w, a, n, out, ep); break;
-        default: mmv_kquant_kernel<JF_TENSOR_Q2_K><<<grid, kWarps * 32, 0, s>>>(w, a, n, out, ep); break;
+        case JF_TENSOR_Q4_K: e = launch_k(mmv_kquant_kernel<JF_TENSOR_Q4_K>, grid, dim3(kWarps * 32), 0, s, w, a, n, out, ep); break;
+        case JF_TENSOR_Q6_K: e = launch_k(mmv_kquant_kernel<JF_TENSOR_Q6_K>, grid, dim3(kWarps * 32), 0, s, w, a, n, out, ep); break;
+        default: e = launch_k(mmv_kquant_kernel<JF_TENSOR_Q2_K>, grid, dim3(kWarps * 32), 0, s, w, a, n, out, ep); break;
         }
+        if (e != cudaSuccess) return status_error(JFB_STATUS_CUDA_ERROR, "jfb_matmul: %s", cudaGetErrorString(e));
         return launch_status("jfb_matmul(kquant)");
     }
     if (x_f32 == nullptr) return status_error(JFB_STATUS_INVALID_ARGUMENT, "float matmul needs f32 activations");
     if (w.type == JF_TENSOR_F32) {
-        mmv_float_kernel<false><<<grid, kWarps * 32, 0, s>>>(w, x_f32, n, out, ep);
+        const cudaError_t e = launch_k(mmv_float_kernel<false>, grid, dim3(kWarps * 32), 0, s, w, x_f32, n, out, ep);
+        if (e != cudaSuccess) return status_error(JFB_STATUS_CUDA_ERROR, "jfb_matmul: %s", cudaGetErrorString(e));
     } else if (w.type == JF_TENSOR_F16) {
-        mmv_float_kernel<true><<<grid, kWarps * 32, 0, s>>>(w, x_f32, n, out, ep);
+        const cudaError_t e = launch_k(mmv_float_kernel<true>, grid, dim3(kWarps * 32), 0, s, w, x_f32, n, out, ep);
+        if (e != cudaSuccess) return status_error(JFB_STATUS_CUDA_ERROR, "jfb_matmul: %s", cudaGetErrorString(e));
     } else {
         return status_error(JFB_STATUS_UNSUPPORTED, "matmul weight type %u is not supported", w.type);
     }

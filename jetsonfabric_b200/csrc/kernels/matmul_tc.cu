@@ -650,6 +650,7 @@ __global__ void __launch_bounds__(Roles<BN>::kThreads) __maxnreg__(Roles<BN>::kR
     uint32_t * tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
     volatile int * abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
+    pdl_trigger();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint64_t g = gridDim.x;
     const uint64_t w_begin = range_start(blockIdx.x, p.work, g);
@@ -697,11 +698,45 @@ __global__ void __launch_bounds__(Roles<BN>::kThreads) __maxnreg__(Roles<BN>::kR
             uint32_t rs = 0, rph = 0, es = 0, eph = 0;
             uint64_t issued = 0, e_issued = 0;
             bool ok = true;
+            auto issue_weights = [&](uint8_t * r, const Cursor & c, int h, uint64_t * bar) {
+                const int32_t y_w = int32_t(c.tm * kRows);
+                const int32_t x_blk = int32_t(c.b * T::kBlockBytes);
+                tma_load_2d(r + L::kW0Off, &maps.w0, x_blk + int32_t(T::kW0 * h), y_w, bar);
+                if constexpr (T::kW1 > 0) tma_load_2d(r + L::kW1Off, &maps.w1, x_blk + 128 + int32_t(T::kW1 * h), y_w, bar);
+                tma_load_2d(r + L::kScOff, &maps.sc, int32_t(c.b * 16), y_w, bar);
+            };
+            // x coordinates: f16 elements (codes: multiples of 64; partial sums: of 8), bytes for the
+            // weight planes (multiples of 16): all 16-byte aligned
+            auto issue_activations = [&](uint8_t * r, const Cursor & c, int h, uint64_t * bar) {
+                const int32_t y_a = int32_t(c.tn * BN);
+                const int32_t x_codes = int32_t(c.b * kQK + 128 * h);
+                tma_load_2d(r + L::kBOff, &maps.qs, x_codes, y_a, bar);
+                tma_load_2d(r + L::kBOff + L::kBHalf, &maps.qs, x_codes + 64, y_a, bar);
+                if (T::kMins && h == 0) {
+                    tma_load_2d(r + L::kB2Off, &maps.b2, int32_t(c.b * 16), y_a, bar);
+                    tma_load_2d(r + L::kB2Off + uint32_t(BN) * 16, &maps.b2, int32_t(c.b * 16 + 8), y_a, bar);
+                }
+            };
+            // The weights of the first raw stages depend on no earlier kernel:
+            // they are requested before waiting for the previous kernel, so
+            // their latency overlaps its tail (programmatic dependent launch).
+            const uint64_t pre = std::min<uint64_t>(uint64_t(NR), 2 * (w_end - w_begin));
+            {
+                Cursor c0;
+                c0.init(w_begin, nb, p.tiles_m);
+                for (uint64_t k = 0; k < pre; ++k) {
+                    const int h = int(k & 1);
+                    mbar_arrive_expect_tx(&raw_full[k], h == 0 ? L::kTx0 : L::kTx1);  // fresh stages: nothing to wait for
+                    issue_weights(raw + k * L::kRawBytes, c0, h, &raw_full[k]);
+                    if (h == 1) c0.next(nb, p.tiles_m);
+                }
+            }
+            pdl_wait();
             Cursor cur;
             cur.init(w_begin, nb, p.tiles_m);
             for (uint64_t w = w_begin; w < w_end && ok && !*abort_flag; ++w, cur.next(nb, p.tiles_m)) {
                 const uint32_t b = cur.b;
-                const int32_t y_w = int32_t(cur.tm * kRows), y_a = int32_t(cur.tn * BN);
+                const int32_t y_a = int32_t(cur.tn * BN);
                 // the unit's activation scales d[tokens][b] (one row of d_t)
                 if (!mbar_wait(&epi_empty[es], eph ^ 1u, abort_flag, p.error, kErrWaitEpiEmpty)) break;
                 mbar_arrive_expect_tx(&epi_tx[es], uint32_t(BN) * 4);
@@ -712,28 +747,16 @@ __global__ void __launch_bounds__(Roles<BN>::kThreads) __maxnreg__(Roles<BN>::kR
                     eph ^= 1u;
                 }
                 for (int h = 0; h < 2; ++h) {
-                    if (!mbar_wait(&raw_empty[rs], rph ^ 1u, abort_flag, p.error, kErrWaitRawEmpty)) {
-                        ok = false;
-                        break;
-                    }
                     uint8_t * r = raw + rs * L::kRawBytes;
-                    mbar_arrive_expect_tx(&raw_full[rs], h == 0 ? L::kTx0 : L::kTx1);
-                    // x coordinates: f16 elements (codes: multiples of 64; partial sums: of 8), bytes for the
-                    // weight planes (multiples of 16): all 16-byte aligned
-                    const int32_t x_codes = int32_t(b * kQK + 128 * h);
-                    tma_load_2d(r + L::kBOff, &maps.qs, x_codes, y_a, &raw_full[rs]);
-                    tma_load_2d(r + L::kBOff + L::kBHalf, &maps.qs, x_codes + 64, y_a, &raw_full[rs]);
-                    const int32_t x_blk = int32_t(b * T::kBlockBytes);
-                    tma_load_2d(r + L::kW0Off, &maps.w0, x_blk + int32_t(T::kW0 * h), y_w, &raw_full[rs]);
-                    if constexpr (T::kW1 > 0) {
-                        tma_load_2d(r + L::kW1Off, &maps.w1, x_blk + 128 + int32_t(T::kW1 * h), y_w, &raw_full[rs]);
+                    if (issued >= pre) {
+                        if (!mbar_wait(&raw_empty[rs], rph ^ 1u, abort_flag, p.error, kErrWaitRawEmpty)) {
+                            ok = false;
+                            break;
+                        }
+                        mbar_arrive_expect_tx(&raw_full[rs], h == 0 ? L::kTx0 : L::kTx1);
+                        issue_weights(r, cur, h, &raw_full[rs]);
                     }
-                    tma_load_2d(r + L::kScOff, &maps.sc, int32_t(b * 16), y_w, &raw_full[rs]);
-                    if (T::kMins && h == 0) {
-                        tma_load_2d(r + L::kB2Off, &maps.b2, int32_t(b * 16), y_a, &raw_full[rs]);
-                        tma_load_2d(r + L::kB2Off + uint32_t(BN) * 16, &maps.b2, int32_t(b * 16 + 8), y_a,
-                                    &raw_full[rs]);
-                    }
+                    issue_activations(r, cur, h, &raw_full[rs]);
                     ++issued;
                     if (++rs == NR) {
                         rs = 0;
@@ -744,8 +767,16 @@ __global__ void __launch_bounds__(Roles<BN>::kThreads) __maxnreg__(Roles<BN>::kR
             // a stopped kernel must not exit with loads still landing in its
             // shared memory: wait (bounded) for the last issue of every slot
             if (*abort_flag) {
+                // pre-issued stages whose activation boxes were not requested yet
+                // get them now, so that every transaction completes
+                for (uint64_t j = issued; j < pre; ++j) {
+                    Cursor cj;
+                    cj.init(w_begin + j / 2, nb, p.tiles_m);
+                    issue_activations(raw + j * L::kRawBytes, cj, int(j & 1), &raw_full[j]);
+                }
                 volatile int no_abort = 0;
-                for (uint64_t j = issued > uint64_t(NR) ? issued - NR : 0; j < issued; ++j) {
+                const uint64_t last = std::max(issued, pre);
+                for (uint64_t j = last > uint64_t(NR) ? last - NR : 0; j < last; ++j) {
                     (void) mbar_wait(&raw_full[j % NR], uint32_t((j / NR) & 1u), &no_abort, nullptr, 0);
                 }
                 for (uint64_t j = e_issued > uint64_t(kEpiRing) ? e_issued - kEpiRing : 0; j < e_issued; ++j) {
@@ -909,6 +940,7 @@ __global__ void __launch_bounds__(Roles<BN>::kThreads) __maxnreg__(Roles<BN>::kR
         double sum[kCols];
         uint64_t seg_begin = w_begin;
         uint32_t i = 0, es = 0, eph = 0;
+        pdl_wait();  // outputs, residuals and the stream-K workspace are shared with earlier kernels
         Cursor cur;
         cur.init(w_begin, nb, p.tiles_m);
         for (uint64_t w = w_begin; w < w_end; ++w, ++i, cur.next(nb, p.tiles_m)) {

@@ -17,6 +17,8 @@ __device__ __forceinline__ void better(float & v, int & i, float ov, int oi) {
 __global__ void __launch_bounds__(1024) argmax_kernel(const float * __restrict__ x, uint32_t cols, int32_t * out) {
     __shared__ float sv[32];
     __shared__ int si[32];
+    pdl_trigger();
+    pdl_wait();
     const float * row = x + uint64_t(blockIdx.x) * cols;
     float v = -INFINITY;
     int idx = 0x7fffffff;
@@ -105,12 +107,16 @@ __device__ __forceinline__ float codec_half_to_float(uint16_t value) {
 }
 
 __global__ void encode_kernel(const float * __restrict__ in, uint16_t * __restrict__ out, uint64_t count) {
+    pdl_trigger();
+    pdl_wait();
     for (uint64_t i = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < count; i += uint64_t(gridDim.x) * blockDim.x) {
         out[i] = codec_float_to_half(in[i]);
     }
 }
 
 __global__ void decode_kernel(const uint16_t * __restrict__ in, float * __restrict__ out, uint64_t count) {
+    pdl_trigger();
+    pdl_wait();
     for (uint64_t i = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < count; i += uint64_t(gridDim.x) * blockDim.x) {
         out[i] = codec_half_to_float(in[i]);
     }
@@ -129,20 +135,23 @@ using namespace jfb;
 extern "C" jfb_status jfb_argmax(const float * logits, uint32_t n, uint32_t cols, int32_t * out, void * stream) {
     if (logits == nullptr || out == nullptr || cols == 0) return status_error(JFB_STATUS_INVALID_ARGUMENT, "argmax operands are required");
     if (n == 0) return status_ok();
-    argmax_kernel<<<n, 1024, 0, as_stream(stream)>>>(logits, cols, out);
+    const cudaError_t e = launch_k(argmax_kernel, dim3(n), dim3(1024), 0, as_stream(stream), logits, cols, out);
+    if (e != cudaSuccess) return status_error(JFB_STATUS_CUDA_ERROR, "jfb_argmax: %s", cudaGetErrorString(e));
     return launch_status("jfb_argmax");
 }
 
 extern "C" jfb_status jfb_codec_f32_to_f16(const float * in, uint16_t * out, uint64_t count, void * stream) {
     if (count == 0) return status_ok();
     if (in == nullptr || out == nullptr) return status_error(JFB_STATUS_INVALID_ARGUMENT, "codec buffers are required");
-    encode_kernel<<<grid_for(count), 256, 0, as_stream(stream)>>>(in, out, count);
+    const cudaError_t e = launch_k(encode_kernel, dim3(grid_for(count)), dim3(256), 0, as_stream(stream), in, out, count);
+    if (e != cudaSuccess) return status_error(JFB_STATUS_CUDA_ERROR, "jfb_codec_f32_to_f16: %s", cudaGetErrorString(e));
     return launch_status("jfb_codec_f32_to_f16");
 }
 
 extern "C" jfb_status jfb_codec_f16_to_f32(const uint16_t * in, float * out, uint64_t count, void * stream) {
     if (count == 0) return status_ok();
     if (in == nullptr || out == nullptr) return status_error(JFB_STATUS_INVALID_ARGUMENT, "codec buffers are required");
-    decode_kernel<<<grid_for(count), 256, 0, as_stream(stream)>>>(in, out, count);
+    const cudaError_t e = launch_k(decode_kernel, dim3(grid_for(count)), dim3(256), 0, as_stream(stream), in, out, count);
+    if (e != cudaSuccess) return status_error(JFB_STATUS_CUDA_ERROR, "jfb_codec_f16_to_f32: %s", cudaGetErrorString(e));
     return launch_status("jfb_codec_f16_to_f32");
 }

@@ -42,6 +42,8 @@ __global__ void __launch_bounds__(kThreads) rmsnorm_quant_kernel(
     uint32_t cols, float eps, float * __restrict__ out_f32, jfb_q8k q8, int quantize) {
     constexpr int kRounds = kMaxRowChunks / 8;  // 2048 values per round
     __shared__ double red[kThreads / 32];
+    pdl_trigger();
+    pdl_wait();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t row = blockIdx.x;
     const uint64_t src_row = row_index != nullptr ? uint64_t(row_index[row]) : uint64_t(row);
@@ -79,6 +81,8 @@ __global__ void __launch_bounds__(kThreads) rmsnorm_quant_kernel(
 
 // One warp per Q8_K block: grid (ceil(blocks / 8), rows).
 __global__ void __launch_bounds__(kThreads) quantize_kernel(const float * __restrict__ x, uint32_t cols, jfb_q8k q8) {
+    pdl_trigger();
+    pdl_wait();
     const uint32_t blk = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (blk >= cols / kQK) return;  // warp-uniform
     const uint32_t row = blockIdx.y;
@@ -100,6 +104,8 @@ __device__ __forceinline__ float swiglu(float g, float u) {
 __global__ void __launch_bounds__(kThreads) swiglu_quant_kernel(const float * __restrict__ gate, const float * __restrict__ up,
                                                              uint32_t cols, float * __restrict__ out_f32, jfb_q8k q8,
                                                              int quantize) {
+    pdl_trigger();
+    pdl_wait();
     const uint32_t blk = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (blk * kQK >= cols) return;  // warp-uniform
     const uint32_t row = blockIdx.y;
@@ -143,8 +149,9 @@ extern "C" jfb_status jfb_rmsnorm_quant(const float * x, const int32_t * row_ind
     if (s.code != JFB_STATUS_OK) return s;
     if (n == 0) return status_ok();
     const jfb_q8k q8 = out_q8 != nullptr ? *out_q8 : jfb_q8k{};
-    rmsnorm_quant_kernel<<<n, kThreads, 0, as_stream(stream)>>>(x, row_index, norm_weight, cols, eps, out_f32, q8,
-                                                                 out_q8 != nullptr);
+    const cudaError_t e = launch_k(rmsnorm_quant_kernel, dim3(n), dim3(kThreads), 0, as_stream(stream), x, row_index,
+                                   norm_weight, cols, eps, out_f32, q8, out_q8 != nullptr ? 1 : 0);
+    if (e != cudaSuccess) return status_error(JFB_STATUS_CUDA_ERROR, "jfb_rmsnorm_quant: %s", cudaGetErrorString(e));
     return launch_status("jfb_rmsnorm_quant");
 }
 
@@ -154,7 +161,9 @@ extern "C" jfb_status jfb_quantize_q8k(const float * x, uint32_t n, uint32_t col
     if (s.code != JFB_STATUS_OK) return s;
     if (n == 0) return status_ok();
     if (n > 65535u) return status_error(JFB_STATUS_INVALID_ARGUMENT, "Q8_K rows above 65535 per call");
-    quantize_kernel<<<dim3((cols / kQK + 7) / 8, n), kThreads, 0, as_stream(stream)>>>(x, cols, *out);
+    const cudaError_t e = launch_k(quantize_kernel, dim3((cols / kQK + 7) / 8, n), dim3(kThreads), 0, as_stream(stream), x,
+                                   cols, *out);
+    if (e != cudaSuccess) return status_error(JFB_STATUS_CUDA_ERROR, "jfb_quantize_q8k: %s", cudaGetErrorString(e));
     return launch_status("jfb_quantize_q8k");
 }
 
@@ -168,7 +177,8 @@ extern "C" jfb_status jfb_swiglu_quant(const float * gate, const float * up, uin
     if (n == 0 || cols == 0) return status_ok();
     const jfb_q8k q8 = out_q8 != nullptr ? *out_q8 : jfb_q8k{};
     if (n > 65535u) return status_error(JFB_STATUS_INVALID_ARGUMENT, "swiglu rows above 65535 per call");
-    swiglu_quant_kernel<<<dim3((cols + 8 * kQK - 1) / (8 * kQK), n), kThreads, 0, as_stream(stream)>>>(
-        gate, up, cols, out_f32, q8, out_q8 != nullptr);
+    const cudaError_t e = launch_k(swiglu_quant_kernel, dim3((cols + 8 * kQK - 1) / (8 * kQK), n), dim3(kThreads), 0,
+                                   as_stream(stream), gate, up, cols, out_f32, q8, out_q8 != nullptr ? 1 : 0);
+    if (e != cudaSuccess) return status_error(JFB_STATUS_CUDA_ERROR, "jfb_swiglu_quant: %s", cudaGetErrorString(e));
     return launch_status("jfb_swiglu_quant");
 }

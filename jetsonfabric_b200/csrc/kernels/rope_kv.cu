@@ -25,9 +25,11 @@ __global__ void __launch_bounds__(kThreads) rope_kv_kernel(float * __restrict__ 
                                                          uint32_t kv_heads, uint32_t head_dim, uint32_t rope_dims,
                                                          const float2 * __restrict__ table, uint32_t table_positions,
                                                          const jfb_kv_slot * __restrict__ slots, uint32_t layer) {
+    pdl_trigger();
     const uint32_t r = blockIdx.x;
-    const int32_t p = pos[r];
+    const int32_t p = pos[r];                 // per-call metadata: written before the first kernel of the call
     const jfb_kv_slot slot = slots[seq[r]];
+    pdl_wait();                                // q, k, v come from the projection before this kernel
     if (p < 0 || uint32_t(p) >= slot.capacity || uint32_t(p) >= table_positions) return;  // never issued by the engine
     const uint32_t pairs = rope_dims / 2;
     const float2 * cs = table + uint64_t(p) * pairs;
@@ -93,8 +95,9 @@ extern "C" jfb_status jfb_rope_kv_append(float * q, const float * k, const float
         return status_error(JFB_STATUS_INVALID_ARGUMENT, "rope/kv append dimensions are inconsistent");
     }
     if (n == 0) return status_ok();
-    rope_kv_kernel<<<n, kThreads, 0, as_stream(stream)>>>(q, k, v, seq, pos, heads, kv_heads, head_dim, rope_dims,
-                                                          reinterpret_cast<const float2 *>(rope_table), table_positions,
-                                                          slots, layer);
+    const cudaError_t e = launch_k(rope_kv_kernel, dim3(n), dim3(kThreads), 0, as_stream(stream), q, k, v, seq, pos, heads,
+                                   kv_heads, head_dim, rope_dims, reinterpret_cast<const float2 *>(rope_table),
+                                   table_positions, slots, layer);
+    if (e != cudaSuccess) return status_error(JFB_STATUS_CUDA_ERROR, "jfb_rope_kv_append: %s", cudaGetErrorString(e));
     return launch_status("jfb_rope_kv_append");
 }

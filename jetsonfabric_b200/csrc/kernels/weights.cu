@@ -139,6 +139,8 @@ __global__ void dequantize_kernel(jfb_weight w, float * __restrict__ out) {
 
 __global__ void embed_kernel(jfb_weight w, const int32_t * __restrict__ tokens, float * __restrict__ hidden,
                              int32_t * error_flag) {
+    pdl_trigger();
+    pdl_wait();  // the token ids may be the previous step's greedy tokens
     const int r = blockIdx.x;
     const int32_t tok = tokens[r];
     float * out = hidden + uint64_t(r) * w.cols;
@@ -245,6 +247,7 @@ extern "C" jfb_status jfb_embed_rows(const jfb_weight * embd, const int32_t * to
     if (n == 0) return status_ok();
     jfb_status s = check_weight_shape(embd->type, embd->rows, embd->cols);
     if (s.code != JFB_STATUS_OK) return s;
-    embed_kernel<<<n, 256, 0, as_stream(stream)>>>(*embd, tokens, hidden, error_flag);
+    const cudaError_t e = launch_k(embed_kernel, dim3(n), dim3(256), 0, as_stream(stream), *embd, tokens, hidden, error_flag);
+    if (e != cudaSuccess) return status_error(JFB_STATUS_CUDA_ERROR, "jfb_embed_rows: %s", cudaGetErrorString(e));
     return launch_status("jfb_embed_rows");
 }

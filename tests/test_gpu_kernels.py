@@ -261,3 +261,63 @@ def test_rope_kv_and_attention(K, heads, kv_heads, hd):
         L.orc_attention_row(qrot.ctypes.data, kcu.ctypes.data, vcu.ctypes.data, p, heads, kv_heads, hd, ref.ctypes.data)
         got = out[i].cpu().numpy()
         assert np.array_equal(got.view(np.uint32), ref.view(np.uint32)), np.abs(got - ref).max()
+
+
+def _attention_case(K, rng, heads, kv_heads, hd, lengths, rows):
+    """KV caches of random f16 rows; `rows` = [(sequence, position)]: the
+    query rows of one jfb_attention call, with max_keys the longest row."""
+    kvd = kv_heads * hd
+    cap = max(lengths)
+    kbuf = [torch.from_numpy(rng.normal(0, 1, (1, cap, kvd)).astype(np.float16)).cuda() for _ in lengths]
+    vbuf = [torch.from_numpy(rng.normal(0, 1, (1, cap, kvd)).astype(np.float16)).cuda() for _ in lengths]
+    slots = (K.KvSlot * len(lengths))()
+    for i in range(len(lengths)):
+        slots[i] = K.KvSlot(kbuf[i].data_ptr(), vbuf[i].data_ptr(), cap, 0)
+    slots_dev = torch.frombuffer(bytearray(bytes(slots)), dtype=torch.uint8).cuda()
+    n = len(rows)
+    q = rng.normal(0, 1, (n, heads * hd)).astype(np.float32)
+    seq = torch.tensor([s for s, _ in rows], dtype=torch.int32, device="cuda")
+    pos = torch.tensor([p for _, p in rows], dtype=torch.int32, device="cuda")
+    max_keys = max(p for _, p in rows) + 1
+    scratch = torch.empty(K.attention_scratch_bytes(n, heads, hd, max_keys), dtype=torch.uint8, device="cuda")
+    out = torch.empty((n, heads * hd), dtype=torch.float32, device="cuda")
+    q8 = K.Q8Buffer(n, heads * hd) if (heads * hd) % 256 == 0 else None
+    K.attention(torch.from_numpy(q).cuda(), seq, pos, heads, kv_heads, hd, max_keys, slots_dev, 0, scratch, out,
+                out_q8=q8)
+    torch.cuda.synchronize()
+    got = out.cpu().numpy()
+    L = ob.lib()
+    kc = [np.ascontiguousarray(b[0].cpu().numpy().view(np.uint16)) for b in kbuf]
+    vc = [np.ascontiguousarray(b[0].cpu().numpy().view(np.uint16)) for b in vbuf]
+    for i, (s, p) in enumerate(rows):
+        ref = np.empty(heads * hd, np.float32)
+        L.orc_attention_row(q[i].ctypes.data, kc[s].ctypes.data, vc[s].ctypes.data, p, heads, kv_heads, hd,
+                            ref.ctypes.data)
+        assert np.array_equal(got[i].view(np.uint32), ref.view(np.uint32)), (i, s, p, np.abs(got[i] - ref).max())
+    if q8 is not None:  # the fused Q8_K output equals quantizing the rows
+        again = K.Q8Buffer(n, heads * hd)
+        K.quantize_q8k(out, again)
+        torch.cuda.synchronize()
+        for a, b in [(q8.qs, again.qs), (q8.d, again.d), (q8.bsums, again.bsums), (q8.qs_f16, again.qs_f16),
+                     (q8.d_t, again.d_t)]:
+            assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("heads,kv_heads,lengths", [
+    (16, 2, [300, 340]),   # 640 causal rows: 8 rows per CTA, one CTA per key range
+    (16, 2, [600, 100]),   # 700 rows, rows up to 600 keys: clusters of 2 CTAs
+    (40, 8, [200]),        # 5 query heads per kv head: padded MMA rows, separate quantization
+])
+def test_prefill_attention_matches_oracle(K, heads, kv_heads, lengths):
+    """Every causal row of whole prompts in one call (the prefill shape)."""
+    rng = np.random.default_rng(sum(lengths) + heads)
+    rows = [(s, p) for s, length in enumerate(lengths) for p in range(length)]
+    _attention_case(K, rng, heads, kv_heads, 128, lengths, rows)
+
+
+@pytest.mark.parametrize("positions", [[0, 4500, 9000], [8191, 17, 5000, 1, 0, 3000]])
+def test_long_decode_attention_matches_oracle(K, positions):
+    """Decode rows with long contexts: keys split over clusters of up to 8 CTAs."""
+    rng = np.random.default_rng(len(positions))
+    lengths = [p + 1 for p in positions]
+    _attention_case(K, rng, 16, 2, 128, lengths, list(enumerate(positions)))
