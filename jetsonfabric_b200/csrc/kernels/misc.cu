@@ -22,9 +22,25 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float * __restrict__
     const float * row = x + uint64_t(blockIdx.x) * cols;
     float v = -INFINITY;
     int idx = 0x7fffffff;
-    for (uint32_t c = threadIdx.x; c < cols; c += blockDim.x) {
+    // eight loads in flight per thread; each thread visits its indices in
+    // increasing order, so `>` keeps the first index of its maximum
+    constexpr uint32_t kUnroll = 8;
+    uint32_t c = threadIdx.x;
+    for (; c + (kUnroll - 1) * blockDim.x < cols; c += kUnroll * blockDim.x) {
+        float e[kUnroll];
+#pragma unroll
+        for (uint32_t u = 0; u < kUnroll; ++u) e[u] = __ldg(row + c + u * blockDim.x);
+#pragma unroll
+        for (uint32_t u = 0; u < kUnroll; ++u) {
+            if (e[u] > v) {
+                v = e[u];
+                idx = int(c + u * blockDim.x);
+            }
+        }
+    }
+    for (; c < cols; c += blockDim.x) {
         const float e = row[c];
-        if (e > v) {  // strided scan visits indices in increasing order per thread
+        if (e > v) {
             v = e;
             idx = int(c);
         }

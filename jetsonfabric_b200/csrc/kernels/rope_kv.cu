@@ -17,8 +17,12 @@
 namespace jfb {
 namespace {
 
-constexpr int kThreads = 128;
+constexpr int kThreads = 256;
 
+// One element per thread: grid (rows, ceil((heads * rope_dims / 2 + kv_dim) / 256)). Items
+// [0, heads * pairs) are the rotated pairs of q (in place); the next kv_dim
+// items are the k elements (rotated or passed through) and v elements of the
+// appended cache row. Each thread does one round of independent loads.
 __global__ void __launch_bounds__(kThreads) rope_kv_kernel(float * __restrict__ q, const float * __restrict__ k,
                                                          const float * __restrict__ v, const int32_t * __restrict__ seq,
                                                          const int32_t * __restrict__ pos, uint32_t heads,
@@ -29,25 +33,24 @@ __global__ void __launch_bounds__(kThreads) rope_kv_kernel(float * __restrict__ 
     const uint32_t r = blockIdx.x;
     const int32_t p = pos[r];                 // per-call metadata: written before the first kernel of the call
     const jfb_kv_slot slot = slots[seq[r]];
-    pdl_wait();                                // q, k, v come from the projection before this kernel
     if (p < 0 || uint32_t(p) >= slot.capacity || uint32_t(p) >= table_positions) return;  // never issued by the engine
     const uint32_t pairs = rope_dims / 2;
     const float2 * cs = table + uint64_t(p) * pairs;
     const uint32_t hd = heads * head_dim, kvd = kv_heads * head_dim;
-    float * qr = q + uint64_t(r) * hd;
-    for (uint32_t idx = threadIdx.x; idx < heads * pairs; idx += kThreads) {
+    const uint32_t idx = blockIdx.y * kThreads + threadIdx.x;
+    const uint32_t qitems = heads * pairs;
+    pdl_wait();                                // q, k, v come from the projection before this kernel
+    if (idx < qitems) {
         const uint32_t h = idx / pairs, i = idx % pairs;
-        float * x = qr + h * head_dim;
+        float * x = q + uint64_t(r) * hd + h * head_dim;
         const float2 c = cs[i];
         const float x0 = x[i], x1 = x[i + pairs];
         x[i] = __fsub_rn(__fmul_rn(x0, c.x), __fmul_rn(x1, c.y));
         x[i + pairs] = __fadd_rn(__fmul_rn(x0, c.y), __fmul_rn(x1, c.x));
-    }
-    const uint64_t row = (uint64_t(layer) * slot.capacity + uint64_t(p)) * kvd;
-    const float * kr = k + uint64_t(r) * kvd;
-    const float * vr = v + uint64_t(r) * kvd;
-    for (uint32_t idx = threadIdx.x; idx < kvd; idx += kThreads) {
-        const uint32_t h = idx / head_dim, e = idx % head_dim;
+    } else if (idx < qitems + kvd) {
+        const uint32_t e_all = idx - qitems;
+        const uint32_t h = e_all / head_dim, e = e_all % head_dim;
+        const float * kr = k + uint64_t(r) * kvd;
         float y;
         if (e < rope_dims) {
             const uint32_t i = e % pairs;
@@ -56,10 +59,11 @@ __global__ void __launch_bounds__(kThreads) rope_kv_kernel(float * __restrict__ 
             y = e < pairs ? __fsub_rn(__fmul_rn(x0, c.x), __fmul_rn(x1, c.y))
                           : __fadd_rn(__fmul_rn(x0, c.y), __fmul_rn(x1, c.x));
         } else {
-            y = kr[idx];
+            y = kr[e_all];
         }
-        slot.k[row + idx] = float_to_half_bits(y);
-        slot.v[row + idx] = float_to_half_bits(vr[idx]);
+        const uint64_t row = (uint64_t(layer) * slot.capacity + uint64_t(p)) * kvd;
+        slot.k[row + e_all] = float_to_half_bits(y);
+        slot.v[row + e_all] = float_to_half_bits(v[uint64_t(r) * kvd + e_all]);
     }
 }
 
@@ -95,7 +99,9 @@ extern "C" jfb_status jfb_rope_kv_append(float * q, const float * k, const float
         return status_error(JFB_STATUS_INVALID_ARGUMENT, "rope/kv append dimensions are inconsistent");
     }
     if (n == 0) return status_ok();
-    const cudaError_t e = launch_k(rope_kv_kernel, dim3(n), dim3(kThreads), 0, as_stream(stream), q, k, v, seq, pos, heads,
+    const uint32_t items = heads * (rope_dims / 2) + kv_heads * head_dim;
+    const cudaError_t e = launch_k(rope_kv_kernel, dim3(n, (items + kThreads - 1) / kThreads), dim3(kThreads), 0,
+                                   as_stream(stream), q, k, v, seq, pos, heads,
                                    kv_heads, head_dim, rope_dims, reinterpret_cast<const float2 *>(rope_table),
                                    table_positions, slots, layer);
     if (e != cudaSuccess) return status_error(JFB_STATUS_CUDA_ERROR, "jfb_rope_kv_append: %s", cudaGetErrorString(e));
