@@ -46,7 +46,7 @@
 // per-tile, per-warp counter) adds all contributors' partials in CTA order, so
 // the result does not depend on timing and no CTA ever waits for another.
 //
-// Warp roles (BN = 32: 18 warps; BN = 64: 14 warps):
+// Warp roles (BN = 32: 19 warps; BN = 64: 15 warps):
 //   epilogue    8 warps: warp w owns TMEM lanes 32(w % 4)..+31 (weight rows)
 //               and token columns (BN/2)(w / 4)..+BN/2-1;
 //   converters  8 warps for BN = 32 (two threads per weight row, 64 values
@@ -54,9 +54,10 @@
 //               weight codes -> exact f16 products in TMEM (tcgen05.st), the
 //               mins -> a K = 16 shared-memory tile, and each row's block
 //               scale word -> the epilogue ring;
-//   MMA         one thread: TMEM allocation and the tcgen05.mma chain of each
-//               half-block; its commits free the A stage, the raw stage (which
-//               holds B) and hand the accumulator to the epilogue;
+//   MMA         two warps, one issuing thread each, for the even and the odd
+//               units (the first also allocates TMEM): the tcgen05.mma chain
+//               of each half-block; commits free the A stage, the raw stage
+//               (which holds B) and hand the accumulator to the epilogue;
 //   TMA         one thread: the 2D loads (cp.async.bulk.tensor, no multicast)
 //               of the raw stages (weights, scale bytes, f16 codes, f16
 //               partial sums) and of each unit's activation scales, several
@@ -140,8 +141,12 @@ struct Roles {
     static constexpr int kConvThreads = kConvWarps * 32;
     static constexpr int kParts = kConvThreads / kRows;  // converter threads per weight row
     static constexpr int kScaleWriterWarps = 4;          // the part-0 converter warps
+    // two MMA warps issue alternate units: a memory read by an issuing
+    // thread (its barrier waits) stalls its issue for hundreds of cycles, and
+    // the other thread's MMAs keep the tensor pipe busy meanwhile
     static constexpr int kMmaWarp = kEpiWarps + kConvWarps;
-    static constexpr int kTmaWarp = kMmaWarp + 1;
+    static constexpr int kMmaWarps = 2;
+    static constexpr int kTmaWarp = kMmaWarp + kMmaWarps;
     static constexpr int kWarps = kTmaWarp + 1;
     static constexpr int kThreads = kWarps * 32;
     // registers per thread: each of the SM's 4 sub-partitions has 16 K
@@ -646,8 +651,8 @@ __global__ void __launch_bounds__(Roles<BN>::kThreads) __maxnreg__(Roles<BN>::kR
     uint64_t * epi_full = acc_empty + 2;                   // [kEpiRing] weight scale words (converters)
     uint64_t * epi_tx = epi_full + kEpiRing;               // [kEpiRing] activation d landed (TMA)
     uint64_t * epi_empty = epi_tx + kEpiRing;              // [kEpiRing]
-    uint64_t * drain = epi_empty + kEpiRing;               // [1]
-    uint32_t * tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+    uint64_t * drain = epi_empty + kEpiRing;               // [kMmaWarps]
+    uint32_t * tmem_slot = reinterpret_cast<uint32_t *>(drain + R::kMmaWarps);
     volatile int * abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     pdl_trigger();
@@ -675,7 +680,7 @@ __global__ void __launch_bounds__(Roles<BN>::kThreads) __maxnreg__(Roles<BN>::kR
             mbar_init(&epi_tx[e], 1);
             mbar_init(&epi_empty[e], R::kEpiWarps);
         }
-        mbar_init(drain, 1);
+        for (int d = 0; d < R::kMmaWarps; ++d) mbar_init(&drain[d], 1);
         // the swizzled boxes need a 1024-byte aligned ring; stop before any load otherwise
         const bool aligned = (smem_u32(smem) & 1023u) == 0;
         *abort_flag = aligned ? 0 : 1;
@@ -870,20 +875,32 @@ __global__ void __launch_bounds__(Roles<BN>::kThreads) __maxnreg__(Roles<BN>::kR
             }
             if (!ok) break;
         }
-    } else if (warp == R::kMmaWarp) {
-        // ---------------- MMA issue (one thread) ----------------
-        if (lane == 0) {
+    } else if (warp >= R::kMmaWarp && warp < R::kTmaWarp) {
+        // ---------------- MMA issue (one thread per MMA warp) ----------------
+        // With A stages in a multiple of 4, MMA warp `mid` issues the units i
+        // with i % 2 == mid: those are the units of accumulator buffer `mid`
+        // and of A stages {2 mid, 2 mid + 1} (mod 4), so every barrier a thread
+        // waits on is used by that thread alone and its phases come in order.
+        // With fewer stages one thread issues every unit.
+        constexpr uint32_t kIssuers = NS % 4 == 0 ? 2u : 1u;
+        const uint32_t mid = uint32_t(warp - R::kMmaWarp);
+        if (lane == 0 && mid < kIssuers) {
             constexpr uint32_t idesc = instr_desc(kRows, BN);
-            uint32_t stage = 0, phase = 0, rs = 0, rph = 0, i = 0;
             bool ok = true;
-            for (uint64_t w = w_begin; w < w_end && ok && !*abort_flag; ++w, ++i) {
+            uint32_t i = mid;
+            for (uint64_t w = w_begin + mid; w < w_end && ok && !*abort_flag; w += kIssuers, i += kIssuers) {
                 const uint32_t acc = i & 1u, use = i >> 1;
                 if (!mbar_wait(&acc_empty[acc], (use & 1u) ^ 1u, abort_flag, p.error, kErrWaitAccEmpty)) break;
                 tc_fence_after();
                 const uint32_t d = tmem + acc * (T::kAcc * BN);
                 for (int h = 0; h < 2; ++h) {
+                    const uint64_t hb = 2 * uint64_t(i) + uint64_t(h);  // half-block index of the CTA's range
+                    const uint32_t stage = uint32_t(hb % NS), phase = uint32_t((hb / NS) & 1u);
+                    const uint32_t rs = uint32_t(hb % NR), rph = uint32_t((hb / NR) & 1u);
+                    // (the converters waited for the raw stage before completing full[stage];
+                    // with two issuers the raw barriers are shared, so only one waits on them)
                     if (!mbar_wait(&full[stage], phase, abort_flag, p.error, kErrWaitFull) ||
-                        !mbar_wait(&raw_full[rs], rph, abort_flag, p.error, kErrWaitRawFull)) {
+                        (kIssuers == 1 && !mbar_wait(&raw_full[rs], rph, abort_flag, p.error, kErrWaitRawFull))) {
                         ok = false;
                         break;
                     }
@@ -912,21 +929,13 @@ __global__ void __launch_bounds__(Roles<BN>::kThreads) __maxnreg__(Roles<BN>::kR
                     }
                     mma_commit(&empty[stage]);   // the A stage is free once these MMAs are done
                     mma_commit(&raw_empty[rs]);  // and so is the raw stage that holds B
-                    if (++stage == NS) {
-                        stage = 0;
-                        phase ^= 1u;
-                    }
-                    if (++rs == NR) {
-                        rs = 0;
-                        rph ^= 1u;
-                    }
                 }
                 if (ok) mma_commit(&acc_full[acc]);
             }
             // every issued MMA completes before TMEM is released
-            mma_commit(drain);
+            mma_commit(&drain[mid]);
             volatile int no_abort = 0;
-            (void) mbar_wait(drain, 0, &no_abort, nullptr, 0);
+            (void) mbar_wait(&drain[mid], 0, &no_abort, nullptr, 0);
         }
         __syncwarp();
     } else {
