@@ -83,6 +83,9 @@ def parse():
     p.add_argument("--matmul-shape", choices=sorted(MATMUL_SHAPES), default=None,
                    help="time only the tcgen05 K-quant matmul on one weight shape of the workload (profiling target)")
     p.add_argument("--matmul-rows", type=int, default=32, help="activation rows for --matmul-shape")
+    p.add_argument("--attention-shape", choices=["decode", "prefill"], default=None,
+                   help="time only jfb_attention on the workload's decode (32 rows x 768 keys) or prefill "
+                        "(32 x 512 causal rows) shape (profiling target)")
     return p.parse_args()
 
 
@@ -508,6 +511,50 @@ def run_matmul_shape(args) -> dict:
             "gbs": round(len(raw) / (med * 1e-6) / 1e9, 1), "l2": f"{copies} weight copies rotated"}
 
 
+def run_attention_shape(args) -> dict:
+    """jfb_attention alone on the 3B workload's attention shape: random F16
+    KV caches for 32 sequences, 16 query heads over 2 KV heads (head_dim 128),
+    Q8_K output fused; `warmup` untimed then `steps` timed launches (CUDA
+    events on the launching stream)."""
+    import torch
+    from jetsonfabric_b200 import kernels as K
+
+    heads, kvh, hd, n_seq = 16, 2, 128, args.concurrency
+    ctx = 768 if args.attention_shape == "decode" else 512
+    rows_per_seq = 1 if args.attention_shape == "decode" else ctx
+    kvd = kvh * hd
+    gen = torch.Generator(device="cuda").manual_seed(args.seed)
+    kb = torch.randn(n_seq, 1, ctx, kvd, device="cuda", generator=gen).half()
+    vb = torch.randn(n_seq, 1, ctx, kvd, device="cuda", generator=gen).half()
+    slots = (K.KvSlot * n_seq)()
+    for i in range(n_seq):
+        slots[i] = K.KvSlot(kb[i].data_ptr(), vb[i].data_ptr(), ctx, 0)
+    slots_dev = torch.frombuffer(bytearray(bytes(slots)), dtype=torch.uint8).cuda()
+    rows = [(s, p) for s in range(n_seq) for p in range(ctx - rows_per_seq, ctx)]
+    n = len(rows)
+    seq = torch.tensor([s for s, _ in rows], dtype=torch.int32, device="cuda")
+    pos = torch.tensor([p for _, p in rows], dtype=torch.int32, device="cuda")
+    q = torch.randn(n, heads * hd, device="cuda", generator=gen)
+    scratch = torch.empty(K.attention_scratch_bytes(n, heads, hd, ctx), dtype=torch.uint8, device="cuda")
+    out = torch.empty(n, heads * hd, device="cuda")
+    q8 = K.Q8Buffer(n, heads * hd)
+    for _ in range(max(args.warmup, 0)):
+        K.attention(q, seq, pos, heads, kvh, hd, ctx, slots_dev, 0, scratch, out, out_q8=q8)
+    torch.cuda.synchronize()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2 * args.steps)]
+    for i in range(args.steps):
+        ev[2 * i].record()
+        K.attention(q, seq, pos, heads, kvh, hd, ctx, slots_dev, 0, scratch, out, out_q8=q8)
+        ev[2 * i + 1].record()
+    torch.cuda.synchronize()
+    us = sorted(ev[2 * i].elapsed_time(ev[2 * i + 1]) * 1000 for i in range(args.steps))
+    med = us[len(us) // 2]
+    kv_bytes = sum(p + 1 for _, p in rows) * kvd * 2 * 2
+    return {"kernel": "jfb_attention", "shape": args.attention_shape, "rows": n, "keys_max": ctx, "heads": heads,
+            "kv_heads": kvh, "head_dim": hd, "launches": args.steps, "median_us": round(med, 2),
+            "kv_bytes": kv_bytes, "kv_gbs": round(kv_bytes / (med * 1e-6) / 1e9, 1)}
+
+
 def traffic_from_profiles():
     path = REPO / "profiles" / "decode_matmul_traffic.json"
     if path.exists():
@@ -594,6 +641,9 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.attention_shape is not None:
+        print(json.dumps(run_attention_shape(args)), flush=True)
+        return
     if args.matmul_shape is not None:
         result = run_matmul_shape(args)
     elif args.impl == "reference":
