@@ -1267,7 +1267,11 @@ jfb_status launch(TcParams & p, const jfb_q8k & x, uint32_t cols, uint32_t grid,
             attribute_set[dev] = true;
         }
     }
-    kernel<<<grid, R::kThreads, bytes, s>>>(maps, p);
+    // programmatic dependent launch: the prologue (barriers, TMEM, the first
+    // weight loads) overlaps the previous kernel; every write follows the
+    // kernel's griddepcontrol.wait
+    const cudaError_t e = launch_k(kernel, dim3(grid), dim3(R::kThreads), bytes, s, maps, p);
+    if (e != cudaSuccess) return status_error(JFB_STATUS_CUDA_ERROR, "jfb_matmul_tc: %s", cudaGetErrorString(e));
     return launch_status("jfb_matmul_tc");
 }
 
