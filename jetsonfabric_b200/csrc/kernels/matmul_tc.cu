@@ -89,9 +89,8 @@ constexpr uint32_t kTailBytes = 1024;                 // barriers, TMEM slot, fl
 constexpr uint64_t kWaitNs = 2000000000ull;           // bound of every pipeline wait
 constexpr uint32_t kSuspendNs = 1000000;              // longest single suspension of a waiting thread
 constexpr uint32_t kTmemCols = 512;                   // one CTA per SM owns all of TMEM
-constexpr int kEpiRing = 4;                           // units of epilogue scales staged ahead
-constexpr uint32_t kEpiSlotBytes = 1024;              // [128] weight scale words, then [BN] activation d
-constexpr uint32_t kEpiDaOff = 512;
+constexpr int kEpiRing = 8;                           // units of activation scales staged ahead
+constexpr uint32_t kEpiSlotBytes = 256;               // [BN] activation d
 constexpr int kMaxBN = 64;
 
 enum : int {
@@ -137,17 +136,24 @@ template <int BN>
 struct Roles {
     static constexpr int kEpiWarps = 8;       // 4 TMEM lane quarters x 2 column halves
     static constexpr int kCols = BN / 2;      // token columns per epilogue thread
-    static constexpr int kConvWarps = BN == 32 ? 8 : 4;
-    static constexpr int kConvThreads = kConvWarps * 32;
-    static constexpr int kParts = kConvThreads / kRows;  // converter threads per weight row
-    static constexpr int kScaleWriterWarps = 4;          // the part-0 converter warps
+    // converter groups: with two, group g converts half-block g of every
+    // unit, so the two halves of a unit are converted concurrently
+    static constexpr int kGroups = BN == 32 ? 2 : 1;
+    static constexpr int kGroupWarps = BN == 32 ? 8 : 4;
+    static constexpr int kConvWarps = kGroups * kGroupWarps;
+    static constexpr int kParts = kGroupWarps * 32 / kRows;  // converter threads per weight row in a group
+    // the epilogue's per-(row, token) double sums: shared memory for 32-token
+    // tiles (which frees the registers for the second converter group),
+    // registers for 64-token tiles
+    static constexpr bool kSmemSums = BN == 32;
     // two MMA warps issue alternate units: a memory read by an issuing
     // thread (its barrier waits) stalls its issue for hundreds of cycles, and
     // the other thread's MMAs keep the tensor pipe busy meanwhile
     static constexpr int kMmaWarp = kEpiWarps + kConvWarps;
     static constexpr int kMmaWarps = 2;
     static constexpr int kTmaWarp = kMmaWarp + kMmaWarps;
-    static constexpr int kWarps = kTmaWarp + 1;
+    static constexpr int kTmaWarps = 2;  // one TMA-issuing thread per half-block
+    static constexpr int kWarps = kTmaWarp + kTmaWarps;
     static constexpr int kThreads = kWarps * 32;
     // registers per thread: each of the SM's 4 sub-partitions has 16 K
     // registers for the warps w with w % 4 == its index, allocated in
@@ -162,7 +168,8 @@ struct Roles {
 //   rows, the scale/header box [128][16 B] and, for types with mins in half 0,
 //   the f16 partial sums as two boxes [BN][16 B];
 //   operand stage: the K = 16 mins tile of A (types with mins);
-//   epilogue ring: per unit the weight rows' scale words and the activation d.
+//   epilogue sums: [BN][128] doubles when the epilogue keeps them in shared memory;
+//   epilogue ring: per unit the activation scales d of the tile's tokens.
 template <uint32_t TYPE, int BN>
 struct Layout {
     using T = TypeTraits<TYPE>;
@@ -178,12 +185,16 @@ struct Layout {
     static constexpr uint32_t kRawBytes = (kTx0 + 1023) / 1024 * 1024;
     static constexpr uint32_t kAccCols = 2 * T::kAcc * uint32_t(BN);  // both accumulator buffers
     static constexpr uint32_t kACols = T::kPlanes * (kKStage / 2);    // one A stage: 64 columns per plane
+    // with two converter groups each group owns every other A stage and raw
+    // stage, so both counts are even
+    static constexpr int kStep = Roles<BN>::kGroups;
     static constexpr int kNsFit = int((kTmemCols - kAccCols) / kACols);
-    static constexpr int NS = kNsFit < 4 ? kNsFit : 4;
+    static constexpr int NS = (kNsFit < 4 ? kNsFit : 4) / kStep * kStep;
     static constexpr uint32_t kOpBytes = T::kMins ? kA2Bytes : 0;
-    static constexpr uint32_t kFixed = uint32_t(NS) * kOpBytes + kEpiRing * kEpiSlotBytes + kTailBytes;
+    static constexpr uint32_t kSumBytes = Roles<BN>::kSmemSums ? uint32_t(kRows) * BN * 8 : 0;
+    static constexpr uint32_t kFixed = uint32_t(NS) * kOpBytes + kSumBytes + kEpiRing * kEpiSlotBytes + kTailBytes;
     static constexpr int kNrFit = int((kMaxSmem - kFixed) / kRawBytes);
-    static constexpr int NR = kNrFit < 12 ? kNrFit : 12;
+    static constexpr int NR = (kNrFit < 12 ? kNrFit : 12) / kStep * kStep;
     static constexpr uint32_t kSmem = uint32_t(NR) * kRawBytes + kFixed;
 };
 
@@ -254,6 +265,17 @@ __device__ __forceinline__ bool mbar_wait(uint64_t * bar, uint32_t parity, volat
     return mbar_wait_slow(bar, parity, abort_flag, error, code);
 }
 
+// Two bounded waits whose first polls are issued together, so that two
+// phases that have already completed cost one shared-memory round trip.
+__device__ __forceinline__ bool mbar_wait2(uint64_t * bar_a, uint32_t parity_a, int code_a, uint64_t * bar_b,
+                                           uint32_t parity_b, int code_b, volatile int * abort_flag, int * error) {
+    const bool a = mbar_try_wait(bar_a, parity_a);
+    const bool b = mbar_try_wait(bar_b, parity_b);
+    if (a && b) return true;
+    return (a || mbar_wait_slow(bar_a, parity_a, abort_flag, error, code_a)) &&
+           (b || mbar_wait_slow(bar_b, parity_b, abort_flag, error, code_b));
+}
+
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t * bar, uint32_t bytes) {
     asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(smem_u32(bar)),
                  "r"(bytes)
@@ -267,6 +289,16 @@ __device__ __forceinline__ void tma_load_2d(void * dst, const CUtensorMap * map,
         "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
             smem_u32(dst)),
         "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// 3D tiled TMA load (no multicast); x is always 0 here.
+__device__ __forceinline__ void tma_load_3d(void * dst, const CUtensorMap * map, int32_t x, int32_t y, int32_t z,
+                                            uint64_t * bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+        "[%5];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
         : "memory");
 }
 
@@ -384,8 +416,9 @@ __device__ __forceinline__ __half2 h2_int_const() {
 }
 
 // Tensor maps of one launch: weight boxes W0/W1 and the scale box (128 rows
-// each), the f16 codes (64 x BN, 128-byte swizzle), the f16 partial sums
-// (8 x BN) and the transposed activation scales (BN x 1).
+// each), the f16 codes (3D: 64 codes x BN rows x 2 chunks, 128-byte swizzle),
+// the f16 partial sums (3D: 8 x BN x 2 chunks) and the transposed activation
+// scales (BN x 1).
 struct TcMaps {
     CUtensorMap w0, w1, sc, qs, b2, dt;
 };
@@ -650,16 +683,16 @@ __global__ void __launch_bounds__(Roles<BN>::kThreads) __maxnreg__(Roles<BN>::kR
     extern __shared__ __align__(1024) uint8_t smem[];
     uint8_t * raw = smem;                                   // [NR][kRawBytes], 1024-byte aligned
     uint8_t * ops = raw + NR * L::kRawBytes;                // [NS][kOpBytes]
-    uint8_t * ering = ops + NS * L::kOpBytes;               // [kEpiRing][kEpiSlotBytes]
+    double * sums = reinterpret_cast<double *>(ops + NS * L::kOpBytes);  // [BN][kRows] (shared-memory sums)
+    uint8_t * ering = reinterpret_cast<uint8_t *>(sums) + L::kSumBytes;  // [kEpiRing][kEpiSlotBytes]
     uint8_t * tail = ering + kEpiRing * kEpiSlotBytes;
-    uint64_t * full = reinterpret_cast<uint64_t *>(tail);  // [NS] A stage written (converters)
+    uint64_t * full = reinterpret_cast<uint64_t *>(tail);  // [NS] A stage written (its converter group)
     uint64_t * empty = full + NS;                          // [NS] A stage consumed (MMA commit)
     uint64_t * raw_full = empty + NS;                      // [NR] TMA landed
-    uint64_t * raw_empty = raw_full + NR;                  // [NR] converters + MMA done with it
+    uint64_t * raw_empty = raw_full + NR;                  // [NR] converter group + MMA done with it
     uint64_t * acc_full = raw_empty + NR;                  // [2]
     uint64_t * acc_empty = acc_full + 2;                   // [2]
-    uint64_t * epi_full = acc_empty + 2;                   // [kEpiRing] weight scale words (converters)
-    uint64_t * epi_tx = epi_full + kEpiRing;               // [kEpiRing] activation d landed (TMA)
+    uint64_t * epi_tx = acc_empty + 2;                     // [kEpiRing] activation d landed (TMA)
     uint64_t * epi_empty = epi_tx + kEpiRing;              // [kEpiRing]
     uint64_t * drain = epi_empty + kEpiRing;               // [kMmaWarps]
     uint32_t * tmem_slot = reinterpret_cast<uint32_t *>(drain + R::kMmaWarps);
@@ -674,19 +707,18 @@ __global__ void __launch_bounds__(Roles<BN>::kThreads) __maxnreg__(Roles<BN>::kR
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < NS; ++s) {
-            mbar_init(&full[s], R::kConvWarps);
+            mbar_init(&full[s], R::kGroupWarps);
             mbar_init(&empty[s], 1);
         }
         for (int s = 0; s < NR; ++s) {
             mbar_init(&raw_full[s], 1);
-            mbar_init(&raw_empty[s], R::kConvWarps + 1);
+            mbar_init(&raw_empty[s], R::kGroupWarps + 1);
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(&acc_full[a], 1);
             mbar_init(&acc_empty[a], R::kEpiWarps);
         }
         for (int e = 0; e < kEpiRing; ++e) {
-            mbar_init(&epi_full[e], R::kScaleWriterWarps);
             mbar_init(&epi_tx[e], 1);
             mbar_init(&epi_empty[e], R::kEpiWarps);
         }
@@ -707,11 +739,15 @@ __global__ void __launch_bounds__(Roles<BN>::kThreads) __maxnreg__(Roles<BN>::kR
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp == R::kTmaWarp) {
-        // ---------------- TMA loads (one thread) ----------------
+    if (warp >= R::kTmaWarp) {
+        // ---------------- TMA loads (one thread per half-block) ----------------
+        // Thread t issues the loads of half-block t of every unit (raw stages
+        // rs with rs % 2 == t, NR is even); thread 0 also stages each unit's
+        // activation scales in the epilogue ring.
+        const int t = warp - R::kTmaWarp;
         if (lane == 0) {
-            uint32_t rs = 0, rph = 0, es = 0, eph = 0;
-            uint64_t issued = 0, e_issued = 0;
+            uint32_t es = 0, eph = 0;
+            uint64_t e_issued = 0;
             bool ok = true;
             auto issue_weights = [&](uint8_t * r, const Cursor & c, int h, uint64_t * bar) {
                 const int32_t y_w = int32_t(c.tm * kRows);
@@ -720,17 +756,13 @@ __global__ void __launch_bounds__(Roles<BN>::kThreads) __maxnreg__(Roles<BN>::kR
                 if constexpr (T::kW1 > 0) tma_load_2d(r + L::kW1Off, &maps.w1, x_blk + 128 + int32_t(T::kW1 * h), y_w, bar);
                 tma_load_2d(r + L::kScOff, &maps.sc, int32_t(c.b * 16), y_w, bar);
             };
-            // x coordinates: f16 elements (codes: multiples of 64; partial sums: of 8), bytes for the
-            // weight planes (multiples of 16): all 16-byte aligned
+            // one 3D box each: the two 64-code chunks of the half-block and
+            // (half 0, types with mins) the two 8-wide partial-sum chunks; the
+            // x coordinate is 0 and the chunk index is the third coordinate
             auto issue_activations = [&](uint8_t * r, const Cursor & c, int h, uint64_t * bar) {
                 const int32_t y_a = int32_t(c.tn * BN);
-                const int32_t x_codes = int32_t(c.b * kQK + 128 * h);
-                tma_load_2d(r + L::kBOff, &maps.qs, x_codes, y_a, bar);
-                tma_load_2d(r + L::kBOff + L::kBHalf, &maps.qs, x_codes + 64, y_a, bar);
-                if (T::kMins && h == 0) {
-                    tma_load_2d(r + L::kB2Off, &maps.b2, int32_t(c.b * 16), y_a, bar);
-                    tma_load_2d(r + L::kB2Off + uint32_t(BN) * 16, &maps.b2, int32_t(c.b * 16 + 8), y_a, bar);
-                }
+                tma_load_3d(r + L::kBOff, &maps.qs, 0, y_a, int32_t(4 * c.b + 2 * h), bar);
+                if (T::kMins && h == 0) tma_load_3d(r + L::kB2Off, &maps.b2, 0, y_a, int32_t(2 * c.b), bar);
             };
             // The weights of the first raw stages depend on no earlier kernel:
             // they are requested before waiting for the previous kernel, so
@@ -739,59 +771,51 @@ __global__ void __launch_bounds__(Roles<BN>::kThreads) __maxnreg__(Roles<BN>::kR
             {
                 Cursor c0;
                 c0.init(w_begin, nb, p.tiles_m);
-                for (uint64_t k = 0; k < pre; ++k) {
-                    const int h = int(k & 1);
-                    mbar_arrive_expect_tx(&raw_full[k], h == 0 ? L::kTx0 : L::kTx1);  // fresh stages: nothing to wait for
-                    issue_weights(raw + k * L::kRawBytes, c0, h, &raw_full[k]);
-                    if (h == 1) c0.next(nb, p.tiles_m);
+                for (uint64_t k = uint64_t(t); k < pre; k += 2) {
+                    mbar_arrive_expect_tx(&raw_full[k], t == 0 ? L::kTx0 : L::kTx1);  // fresh stages: nothing to wait for
+                    issue_weights(raw + k * L::kRawBytes, c0, t, &raw_full[k]);
+                    c0.next(nb, p.tiles_m);
                 }
             }
             pdl_wait();
             Cursor cur;
             cur.init(w_begin, nb, p.tiles_m);
-            for (uint64_t w = w_begin; w < w_end && ok && !*abort_flag; ++w, cur.next(nb, p.tiles_m)) {
-                const uint32_t b = cur.b;
-                const int32_t y_a = int32_t(cur.tn * BN);
-                // the unit's activation scales d[tokens][b] (one row of d_t)
-                if (!mbar_wait(&epi_empty[es], eph ^ 1u, abort_flag, p.error, kErrWaitEpiEmpty)) break;
-                mbar_arrive_expect_tx(&epi_tx[es], uint32_t(BN) * 4);
-                tma_load_2d(ering + es * kEpiSlotBytes + kEpiDaOff, &maps.dt, y_a, int32_t(b), &epi_tx[es]);
-                ++e_issued;
-                if (++es == kEpiRing) {
-                    es = 0;
-                    eph ^= 1u;
-                }
-                for (int h = 0; h < 2; ++h) {
-                    uint8_t * r = raw + rs * L::kRawBytes;
-                    if (issued >= pre) {
-                        if (!mbar_wait(&raw_empty[rs], rph ^ 1u, abort_flag, p.error, kErrWaitRawEmpty)) {
-                            ok = false;
-                            break;
-                        }
-                        mbar_arrive_expect_tx(&raw_full[rs], h == 0 ? L::kTx0 : L::kTx1);
-                        issue_weights(r, cur, h, &raw_full[rs]);
-                    }
-                    issue_activations(r, cur, h, &raw_full[rs]);
-                    ++issued;
-                    if (++rs == NR) {
-                        rs = 0;
-                        rph ^= 1u;
+            uint64_t hb = uint64_t(t);  // this thread's next half-block
+            for (uint64_t w = w_begin; w < w_end && ok && !*abort_flag; ++w, hb += 2, cur.next(nb, p.tiles_m)) {
+                if (t == 0) {
+                    // the unit's activation scales d[tokens][b] (one row of d_t)
+                    if (!mbar_wait(&epi_empty[es], eph ^ 1u, abort_flag, p.error, kErrWaitEpiEmpty)) break;
+                    mbar_arrive_expect_tx(&epi_tx[es], uint32_t(BN) * 4);
+                    tma_load_2d(ering + es * kEpiSlotBytes, &maps.dt, int32_t(cur.tn * BN), int32_t(cur.b), &epi_tx[es]);
+                    ++e_issued;
+                    if (++es == kEpiRing) {
+                        es = 0;
+                        eph ^= 1u;
                     }
                 }
+                const uint32_t rs = uint32_t(hb % NR), rph = uint32_t((hb / NR) & 1u);
+                uint8_t * r = raw + rs * L::kRawBytes;
+                if (hb >= pre) {
+                    if (!mbar_wait(&raw_empty[rs], rph ^ 1u, abort_flag, p.error, kErrWaitRawEmpty)) break;
+                    mbar_arrive_expect_tx(&raw_full[rs], t == 0 ? L::kTx0 : L::kTx1);
+                    issue_weights(r, cur, t, &raw_full[rs]);
+                }
+                issue_activations(r, cur, t, &raw_full[rs]);
             }
             // a stopped kernel must not exit with loads still landing in its
             // shared memory: wait (bounded) for the last issue of every slot
             if (*abort_flag) {
                 // pre-issued stages whose activation boxes were not requested yet
                 // get them now, so that every transaction completes
-                for (uint64_t j = issued; j < pre; ++j) {
+                for (uint64_t j = hb; j < pre; j += 2) {
                     Cursor cj;
                     cj.init(w_begin + j / 2, nb, p.tiles_m);
-                    issue_activations(raw + j * L::kRawBytes, cj, int(j & 1), &raw_full[j]);
+                    issue_activations(raw + j * L::kRawBytes, cj, t, &raw_full[j]);
                 }
                 volatile int no_abort = 0;
-                const uint64_t last = std::max(issued, pre);
-                for (uint64_t j = last > uint64_t(NR) ? last - NR : 0; j < last; ++j) {
+                uint64_t last = hb;  // every half-block of this thread below `last` was issued
+                while (last < pre) last += 2;
+                for (uint64_t j = last >= uint64_t(NR) ? last - NR : uint64_t(t); j < last; j += 2) {
                     (void) mbar_wait(&raw_full[j % NR], uint32_t((j / NR) & 1u), &no_abort, nullptr, 0);
                 }
                 for (uint64_t j = e_issued > uint64_t(kEpiRing) ? e_issued - kEpiRing : 0; j < e_issued; ++j) {
@@ -802,35 +826,27 @@ __global__ void __launch_bounds__(Roles<BN>::kThreads) __maxnreg__(Roles<BN>::kR
         __syncwarp();
     } else if (warp >= R::kEpiWarps && warp < R::kMmaWarp) {
         // ---------------- converters ----------------
+        // Group `grp` converts the half-blocks h with h % kGroups == grp (with
+        // two groups: half 0 and half 1 of every unit, concurrently). A group
+        // owns the A stages and raw stages of its halves (NS and NR are even
+        // when there are two groups), so each of its barriers completes its
+        // phases in the order the group waits for them.
         const int cw = warp - R::kEpiWarps;
-        const int quarter = warp & 3;                 // TMEM lane quarter of this warp
-        const int part = cw >> 2;                     // uniform per warp (always 0 with one thread per row)
+        const int grp = cw / R::kGroupWarps;
+        const int quarter = warp & 3;                                 // TMEM lane quarter of this warp
+        const int part = (cw % R::kGroupWarps) >> 2;                  // uniform per warp
         const int m = quarter * 32 + lane;
-        const bool scale_writer = part == 0;
         const uint32_t lane_base = uint32_t(quarter * 32) << 16;
-        const uint8_t * p2 = static_cast<const uint8_t *>(p.w.plane[2]);
-        uint32_t stage = 0, phase = 0, rs = 0, rph = 0, es = 0, eph = 0;
-        Cursor cur;
-        cur.init(w_begin, nb, p.tiles_m);
-        for (uint64_t w = w_begin; w < w_end; ++w, cur.next(nb, p.tiles_m)) {
+        uint64_t hb = uint64_t(grp);  // half-block index of the CTA's range
+        for (uint64_t w = w_begin; w < w_end; ++w) {
             if (__any_sync(0xffffffffu, *abort_flag != 0)) break;
-            // the epilogue's weight scale word of this row and block: Q4_K takes
-            // it from the header bytes of the raw stage; Q6_K and Q2_K read
-            // plane 2 here, early, so the load overlaps the conversion
-            uint32_t dword = 0;
-            if constexpr (TYPE != JF_TENSOR_Q4_K) {
-                const uint32_t row = cur.tm * kRows + uint32_t(m);
-                if (scale_writer && row < p.w.rows) {
-                    const uint64_t block = uint64_t(row) * nb + cur.b;
-                    dword = TYPE == JF_TENSOR_Q6_K ? uint32_t(__ldg(reinterpret_cast<const uint16_t *>(p2) + block))
-                                                   : __ldg(reinterpret_cast<const uint32_t *>(p2) + block);
-                }
-            }
             bool ok = true;
-            for (int h = 0; h < 2; ++h) {
+            for (int h = grp; h < 2; h += R::kGroups, hb += R::kGroups) {
+                const uint32_t stage = uint32_t(hb % NS), phase = uint32_t((hb / NS) & 1u);
+                const uint32_t rs = uint32_t(hb % NR), rph = uint32_t((hb / NR) & 1u);
                 // the whole warp proceeds or stops together (TMEM stores are warp-collective)
-                const bool ready = mbar_wait(&raw_full[rs], rph, abort_flag, p.error, kErrWaitRawFull) &&
-                                   mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.error, kErrWaitEmpty);
+                const bool ready = mbar_wait2(&raw_full[rs], rph, kErrWaitRawFull, &empty[stage], phase ^ 1u,
+                                              kErrWaitEmpty, abort_flag, p.error);
                 if (!__all_sync(0xffffffffu, ready)) {
                     ok = false;
                     break;
@@ -849,23 +865,6 @@ __global__ void __launch_bounds__(Roles<BN>::kThreads) __maxnreg__(Roles<BN>::kR
                         if (T::kMins && h == 0) convert_mins<TYPE, L>(r, pt, op, m);
                     }
                 }
-                if (h == 0) {
-                    if (scale_writer) {
-                        if constexpr (TYPE == JF_TENSOR_Q4_K) dword = *reinterpret_cast<const uint32_t *>(r + L::kScOff + m * 16);
-                        const bool free_slot = mbar_wait(&epi_empty[es], eph ^ 1u, abort_flag, p.error, kErrWaitEpiEmpty);
-                        if (!__all_sync(0xffffffffu, free_slot)) {
-                            ok = false;
-                            break;
-                        }
-                        reinterpret_cast<uint32_t *>(ering + es * kEpiSlotBytes)[m] = dword;
-                        __syncwarp();
-                        if (lane == 0) mbar_arrive(&epi_full[es]);
-                    }
-                    if (++es == kEpiRing) {
-                        es = 0;
-                        eph ^= 1u;
-                    }
-                }
                 tmem_wait_st();
                 tc_fence_before();
                 if (T::kMins && h == 0) fence_proxy_async();  // the mins tile is read by the tensor cores
@@ -873,14 +872,6 @@ __global__ void __launch_bounds__(Roles<BN>::kThreads) __maxnreg__(Roles<BN>::kR
                 if (lane == 0) {
                     mbar_arrive(&full[stage]);
                     mbar_arrive(&raw_empty[rs]);
-                }
-                if (++stage == NS) {
-                    stage = 0;
-                    phase ^= 1u;
-                }
-                if (++rs == NR) {
-                    rs = 0;
-                    rph ^= 1u;
                 }
             }
             if (!ok) break;
@@ -915,8 +906,10 @@ __global__ void __launch_bounds__(Roles<BN>::kThreads) __maxnreg__(Roles<BN>::kR
                     const uint32_t rs = uint32_t(hb % NR), rph = uint32_t((hb / NR) & 1u);
                     // (the converters waited for the raw stage before completing full[stage];
                     // with two issuers the raw barriers are shared, so only one waits on them)
-                    const bool ready = mbar_wait(&full[stage], phase, abort_flag, p.error, kErrWaitFull) &&
-                                       (kIssuers == 2 || mbar_wait(&raw_full[rs], rph, abort_flag, p.error, kErrWaitRawFull));
+                    const bool ready = kIssuers == 2
+                                           ? mbar_wait(&full[stage], phase, abort_flag, p.error, kErrWaitFull)
+                                           : mbar_wait2(&full[stage], phase, kErrWaitFull, &raw_full[rs], rph,
+                                                        kErrWaitRawFull, abort_flag, p.error);
                     if (!__all_sync(0xffffffffu, ready)) {
                         ok = false;
                         break;
@@ -957,18 +950,46 @@ __global__ void __launch_bounds__(Roles<BN>::kThreads) __maxnreg__(Roles<BN>::kR
         __syncwarp();
     } else {
         // ---------------- epilogue ----------------
+        // Each thread owns weight row m of the tile (its warp's TMEM lane
+        // quarter) and kCols token columns. It reads its row's scale word of
+        // each block from the weight planes itself, one unit ahead; the TMA
+        // thread stages each unit's activation scales in the epilogue ring.
+        // The per-(row, token) double sums live in shared memory for 32-token
+        // tiles and in registers for 64-token tiles.
         constexpr int kCols = R::kCols;  // token columns of this thread
         const int quarter = warp & 3;
         const int m = quarter * 32 + lane;  // the warp's TMEM lane quarter = its 32 weight rows
         const int col0 = (warp >> 2) * kCols;
         const uint32_t lane_base = uint32_t(quarter * 32) << 16;
         const uint32_t first_tile = uint32_t(w_begin / nb);
-        double sum[kCols];
+        double rsum[R::kSmemSums ? 1 : kCols];
+        double * ssum = sums + uint32_t(col0) * kRows + uint32_t(m);  // element t at ssum[t * kRows]
+        auto sum_get = [&](int t) -> double {
+            if constexpr (R::kSmemSums) return ssum[t * kRows];
+            else return rsum[t];
+        };
+        auto sum_set = [&](int t, double v) {
+            if constexpr (R::kSmemSums) ssum[t * kRows] = v;
+            else rsum[t] = v;
+        };
+        const uint8_t * p1 = static_cast<const uint8_t *>(p.w.plane[1]);
+        const uint8_t * p2 = static_cast<const uint8_t *>(p.w.plane[2]);
+        // this row's scale word of the unit's block: Q4_K (d | dmin << 16) from
+        // the 16-byte header, Q6_K d, Q2_K (d | dmin << 16); 0 past the last row
+        auto load_word = [&](const Cursor & c) -> uint32_t {
+            const uint32_t row = c.tm * kRows + uint32_t(m);
+            if (row >= p.w.rows) return 0u;
+            const uint64_t block = uint64_t(row) * nb + c.b;
+            if constexpr (TYPE == JF_TENSOR_Q4_K) return __ldg(reinterpret_cast<const uint32_t *>(p1 + block * 16));
+            else if constexpr (TYPE == JF_TENSOR_Q6_K) return uint32_t(__ldg(reinterpret_cast<const uint16_t *>(p2) + block));
+            else return __ldg(reinterpret_cast<const uint32_t *>(p2) + block);
+        };
         uint64_t seg_begin = w_begin;
         uint32_t i = 0, es = 0, eph = 0;
-        pdl_wait();  // outputs, residuals and the stream-K workspace are shared with earlier kernels
         Cursor cur;
         cur.init(w_begin, nb, p.tiles_m);
+        uint32_t word_next = w_begin < w_end ? load_word(cur) : 0u;  // weights: written by no earlier kernel
+        pdl_wait();  // outputs, residuals and the stream-K workspace are shared with earlier kernels
         for (uint64_t w = w_begin; w < w_end; ++w, ++i, cur.next(nb, p.tiles_m)) {
             // warp-uniform stop: the warp collectives below need every lane
             if (__any_sync(0xffffffffu, *abort_flag != 0)) break;
@@ -976,21 +997,24 @@ __global__ void __launch_bounds__(Roles<BN>::kThreads) __maxnreg__(Roles<BN>::kR
             const uint32_t row = cur.tm * kRows + uint32_t(m), tok0 = cur.tn * BN;
             if (w == seg_begin) {
 #pragma unroll
-                for (int t = 0; t < kCols; ++t) sum[t] = 0.0;
+                for (int t = 0; t < kCols; ++t) sum_set(t, 0.0);
+            }
+            const uint32_t word = word_next;
+            if (w + 1 < w_end) {
+                Cursor nx = cur;
+                nx.next(nb, p.tiles_m);
+                word_next = load_word(nx);
             }
             const uint32_t acc = i & 1u, use = i >> 1;
             // the whole warp proceeds or stops together
-            const bool ready = mbar_wait(&epi_full[es], eph, abort_flag, p.error, kErrWaitEpiFull) &&
-                               mbar_wait(&epi_tx[es], eph, abort_flag, p.error, kErrWaitEpiFull) &&
-                               mbar_wait(&acc_full[acc], use & 1u, abort_flag, p.error, kErrWaitAccFull);
+            const bool ready = mbar_wait2(&epi_tx[es], eph, kErrWaitEpiFull, &acc_full[acc], use & 1u, kErrWaitAccFull,
+                                          abort_flag, p.error);
             if (!__all_sync(0xffffffffu, ready)) break;
             tc_fence_after();
-            const uint8_t * slot = ering + es * kEpiSlotBytes;
-            const uint32_t word = reinterpret_cast<const uint32_t *>(slot)[m];
+            const float * da_s = reinterpret_cast<const float *>(ering + es * kEpiSlotBytes) + col0;
             const float dw = half_bits_to_float(uint16_t(word & 0xffffu));
             const float dmin = half_bits_to_float(uint16_t(word >> 16));  // unused for Q6_K
             const float2 dw2 = f2(dw, dw), dmin2 = f2(dmin, dmin);
-            const float * da_s = reinterpret_cast<const float *>(slot + kEpiDaOff) + col0;
             const uint32_t base = tmem + lane_base + acc * (T::kAcc * BN) + col0;
 #pragma unroll
             for (int ch = 0; ch < kCols / 8; ++ch) {
@@ -1013,7 +1037,7 @@ __global__ void __launch_bounds__(Roles<BN>::kThreads) __maxnreg__(Roles<BN>::kR
                 const float2 das[4] = {f2(da0.x, da0.y), f2(da0.z, da0.w), f2(da1.x, da1.y), f2(da1.z, da1.w)};
 #pragma unroll
                 for (int k = 0; k < 4; ++k) {
-                    const float2 da = das[k];
+                    const float2 da2 = das[k];
                     const float2 a0 = f2(__uint_as_float(r0[2 * k]), __uint_as_float(r0[2 * k + 1]));
                     const float2 a1 = f2(__uint_as_float(r1[2 * k]), __uint_as_float(r1[2 * k + 1]));
                     float2 c;
@@ -1021,22 +1045,24 @@ __global__ void __launch_bounds__(Roles<BN>::kThreads) __maxnreg__(Roles<BN>::kR
                         // c = (dw*da)*RN(D0 + D1) - (dmin*da)*msum
                         const float2 a2 = f2(__uint_as_float(r2[2 * k]), __uint_as_float(r2[2 * k + 1]));
                         const float2 isum = f2(__fadd_rn(a0.x, a1.x), __fadd_rn(a0.y, a1.y));
-                        const float2 t1 = mul2_rn(mul2_rn(dw2, da), isum);
-                        const float2 t2 = mul2_rn(mul2_rn(dmin2, da), a2);
+                        const float2 t1 = mul2_rn(mul2_rn(dw2, da2), isum);
+                        const float2 t2 = mul2_rn(mul2_rn(dmin2, da2), a2);
                         c = f2(__fsub_rn(t1.x, t2.x), __fsub_rn(t1.y, t2.y));
                     } else if constexpr (TYPE == JF_TENSOR_Q6_K) {
                         // 16*Dhi is exact, so the fused form rounds once, like RN(isum)
                         const float2 isum = fma2_rn(f2(16.0f, 16.0f), a0, a1);
-                        c = mul2_rn(mul2_rn(dw2, da), isum);
+                        c = mul2_rn(mul2_rn(dw2, da2), isum);
                     } else {
-                        const float2 t1 = mul2_rn(mul2_rn(dw2, da), a0);
-                        const float2 t2 = mul2_rn(mul2_rn(dmin2, da), a1);
+                        const float2 t1 = mul2_rn(mul2_rn(dw2, da2), a0);
+                        const float2 t2 = mul2_rn(mul2_rn(dmin2, da2), a1);
                         c = f2(__fsub_rn(t1.x, t2.x), __fsub_rn(t1.y, t2.y));
                     }
-                    sum[8 * ch + 2 * k] += double(c.x);
-                    sum[8 * ch + 2 * k + 1] += double(c.y);
+                    const int t = 8 * ch + 2 * k;
+                    sum_set(t, sum_get(t) + double(c.x));
+                    sum_set(t + 1, sum_get(t + 1) + double(c.y));
                 }
             }
+
             if (++es == kEpiRing) {
                 es = 0;
                 eph ^= 1u;
@@ -1050,7 +1076,7 @@ __global__ void __launch_bounds__(Roles<BN>::kThreads) __maxnreg__(Roles<BN>::kR
                 const uint32_t slot_p = 2 * blockIdx.x + (tile == first_tile ? 0 : 1);
                 double * part = p.partial + uint64_t(slot_p) * R::kSlotDoubles;
 #pragma unroll
-                for (int t = 0; t < kCols; ++t) part[(col0 + t) * kRows + m] = sum[t];
+                for (int t = 0; t < kCols; ++t) part[(col0 + t) * kRows + m] = sum_get(t);
                 __threadfence();
                 __syncwarp();
                 const uint32_t lo = cta_of(uint64_t(tile) * nb, p.work, g);
@@ -1087,7 +1113,7 @@ __global__ void __launch_bounds__(Roles<BN>::kThreads) __maxnreg__(Roles<BN>::kR
                         for (int k = 0; k < 8; ++k) acc8[k] += v[k];
                     }
 #pragma unroll
-                    for (int k = 0; k < 8; ++k) sum[t0 + k] = acc8[k];
+                    for (int k = 0; k < 8; ++k) sum_set(t0 + k, acc8[k]);
                 }
             }
             if (row < p.w.rows) {
@@ -1106,7 +1132,7 @@ __global__ void __launch_bounds__(Roles<BN>::kThreads) __maxnreg__(Roles<BN>::kR
                     const uint32_t tok = tok0 + col0 + t;
                     if (tok >= p.n) break;
                     const uint64_t at = uint64_t(tok) * ld + r;
-                    float v = __double2float_rn(sum[t]);
+                    float v = __double2float_rn(sum_get(t));
                     if (ep == JFB_EPILOGUE_BIAS) v = __fadd_rn(v, bias[r]);
                     else if (ep == JFB_EPILOGUE_RESIDUAL) v = __fadd_rn(v, residual[at]);
                     out[at] = v;
@@ -1217,6 +1243,42 @@ bool tensor_map_2d(CUtensorMap & out, const void * base, uint32_t elem_bytes, ui
     return true;
 }
 
+// 3D tensor map over f16 rows [rows][width] that views each row as chunks of
+// `chunk` elements: dims (chunk, rows, width / chunk), strides (row pitch,
+// chunk bytes). A box (chunk, box_rows, 2) lands in shared memory as two
+// consecutive [box_rows][chunk] tiles, exactly as two 2D boxes would. Cached
+// like tensor_map_2d.
+bool tensor_map_chunks(CUtensorMap & out, const void * base, uint32_t chunk, uint64_t width, uint64_t rows,
+                       uint32_t box_rows, bool swizzle128) {
+    using Key = std::tuple<uintptr_t, uint32_t, uint64_t, uint64_t, uint32_t, bool>;
+    static std::mutex mu;
+    static std::map<Key, CUtensorMap> cache;
+    const Key key{reinterpret_cast<uintptr_t>(base), chunk, width, rows, box_rows, swizzle128};
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) {
+        out = it->second;
+        return true;
+    }
+    PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
+    if (encode == nullptr || width % chunk != 0) return false;
+    const cuuint64_t dims[3] = {chunk, rows, width / chunk};
+    const cuuint64_t strides[2] = {width * 2, uint64_t(chunk) * 2};
+    const cuuint32_t box[3] = {chunk, box_rows, 2};
+    const cuuint32_t elem[3] = {1, 1, 1};
+    CUtensorMap map;
+    std::memset(&map, 0, sizeof(map));
+    if (encode(&map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, const_cast<void *>(base), dims, strides, box, elem,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS) {
+        return false;
+    }
+    if (cache.size() >= 4096) cache.clear();
+    cache.emplace(key, map);
+    out = map;
+    return true;
+}
+
 template <uint32_t TYPE, int BN>
 jfb_status build_maps(TcMaps & maps, const TcParams & p, const jfb_q8k & x, uint32_t cols) {
     using T = TypeTraits<TYPE>;
@@ -1224,8 +1286,8 @@ jfb_status build_maps(TcMaps & maps, const TcParams & p, const jfb_q8k & x, uint
     const bool ok = tensor_map_2d(maps.w0, p.w.plane[0], 1, wb, wb, p.w.rows, T::kW0, kRows) &&
                     tensor_map_2d(maps.w1, p.w.plane[0], 1, wb, wb, p.w.rows, T::kW1 > 0 ? T::kW1 : 16, kRows) &&
                     tensor_map_2d(maps.sc, p.w.plane[1], 1, nb * 16, nb * 16, p.w.rows, 16, kRows) &&
-                    tensor_map_2d(maps.qs, x.qs_f16, 2, cols, cols, p.n, 64, BN, true) &&
-                    tensor_map_2d(maps.b2, x.bsums_f16, 2, cols / 16, cols / 16, p.n, 8, BN) &&
+                    tensor_map_chunks(maps.qs, x.qs_f16, 64, cols, p.n, BN, true) &&
+                    tensor_map_chunks(maps.b2, x.bsums_f16, 8, cols / 16, p.n, BN, false) &&
                     tensor_map_2d(maps.dt, x.d_t, 4, p.n, x.d_stride, nb, BN, 1);
     if (!ok) return status_error(JFB_STATUS_CUDA_ERROR, "jfb_matmul_tc: could not encode a TMA tensor map");
     return status_ok();
@@ -1241,9 +1303,12 @@ jfb_status launch(TcParams & p, const jfb_q8k & x, uint32_t cols, uint32_t grid,
     static_assert(L::NS >= 2, "operand pipeline depth");
     static_assert(L::kAccCols + L::NS * L::kACols <= kTmemCols, "TMEM budget");
     static_assert(L::kRawBytes % 1024 == 0 && L::kBHalf % 1024 == 0, "swizzled boxes stay 1024-byte aligned");
-    static_assert(L::kOpBytes % 1024 == 0 && kEpiSlotBytes % 128 == 0, "TMA destinations stay 128-byte aligned");
-    static_assert(kEpiDaOff >= kRows * 4 && kEpiDaOff + BN * 4 <= kEpiSlotBytes, "epilogue slot layout");
-    static_assert(R::kConvWarps % 4 == 0 && R::kParts * kRows == R::kConvThreads, "converter lanes cover the rows");
+    static_assert(L::kOpBytes % 1024 == 0 && kEpiSlotBytes % 128 == 0 && L::kSumBytes % 1024 == 0,
+                  "TMA destinations stay 128-byte aligned");
+    static_assert(BN * 4 <= kEpiSlotBytes, "epilogue slot layout");
+    static_assert(R::kGroupWarps % 4 == 0 && R::kParts * kRows == R::kGroupWarps * 32 && R::kParts <= 2,
+                  "converter lanes cover the rows");
+    static_assert(L::NS % R::kGroups == 0 && L::NR % R::kGroups == 0, "each converter group owns its stages");
     static_assert(R::kEpiWarps * 32 * R::kCols == kRows * BN && R::kCols % 8 == 0, "epilogue threads cover the tile");
     static_assert(BN <= kMaxBN, "partial slots are sized for kMaxBN");
     static_assert(R::kEpiWarps == Roles<32>::kEpiWarps, "one counter layout for every tile width");
