@@ -91,7 +91,6 @@ constexpr uint32_t kSuspendNs = 1000000;              // longest single suspensi
 constexpr uint32_t kTmemCols = 512;                   // one CTA per SM owns all of TMEM
 constexpr int kEpiRing = 8;                           // units of activation scales staged ahead
 constexpr uint32_t kEpiSlotBytes = 256;               // [BN] activation d
-constexpr int kMaxBN = 64;
 
 enum : int {
     kErrWaitEmpty = 1,
@@ -103,6 +102,7 @@ enum : int {
     kErrWaitEpiEmpty = 7,
     kErrWaitEpiFull = 8,
     kErrSmemAlign = 9,
+    kErrWaitReduce = 10,
 };
 
 // Per type: A planes (Q6_K: hi and lo), accumulators per unit, raw weight
@@ -146,6 +146,11 @@ struct Roles {
     // tiles (which frees the registers for the second converter group),
     // registers for 64-token tiles
     static constexpr bool kSmemSums = BN == 32;
+    // two alternating shared-memory sum buffers when the sums live there
+    static constexpr uint32_t kSumBufs = kSmemSums ? 2 : 0;
+    // cluster schedules (K slices of a tile added over distributed shared
+    // memory) for 32-token tiles; 64-token launches always run stream-K
+    static constexpr bool kClusters = kSmemSums;
     // two MMA warps issue alternate units: a memory read by an issuing
     // thread (its barrier waits) stalls its issue for hundreds of cycles, and
     // the other thread's MMAs keep the tensor pipe busy meanwhile
@@ -159,7 +164,6 @@ struct Roles {
     // registers for the warps w with w % 4 == its index, allocated in
     // multiples of 8 per thread
     static constexpr int kRegs = (16384 / (((kWarps + 3) / 4) * 32)) / 8 * 8;
-    static constexpr uint32_t kSlotDoubles = uint32_t(kRows) * BN;  // one partial tile
 };
 
 // Shared and tensor memory of one (type, BN):
@@ -168,7 +172,7 @@ struct Roles {
 //   rows, the scale/header box [128][16 B] and, for types with mins in half 0,
 //   the f16 partial sums as two boxes [BN][16 B];
 //   operand stage: the K = 16 mins tile of A (types with mins);
-//   epilogue sums: [BN][128] doubles when the epilogue keeps them in shared memory;
+//   epilogue sums (32-token tiles): two [BN][128] double buffers of running sums;
 //   epilogue ring: per unit the activation scales d of the tile's tokens.
 template <uint32_t TYPE, int BN>
 struct Layout {
@@ -191,7 +195,7 @@ struct Layout {
     static constexpr int kNsFit = int((kTmemCols - kAccCols) / kACols);
     static constexpr int NS = (kNsFit < 4 ? kNsFit : 4) / kStep * kStep;
     static constexpr uint32_t kOpBytes = T::kMins ? kA2Bytes : 0;
-    static constexpr uint32_t kSumBytes = Roles<BN>::kSmemSums ? uint32_t(kRows) * BN * 8 : 0;
+    static constexpr uint32_t kSumBytes = Roles<BN>::kSumBufs * uint32_t(kRows) * BN * 8;
     static constexpr uint32_t kFixed = uint32_t(NS) * kOpBytes + kSumBytes + kEpiRing * kEpiSlotBytes + kTailBytes;
     static constexpr int kNrFit = int((kMaxSmem - kFixed) / kRawBytes);
     static constexpr int NR = (kNrFit < 12 ? kNrFit : 12) / kStep * kStep;
@@ -274,6 +278,60 @@ __device__ __forceinline__ bool mbar_wait2(uint64_t * bar_a, uint32_t parity_a, 
     if (a && b) return true;
     return (a || mbar_wait_slow(bar_a, parity_a, abort_flag, error, code_a)) &&
            (b || mbar_wait_slow(bar_b, parity_b, abort_flag, error, code_b));
+}
+
+// ---- clusters: the K slices of a tile are added over distributed shared memory
+
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Shared-memory address of `p` in the CTA of cluster rank `rank`.
+__device__ __forceinline__ uint32_t dsmem_addr(const void * p, uint32_t rank) {
+    uint32_t out;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(smem_u32(p)), "r"(rank));
+    return out;
+}
+
+__device__ __forceinline__ double dsmem_f64(uint32_t addr) {
+    double v;
+    asm volatile("ld.shared::cluster.f64 %0, [%1];" : "=d"(v) : "r"(addr) : "memory");
+    return v;
+}
+
+// Arrival on the barrier at the same offset in the CTA of rank `rank`,
+// releasing (at cluster scope) this thread's earlier shared-memory accesses
+// and, through the fence and the warp barrier before it, its warp's.
+__device__ __forceinline__ void mbar_arrive_remote(uint64_t * bar, uint32_t rank) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(dsmem_addr(bar, rank)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t * bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.b32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait with cluster-scope acquire (the arrivals come from the CTAs of
+// the cluster); same limit and error reporting as mbar_wait.
+__device__ __noinline__ bool mbar_wait_cluster(uint64_t * bar, uint32_t parity, volatile int * abort_flag, int * error,
+                                               int code) {
+    const uint64_t t0 = global_ns();
+    for (;;) {
+        if (mbar_try_wait_cluster(bar, parity)) return true;
+        if (*abort_flag) return false;
+        if (global_ns() - t0 > kWaitNs) break;
+        __nanosleep(64);
+    }
+    *abort_flag = 1;
+    if (error != nullptr) *reinterpret_cast<volatile int *>(error) = code;
+    return false;
 }
 
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t * bar, uint32_t bytes) {
@@ -430,6 +488,7 @@ struct TcParams {
     uint32_t tiles_m;
     uint32_t tiles;
     uint64_t work;          // tiles * blocks
+    uint32_t csize;         // 1: stream-K over the grid; > 1: CTAs per cluster, the K slices of one tile
     // output segments: rows [seg_end[k-1], seg_end[k]) -> seg_out[k] [n][rows of k]
     uint32_t nseg;
     uint32_t seg_end[JFB_MATMUL_MAX_SEGMENTS];
@@ -437,32 +496,71 @@ struct TcParams {
     const float * seg_bias[JFB_MATMUL_MAX_SEGMENTS];
     const float * seg_residual[JFB_MATMUL_MAX_SEGMENTS];
     float * seg_out[JFB_MATMUL_MAX_SEGMENTS];
-    double * partial;       // [2 * gridDim.x][BN][kRows]
-    uint32_t * counters;    // [tiles][epilogue warps]
+    double * partial;       // stream-K: [2 * gridDim.x][BN][kRows]
+    uint32_t * counters;    // stream-K: [tiles][epilogue warps]
     int * error;
 };
 
 __host__ __device__ __forceinline__ uint64_t range_start(uint64_t c, uint64_t work, uint64_t g) {
     return c * work / g;
 }
-// The CTA whose range holds `unit`.
+// The CTA whose stream-K range holds `unit`.
 __device__ __forceinline__ uint32_t cta_of(uint64_t unit, uint64_t work, uint64_t g) {
     return uint32_t(((unit + 1) * g - 1) / work);
+}
+
+// This CTA's work: U units, one (tile, K block) pair each, starting at
+// (tile0, bstart); within a tile the blocks run from b0 to b1 - 1.
+//   Stream-K (csize == 1): CTA c of G takes the contiguous unit range
+//   [c*W/G, (c+1)*W/G) of the W = tiles * nb units (b0 = 0, b1 = nb); a tile
+//   split between CTAs is finished by the last one to arrive, from partial
+//   sums in global memory.
+//   Clusters (csize > 1): cluster k of G takes the tiles [k*T/G, (k+1)*T/G)
+//   and its CTA of rank r the blocks [r*nb/csize, (r+1)*nb/csize) of each;
+//   the K slices of a tile are added over distributed shared memory.
+struct Work {
+    uint32_t tile0, bstart, b0, b1, units, rank;
+};
+
+__device__ __forceinline__ Work cta_work(const TcParams & p) {
+    Work w;
+    const uint32_t nb = p.blocks;
+    if (p.csize == 1) {
+        const uint64_t wb = range_start(blockIdx.x, p.work, gridDim.x);
+        const uint64_t we = range_start(blockIdx.x + 1, p.work, gridDim.x);
+        w.tile0 = uint32_t(wb / nb);
+        w.bstart = uint32_t(wb - uint64_t(w.tile0) * nb);
+        w.b0 = 0;
+        w.b1 = nb;
+        w.units = uint32_t(we - wb);
+        w.rank = 0;
+    } else {
+        const uint32_t clusters = gridDim.x / p.csize, c = blockIdx.x / p.csize;
+        w.rank = blockIdx.x - c * p.csize;
+        const uint32_t t0 = uint32_t(uint64_t(c) * p.tiles / clusters);
+        const uint32_t t1 = uint32_t(uint64_t(c + 1) * p.tiles / clusters);
+        w.tile0 = t0;
+        w.b0 = w.rank * nb / p.csize;
+        w.b1 = (w.rank + 1) * nb / p.csize;
+        w.bstart = w.b0;
+        w.units = (t1 - t0) * (w.b1 - w.b0);
+    }
+    return w;
 }
 
 // Position of a work unit: tile = tn * tiles_m + tm, K block b. Advanced one
 // unit at a time so that no role divides per unit.
 struct Cursor {
     uint32_t tile, b, tm, tn;
-    __device__ __forceinline__ void init(uint64_t w, uint32_t nb, uint32_t tiles_m) {
-        tile = uint32_t(w / nb);
-        b = uint32_t(w - uint64_t(tile) * nb);
+    __device__ __forceinline__ void init(const Work & w, uint32_t tiles_m) {
+        tile = w.tile0;
+        b = w.bstart;
         tn = tile / tiles_m;
         tm = tile - tn * tiles_m;
     }
-    __device__ __forceinline__ void next(uint32_t nb, uint32_t tiles_m) {
-        if (++b == nb) {
-            b = 0;
+    __device__ __forceinline__ void next(const Work & w, uint32_t tiles_m) {
+        if (++b == w.b1) {
+            b = w.b0;
             ++tile;
             if (++tm == tiles_m) {
                 tm = 0;
@@ -694,16 +792,18 @@ __global__ void __launch_bounds__(Roles<BN>::kThreads) __maxnreg__(Roles<BN>::kR
     uint64_t * acc_empty = acc_full + 2;                   // [2]
     uint64_t * epi_tx = acc_empty + 2;                     // [kEpiRing] activation d landed (TMA)
     uint64_t * epi_empty = epi_tx + kEpiRing;              // [kEpiRing]
-    uint64_t * drain = epi_empty + kEpiRing;               // [kMmaWarps]
+    uint64_t * red_full = epi_empty + kEpiRing;            // [2] every CTA of the cluster wrote its tile sums
+    uint64_t * red_empty = red_full + 2;                   // [2] every CTA of the cluster read them
+    uint64_t * drain = red_empty + 2;                      // [kMmaWarps]
     uint32_t * tmem_slot = reinterpret_cast<uint32_t *>(drain + R::kMmaWarps);
     volatile int * abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     pdl_trigger();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint64_t g = gridDim.x;
-    const uint64_t w_begin = range_start(blockIdx.x, p.work, g);
-    const uint64_t w_end = range_start(blockIdx.x + 1, p.work, g);
     const uint32_t nb = p.blocks;
+    const uint32_t csize = p.csize;
+    const Work wk = cta_work(p);
+    const uint32_t U = wk.units;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < NS; ++s) {
@@ -722,6 +822,10 @@ __global__ void __launch_bounds__(Roles<BN>::kThreads) __maxnreg__(Roles<BN>::kR
             mbar_init(&epi_tx[e], 1);
             mbar_init(&epi_empty[e], R::kEpiWarps);
         }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&red_full[b], csize * R::kEpiWarps);
+            mbar_init(&red_empty[b], csize * R::kEpiWarps);
+        }
         for (int d = 0; d < R::kMmaWarps; ++d) mbar_init(&drain[d], 1);
         // the swizzled boxes need a 1024-byte aligned ring; stop before any load otherwise
         const bool aligned = (smem_u32(smem) & 1023u) == 0;
@@ -735,7 +839,9 @@ __global__ void __launch_bounds__(Roles<BN>::kThreads) __maxnreg__(Roles<BN>::kR
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
     tc_fence_before();
-    __syncthreads();
+    // with clusters, every CTA's barriers are initialised before any remote arrival
+    if (csize > 1) cluster_sync_all();
+    else __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
@@ -767,21 +873,21 @@ __global__ void __launch_bounds__(Roles<BN>::kThreads) __maxnreg__(Roles<BN>::kR
             // The weights of the first raw stages depend on no earlier kernel:
             // they are requested before waiting for the previous kernel, so
             // their latency overlaps its tail (programmatic dependent launch).
-            const uint64_t pre = std::min<uint64_t>(uint64_t(NR), 2 * (w_end - w_begin));
+            const uint32_t pre = std::min<uint32_t>(uint32_t(NR), 2 * U);
             {
                 Cursor c0;
-                c0.init(w_begin, nb, p.tiles_m);
-                for (uint64_t k = uint64_t(t); k < pre; k += 2) {
+                c0.init(wk, p.tiles_m);
+                for (uint32_t k = uint32_t(t); k < pre; k += 2) {
                     mbar_arrive_expect_tx(&raw_full[k], t == 0 ? L::kTx0 : L::kTx1);  // fresh stages: nothing to wait for
                     issue_weights(raw + k * L::kRawBytes, c0, t, &raw_full[k]);
-                    c0.next(nb, p.tiles_m);
+                    c0.next(wk, p.tiles_m);
                 }
             }
             pdl_wait();
             Cursor cur;
-            cur.init(w_begin, nb, p.tiles_m);
-            uint64_t hb = uint64_t(t);  // this thread's next half-block
-            for (uint64_t w = w_begin; w < w_end && ok && !*abort_flag; ++w, hb += 2, cur.next(nb, p.tiles_m)) {
+            cur.init(wk, p.tiles_m);
+            uint32_t hb = uint32_t(t);  // this thread's next half-block
+            for (uint32_t u = 0; u < U && ok && !*abort_flag; ++u, hb += 2, cur.next(wk, p.tiles_m)) {
                 if (t == 0) {
                     // the unit's activation scales d[tokens][b] (one row of d_t)
                     if (!mbar_wait(&epi_empty[es], eph ^ 1u, abort_flag, p.error, kErrWaitEpiEmpty)) break;
@@ -807,15 +913,16 @@ __global__ void __launch_bounds__(Roles<BN>::kThreads) __maxnreg__(Roles<BN>::kR
             if (*abort_flag) {
                 // pre-issued stages whose activation boxes were not requested yet
                 // get them now, so that every transaction completes
-                for (uint64_t j = hb; j < pre; j += 2) {
+                for (uint32_t j = hb; j < pre; j += 2) {
                     Cursor cj;
-                    cj.init(w_begin + j / 2, nb, p.tiles_m);
+                    cj.init(wk, p.tiles_m);
+                    for (uint32_t k = 0; k < j / 2; ++k) cj.next(wk, p.tiles_m);
                     issue_activations(raw + j * L::kRawBytes, cj, t, &raw_full[j]);
                 }
                 volatile int no_abort = 0;
-                uint64_t last = hb;  // every half-block of this thread below `last` was issued
+                uint32_t last = hb;  // every half-block of this thread below `last` was issued
                 while (last < pre) last += 2;
-                for (uint64_t j = last >= uint64_t(NR) ? last - NR : uint64_t(t); j < last; j += 2) {
+                for (uint32_t j = last >= uint32_t(NR) ? last - NR : uint32_t(t); j < last; j += 2) {
                     (void) mbar_wait(&raw_full[j % NR], uint32_t((j / NR) & 1u), &no_abort, nullptr, 0);
                 }
                 for (uint64_t j = e_issued > uint64_t(kEpiRing) ? e_issued - kEpiRing : 0; j < e_issued; ++j) {
@@ -837,8 +944,8 @@ __global__ void __launch_bounds__(Roles<BN>::kThreads) __maxnreg__(Roles<BN>::kR
         const int part = (cw % R::kGroupWarps) >> 2;                  // uniform per warp
         const int m = quarter * 32 + lane;
         const uint32_t lane_base = uint32_t(quarter * 32) << 16;
-        uint64_t hb = uint64_t(grp);  // half-block index of the CTA's range
-        for (uint64_t w = w_begin; w < w_end; ++w) {
+        uint32_t hb = uint32_t(grp);  // half-block index of the CTA's range
+        for (uint32_t u = 0; u < U; ++u) {
             if (__any_sync(0xffffffffu, *abort_flag != 0)) break;
             bool ok = true;
             for (int h = grp; h < 2; h += R::kGroups, hb += R::kGroups) {
@@ -891,7 +998,7 @@ __global__ void __launch_bounds__(Roles<BN>::kThreads) __maxnreg__(Roles<BN>::kR
             constexpr uint32_t idesc = instr_desc(kRows, BN);
             bool ok = true;
             uint32_t i = mid;
-            for (uint64_t w = w_begin + mid; w < w_end && ok; w += kIssuers, i += kIssuers) {
+            for (; i < U && ok; i += kIssuers) {
                 if (__any_sync(0xffffffffu, *abort_flag != 0)) break;
                 const uint32_t acc = i & 1u, use = i >> 1;
                 if (!__all_sync(0xffffffffu, mbar_wait(&acc_empty[acc], (use & 1u) ^ 1u, abort_flag, p.error,
@@ -901,7 +1008,7 @@ __global__ void __launch_bounds__(Roles<BN>::kThreads) __maxnreg__(Roles<BN>::kR
                 tc_fence_after();
                 const uint32_t d = tmem + acc * (T::kAcc * BN);
                 for (int h = 0; h < 2; ++h) {
-                    const uint64_t hb = 2 * uint64_t(i) + uint64_t(h);  // half-block index of the CTA's range
+                    const uint32_t hb = 2 * i + uint32_t(h);  // half-block index of the CTA's range
                     const uint32_t stage = uint32_t(hb % NS), phase = uint32_t((hb / NS) & 1u);
                     const uint32_t rs = uint32_t(hb % NR), rph = uint32_t((hb / NR) & 1u);
                     // (the converters waited for the raw stage before completing full[stage];
@@ -954,22 +1061,31 @@ __global__ void __launch_bounds__(Roles<BN>::kThreads) __maxnreg__(Roles<BN>::kR
         // quarter) and kCols token columns. It reads its row's scale word of
         // each block from the weight planes itself, one unit ahead; the TMA
         // thread stages each unit's activation scales in the epilogue ring.
-        // The per-(row, token) double sums live in shared memory for 32-token
-        // tiles and in registers for 64-token tiles.
+        // The per-(row, token) double sums of a segment (the CTA's blocks of
+        // one tile) live in shared memory ([BN][kRows], two buffers
+        // alternating by segment) for 32-token tiles and in registers for
+        // 64-token tiles. Stream-K finishes a split tile in the last CTA to
+        // arrive, from partials in global memory; with clusters (32-token
+        // tiles), the K slices of a tile are added over distributed shared
+        // memory: CTA r adds slices 0..csize-1, in that order, for its
+        // 1/csize of the tile's outputs. Either way the result does not depend
+        // on timing.
         constexpr int kCols = R::kCols;  // token columns of this thread
+        constexpr uint32_t kTileOut = uint32_t(kRows) * BN;
         const int quarter = warp & 3;
         const int m = quarter * 32 + lane;  // the warp's TMEM lane quarter = its 32 weight rows
         const int col0 = (warp >> 2) * kCols;
+        const uint32_t et = uint32_t(warp) * 32 + uint32_t(lane);  // 0..255
         const uint32_t lane_base = uint32_t(quarter * 32) << 16;
-        const uint32_t first_tile = uint32_t(w_begin / nb);
-        double rsum[R::kSmemSums ? 1 : kCols];
-        double * ssum = sums + uint32_t(col0) * kRows + uint32_t(m);  // element t at ssum[t * kRows]
+        double rsum[R::kSmemSums ? 1 : kCols] = {};
+        uint32_t bi = 0;  // sums / staging buffer of the current tile
+        auto sbuf = [&](uint32_t k) { return sums + k * kTileOut; };
         auto sum_get = [&](int t) -> double {
-            if constexpr (R::kSmemSums) return ssum[t * kRows];
+            if constexpr (R::kSmemSums) return sbuf(bi)[uint32_t(col0 + t) * kRows + uint32_t(m)];
             else return rsum[t];
         };
         auto sum_set = [&](int t, double v) {
-            if constexpr (R::kSmemSums) ssum[t * kRows] = v;
+            if constexpr (R::kSmemSums) sbuf(bi)[uint32_t(col0 + t) * kRows + uint32_t(m)] = v;
             else rsum[t] = v;
         };
         const uint8_t * p1 = static_cast<const uint8_t *>(p.w.plane[1]);
@@ -984,25 +1100,55 @@ __global__ void __launch_bounds__(Roles<BN>::kThreads) __maxnreg__(Roles<BN>::kR
             else if constexpr (TYPE == JF_TENSOR_Q6_K) return uint32_t(__ldg(reinterpret_cast<const uint16_t *>(p2) + block));
             else return __ldg(reinterpret_cast<const uint32_t *>(p2) + block);
         };
-        uint64_t seg_begin = w_begin;
-        uint32_t i = 0, es = 0, eph = 0;
+        // the output value (tile row tr, token column tc) of tile (tm, tn):
+        // this row's segment, its epilogue and the store
+        auto store_out = [&](uint32_t tm, uint32_t tn, uint32_t tr, uint32_t tc, double sum) {
+            const uint32_t row = tm * kRows + tr, tok = tn * BN + tc;
+            if (row >= p.w.rows || tok >= p.n) return;
+            int k = 0;
+#pragma unroll
+            for (int j = 0; j < JFB_MATMUL_MAX_SEGMENTS - 1; ++j) k += (j < int(p.nseg) - 1 && row >= p.seg_end[j]) ? 1 : 0;
+            const uint32_t seg_begin_row = k == 0 ? 0u : p.seg_end[k - 1];
+            const uint32_t ld = p.seg_end[k] - seg_begin_row, r = row - seg_begin_row;
+            const uint32_t ep = p.seg_epilogue[k];
+            const uint64_t at = uint64_t(tok) * ld + r;
+            float v = __double2float_rn(sum);
+            if (ep == JFB_EPILOGUE_BIAS) v = __fadd_rn(v, p.seg_bias[k][r]);
+            else if (ep == JFB_EPILOGUE_RESIDUAL) v = __fadd_rn(v, p.seg_residual[k][at]);
+            p.seg_out[k][at] = v;
+        };
+        uint32_t i = 0, es = 0, eph = 0, tix = 0;  // unit, ring slot, segment (tile slice) of this CTA
+        uint32_t seg_b = 0;                         // first block of the current segment
+        const uint32_t first_tile = wk.tile0;
+        bool ok = true;
         Cursor cur;
-        cur.init(w_begin, nb, p.tiles_m);
-        uint32_t word_next = w_begin < w_end ? load_word(cur) : 0u;  // weights: written by no earlier kernel
-        pdl_wait();  // outputs, residuals and the stream-K workspace are shared with earlier kernels
-        for (uint64_t w = w_begin; w < w_end; ++w, ++i, cur.next(nb, p.tiles_m)) {
+        cur.init(wk, p.tiles_m);
+        uint32_t word_next = U > 0 ? load_word(cur) : 0u;  // weights: written by no earlier kernel
+        pdl_wait();  // outputs and residuals are shared with earlier kernels
+        for (; i < U && ok; ++i, cur.next(wk, p.tiles_m)) {
             // warp-uniform stop: the warp collectives below need every lane
             if (__any_sync(0xffffffffu, *abort_flag != 0)) break;
-            const uint32_t tile = cur.tile;
-            const uint32_t row = cur.tm * kRows + uint32_t(m), tok0 = cur.tn * BN;
-            if (w == seg_begin) {
+            if (i == 0 || cur.b == wk.b0) {
+                // a new segment: its sums buffer must be free (with clusters:
+                // read by every CTA of the cluster two tiles ago)
+                seg_b = cur.b;
+                if constexpr (R::kSmemSums) {
+                    bi = tix % R::kSumBufs;
+                    if (R::kClusters && csize > 1 && tix >= R::kSumBufs) {
+                        const uint32_t use = tix / R::kSumBufs - 1;
+                        if (!__all_sync(0xffffffffu, mbar_wait_cluster(&red_empty[bi], use & 1u, abort_flag, p.error,
+                                                                        kErrWaitReduce))) {
+                            break;
+                        }
+                    }
+                }
 #pragma unroll
                 for (int t = 0; t < kCols; ++t) sum_set(t, 0.0);
             }
             const uint32_t word = word_next;
-            if (w + 1 < w_end) {
+            if (i + 1 < U) {
                 Cursor nx = cur;
-                nx.next(nb, p.tiles_m);
+                nx.next(wk, p.tiles_m);
                 word_next = load_word(nx);
             }
             const uint32_t acc = i & 1u, use = i >> 1;
@@ -1062,86 +1208,96 @@ __global__ void __launch_bounds__(Roles<BN>::kThreads) __maxnreg__(Roles<BN>::kR
                     sum_set(t + 1, sum_get(t + 1) + double(c.y));
                 }
             }
-
             if (++es == kEpiRing) {
                 es = 0;
                 eph ^= 1u;
             }
 
-            // a segment ends where the CTA's range or the tile's K range ends
-            if (w + 1 != w_end && cur.b + 1 != nb) continue;
-            const bool complete = seg_begin == uint64_t(tile) * nb && w + 1 == uint64_t(tile + 1) * nb;
-            seg_begin = w + 1;
-            if (!complete) {
-                const uint32_t slot_p = 2 * blockIdx.x + (tile == first_tile ? 0 : 1);
-                double * part = p.partial + uint64_t(slot_p) * R::kSlotDoubles;
+            // a segment ends where this CTA's blocks of the tile or its range end
+            if (i + 1 != U && cur.b + 1 != wk.b1) continue;
+            const uint32_t tile_ix = tix++;
+            const uint32_t tile = cur.tile;
+            if (csize == 1) {
+                if (seg_b != 0 || cur.b + 1 != nb) {
+                    // stream-K: part of a tile. Each warp writes its partials;
+                    // the last warp to arrive (per tile and warp) adds every
+                    // contributor's, in CTA order.
+                    const uint64_t g = gridDim.x;
+                    const uint32_t slot_p = 2 * blockIdx.x + (tile == first_tile ? 0 : 1);
+                    double * part = p.partial + uint64_t(slot_p) * (uint64_t(kRows) * BN);
 #pragma unroll
-                for (int t = 0; t < kCols; ++t) part[(col0 + t) * kRows + m] = sum_get(t);
-                __threadfence();
-                __syncwarp();
-                const uint32_t lo = cta_of(uint64_t(tile) * nb, p.work, g);
-                const uint32_t hi = cta_of(uint64_t(tile + 1) * nb - 1, p.work, g);
-                uint32_t arrived = 0;
-                if (lane == 0) {
-                    uint32_t * counter = p.counters + uint64_t(tile) * R::kEpiWarps + warp;
-                    arrived = atomicAdd(counter, 1u) + 1;
-                    if (arrived == hi - lo + 1) *counter = 0;  // every contributor is in
-                }
-                arrived = __shfl_sync(0xffffffffu, arrived, 0);
-                if (arrived != hi - lo + 1) continue;
-                __threadfence();
-                // contributors after `lo` start inside this tile, so it is their
-                // first tile (slot 2c); `lo` used slot 2lo + 1 unless its range
-                // starts exactly at the tile. Partials are added in CTA order,
-                // eight tokens at a time, with the loads of several
-                // contributors in flight together.
-                const uint64_t lo_slot = 2 * uint64_t(lo) + (range_start(lo, p.work, g) == uint64_t(tile) * nb ? 0 : 1);
-                const double * lo_src = p.partial + lo_slot * R::kSlotDoubles + col0 * kRows + m;
-                const double * rest = p.partial + 2 * uint64_t(lo + 1) * R::kSlotDoubles + col0 * kRows + m;
-#pragma unroll
-                for (int t0 = 0; t0 < kCols; t0 += 8) {
-                    double acc8[8];
-#pragma unroll
-                    for (int k = 0; k < 8; ++k) acc8[k] = 0.0 + __ldcg(lo_src + (t0 + k) * kRows);
-#pragma unroll 4
-                    for (uint32_t c = 0; c < hi - lo; ++c) {
-                        const double * src = rest + uint64_t(2 * c) * R::kSlotDoubles;
-                        double v[8];
-#pragma unroll
-                        for (int k = 0; k < 8; ++k) v[k] = __ldcg(src + (t0 + k) * kRows);
-#pragma unroll
-                        for (int k = 0; k < 8; ++k) acc8[k] += v[k];
+                    for (int t = 0; t < kCols; ++t) part[(col0 + t) * kRows + m] = sum_get(t);
+                    __threadfence();
+                    __syncwarp();
+                    const uint32_t lo = cta_of(uint64_t(tile) * nb, p.work, g);
+                    const uint32_t hi = cta_of(uint64_t(tile + 1) * nb - 1, p.work, g);
+                    uint32_t arrived = 0;
+                    if (lane == 0) {
+                        uint32_t * counter = p.counters + uint64_t(tile) * R::kEpiWarps + warp;
+                        arrived = atomicAdd(counter, 1u) + 1;
+                        if (arrived == hi - lo + 1) *counter = 0;  // every contributor is in
                     }
+                    arrived = __shfl_sync(0xffffffffu, arrived, 0);
+                    if (arrived != hi - lo + 1) continue;
+                    __threadfence();
+                    // contributors after `lo` start inside this tile, so it is
+                    // their first tile (slot 2c); `lo` used slot 2lo + 1 unless
+                    // its range starts exactly at the tile
+                    const uint64_t lo_slot =
+                        2 * uint64_t(lo) + (range_start(lo, p.work, g) == uint64_t(tile) * nb ? 0 : 1);
+                    const double * lo_src = p.partial + lo_slot * (uint64_t(kRows) * BN) + col0 * kRows + m;
+                    const double * rest = p.partial + 2 * uint64_t(lo + 1) * (uint64_t(kRows) * BN) + col0 * kRows + m;
 #pragma unroll
-                    for (int k = 0; k < 8; ++k) sum_set(t0 + k, acc8[k]);
+                    for (int t0 = 0; t0 < kCols; t0 += 8) {
+                        double acc8[8];
+#pragma unroll
+                        for (int k = 0; k < 8; ++k) acc8[k] = 0.0 + __ldcg(lo_src + (t0 + k) * kRows);
+#pragma unroll 4
+                        for (uint32_t c = 0; c < hi - lo; ++c) {
+                            const double * src = rest + uint64_t(2 * c) * (uint64_t(kRows) * BN);
+                            double v[8];
+#pragma unroll
+                            for (int k = 0; k < 8; ++k) v[k] = __ldcg(src + (t0 + k) * kRows);
+#pragma unroll
+                            for (int k = 0; k < 8; ++k) acc8[k] += v[k];
+                        }
+#pragma unroll
+                        for (int k = 0; k < 8; ++k) sum_set(t0 + k, acc8[k]);
+                    }
                 }
+#pragma unroll
+                for (int t = 0; t < kCols; ++t) store_out(cur.tm, cur.tn, uint32_t(m), uint32_t(col0 + t), sum_get(t));
+                continue;
             }
-            if (row < p.w.rows) {
-                // this row's output segment
-                int k = 0;
-#pragma unroll
-                for (int j = 0; j < JFB_MATMUL_MAX_SEGMENTS - 1; ++j) k += (j < int(p.nseg) - 1 && row >= p.seg_end[j]) ? 1 : 0;
-                const uint32_t seg_begin_row = k == 0 ? 0u : p.seg_end[k - 1];
-                const uint32_t ld = p.seg_end[k] - seg_begin_row, r = row - seg_begin_row;
-                const uint32_t ep = p.seg_epilogue[k];
-                float * out = p.seg_out[k];
-                const float * bias = p.seg_bias[k];
-                const float * residual = p.seg_residual[k];
-#pragma unroll
-                for (int t = 0; t < kCols; ++t) {
-                    const uint32_t tok = tok0 + col0 + t;
-                    if (tok >= p.n) break;
-                    const uint64_t at = uint64_t(tok) * ld + r;
-                    float v = __double2float_rn(sum_get(t));
-                    if (ep == JFB_EPILOGUE_BIAS) v = __fadd_rn(v, bias[r]);
-                    else if (ep == JFB_EPILOGUE_RESIDUAL) v = __fadd_rn(v, residual[at]);
-                    out[at] = v;
+            if constexpr (R::kClusters) {
+                // clusters (32-token tiles only): add the csize K slices of the tile
+                const uint32_t ph = (tile_ix / R::kSumBufs) & 1u;
+                asm volatile("fence.acq_rel.cluster;" ::: "memory");
+                __syncwarp();
+                if (lane < csize) mbar_arrive_remote(&red_full[bi], lane);  // release: this warp's sums are written
+                if (!__all_sync(0xffffffffu, mbar_wait_cluster(&red_full[bi], ph, abort_flag, p.error, kErrWaitReduce))) {
+                    ok = false;
+                    break;
                 }
+                // this CTA's share of the tile's outputs, element o = token * kRows + row
+                const uint32_t share = kTileOut / csize;
+                const double * buf = sbuf(bi);
+                for (uint32_t o = wk.rank * share + et; o < (wk.rank + 1) * share; o += 32 * R::kEpiWarps) {
+                    double v = 0.0;
+                    for (uint32_t c = 0; c < csize; ++c) v += dsmem_f64(dsmem_addr(buf + o, c));
+                    store_out(cur.tm, cur.tn, o % kRows, o / kRows, v);
+                }
+                asm volatile("fence.acq_rel.cluster;" ::: "memory");
+                __syncwarp();
+                if (lane < csize) mbar_arrive_remote(&red_empty[bi], lane);  // release: this warp's reads are done
             }
         }
     }
     tc_fence_before();
-    __syncthreads();
+    // no CTA leaves while another CTA of its cluster may still read its shared
+    // memory or arrive on its barriers
+    if (csize > 1) cluster_sync_all();
+    else __syncthreads();
     tc_fence_after();
     if (warp == R::kMmaWarp) {
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
@@ -1167,7 +1323,7 @@ int sm_count() {
 uint32_t tile_tokens(uint32_t n) { return n <= 32 ? 32u : 64u; }
 
 struct Plan {
-    uint32_t bn, tiles_m, tiles, grid;
+    uint32_t bn, tiles_m, tiles;
     uint64_t work;
 };
 
@@ -1177,13 +1333,14 @@ Plan make_plan(uint32_t rows, uint32_t cols, uint32_t n) {
     pl.tiles_m = (rows + kRows - 1) / kRows;
     pl.tiles = pl.tiles_m * ((n + pl.bn - 1) / pl.bn);
     pl.work = uint64_t(pl.tiles) * (cols / kQK);
-    pl.grid = uint32_t(std::min<uint64_t>(pl.work, uint64_t(sm_count())));
     return pl;
 }
 
-// Workspace: partial slots for the largest grid and tile this device runs
-// (two per SM), then the arrival counters. Both offsets are the same for every
-// shape, so calls of different shapes can share one workspace on a stream.
+// Workspace (stream-K launches): partial slots for the largest grid and tile
+// this device runs (two per SM), then the arrival counters. Both offsets are
+// the same for every shape, so calls of different shapes can share one
+// workspace on a stream.
+constexpr uint32_t kMaxBN = 64;
 uint64_t partial_bytes() { return uint64_t(2) * uint64_t(sm_count()) * uint64_t(kRows) * kMaxBN * sizeof(double); }
 uint64_t workspace_bytes(const Plan & pl) {
     return partial_bytes() + uint64_t(pl.tiles) * Roles<32>::kEpiWarps * sizeof(uint32_t);
@@ -1293,8 +1450,69 @@ jfb_status build_maps(TcMaps & maps, const TcParams & p, const jfb_q8k & x, uint
     return status_ok();
 }
 
+// Clusters of `csize` CTAs of this kernel that fit on the device at once.
 template <uint32_t TYPE, int BN>
-jfb_status launch(TcParams & p, const jfb_q8k & x, uint32_t cols, uint32_t grid, cudaStream_t s) {
+int max_clusters(uint32_t csize) {
+    using L = Layout<TYPE, BN>;
+    using R = Roles<BN>;
+    if (csize == 1) return sm_count();  // one CTA per SM (shared memory)
+    static std::mutex mu;
+    static std::map<std::pair<int, uint32_t>, int> cache;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) dev = 0;
+    std::lock_guard<std::mutex> lock(mu);
+    const auto key = std::make_pair(dev, csize);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(csize);
+    cfg.blockDim = dim3(R::kThreads);
+    cfg.dynamicSmemBytes = L::kSmem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = csize;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, mmq_tc_kernel<TYPE, BN>, &cfg) != cudaSuccess) {
+        (void) cudaGetLastError();
+        n = 0;
+    }
+    cache.emplace(key, n);
+    return n;
+}
+
+// Schedule. With at least half as many tiles as SMs, stream-K over the whole
+// grid (csize = 1): its unit ranges balance any shape and few tiles are
+// split. With fewer tiles, every tile would be split across several CTAs and
+// finished through global memory, so tiles go to clusters instead: each of G
+// = min(clusters, T) clusters takes ceil(T / G) tiles of ceil(nb / csize)
+// units per CTA, and a tile's slices are added on chip (about one unit more).
+// The smallest cluster size of least cost wins.
+template <uint32_t TYPE, int BN>
+void choose_schedule(uint32_t tiles, uint32_t nb, uint64_t work, uint32_t & csize, uint32_t & grid) {
+    const uint32_t sms = uint32_t(max_clusters<TYPE, BN>(1));
+    csize = 1;
+    grid = uint32_t(std::min<uint64_t>(work, uint64_t(sms)));
+    if (!Roles<BN>::kClusters || 2 * uint64_t(tiles) >= sms) return;
+    uint64_t best = ~uint64_t(0);
+    for (uint32_t c = 2; c <= 8 && c <= nb; c *= 2) {
+        const int mc = max_clusters<TYPE, BN>(c);
+        if (mc <= 0) continue;
+        const uint32_t g = std::min<uint32_t>(tiles, uint32_t(mc));
+        const uint64_t cost = uint64_t((tiles + g - 1) / g) * ((nb + c - 1) / c + 1);
+        if (cost < best) {
+            best = cost;
+            csize = c;
+            grid = g * c;
+        }
+    }
+}
+
+template <uint32_t TYPE, int BN>
+jfb_status launch(TcParams & p, const jfb_q8k & x, uint32_t cols, cudaStream_t s) {
     using L = Layout<TYPE, BN>;
     using R = Roles<BN>;
     constexpr uint32_t bytes = L::kSmem;
@@ -1310,8 +1528,7 @@ jfb_status launch(TcParams & p, const jfb_q8k & x, uint32_t cols, uint32_t grid,
                   "converter lanes cover the rows");
     static_assert(L::NS % R::kGroups == 0 && L::NR % R::kGroups == 0, "each converter group owns its stages");
     static_assert(R::kEpiWarps * 32 * R::kCols == kRows * BN && R::kCols % 8 == 0, "epilogue threads cover the tile");
-    static_assert(BN <= kMaxBN, "partial slots are sized for kMaxBN");
-    static_assert(R::kEpiWarps == Roles<32>::kEpiWarps, "one counter layout for every tile width");
+    static_assert((kRows * BN) % (8 * R::kEpiWarps * 32) == 0, "every cluster share is a whole number of passes");
     TcMaps maps;
     jfb_status st = build_maps<TYPE, BN>(maps, p, x, cols);
     if (st.code != JFB_STATUS_OK) return st;
@@ -1332,17 +1549,41 @@ jfb_status launch(TcParams & p, const jfb_q8k & x, uint32_t cols, uint32_t grid,
             attribute_set[dev] = true;
         }
     }
+    uint32_t csize = 1, grid = 1;
+    choose_schedule<TYPE, BN>(p.tiles, p.blocks, p.work, csize, grid);
+    p.csize = csize;
     // programmatic dependent launch: the prologue (barriers, TMEM, the first
     // weight loads) overlaps the previous kernel; every write follows the
     // kernel's griddepcontrol.wait
-    const cudaError_t e = launch_k(kernel, dim3(grid), dim3(R::kThreads), bytes, s, maps, p);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(R::kThreads);
+    cfg.dynamicSmemBytes = bytes;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    unsigned na = 0;
+    if (csize > 1) {
+        attr[na].id = cudaLaunchAttributeClusterDimension;
+        attr[na].val.clusterDim.x = csize;
+        attr[na].val.clusterDim.y = 1;
+        attr[na].val.clusterDim.z = 1;
+        ++na;
+    }
+    if (pdl_enabled()) {
+        attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[na].val.programmaticStreamSerializationAllowed = 1;
+        ++na;
+    }
+    cfg.attrs = attr;
+    cfg.numAttrs = na;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, maps, p);
     if (e != cudaSuccess) return status_error(JFB_STATUS_CUDA_ERROR, "jfb_matmul_tc: %s", cudaGetErrorString(e));
     return launch_status("jfb_matmul_tc");
 }
 
 template <uint32_t TYPE>
 jfb_status launch_type(TcParams & p, const jfb_q8k & x, uint32_t cols, const Plan & pl, cudaStream_t s) {
-    return pl.bn == 32 ? launch<TYPE, 32>(p, x, cols, pl.grid, s) : launch<TYPE, 64>(p, x, cols, pl.grid, s);
+    return pl.bn == 32 ? launch<TYPE, 32>(p, x, cols, s) : launch<TYPE, 64>(p, x, cols, s);
 }
 
 }  // namespace
@@ -1416,6 +1657,7 @@ extern "C" jfb_status jfb_matmul_tc_segments(const jfb_weight * weight, const jf
     p.tiles_m = pl.tiles_m;
     p.tiles = pl.tiles;
     p.work = pl.work;
+    p.csize = 1;
     p.nseg = segment_count;
     for (uint32_t k = 0; k < JFB_MATMUL_MAX_SEGMENTS; ++k) {
         const bool used = k < segment_count;

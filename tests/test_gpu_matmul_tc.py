@@ -11,10 +11,13 @@ integer block sum above 2^24, where the CPU's (float)isum rounds.
 
 Shapes cover:
 - partial row tiles and partial token tiles;
-- one work unit per CTA, where every tile is split across eight CTAs;
-- CTAs whose work range straddles tiles, which exercises the stream-K fixup
-  and the partial slots;
-- repeated calls on one workspace, which must leave its counters at zero.
+- few tiles, scheduled on clusters: a tile's K blocks split across 2, 4 or 8
+  CTAs (the slices added over distributed shared memory), uneven slices,
+  32-token tiles (sums in shared memory) and 64-token tiles (sums staged);
+- many tiles, scheduled stream-K: CTA ranges that straddle tiles, which
+  exercises the global-memory fixup and the partial slots;
+- repeated calls on one workspace, which must leave its counters at zero
+  (stream-K) or untouched (clusters).
 """
 from __future__ import annotations
 
@@ -114,11 +117,14 @@ def bits(a) -> np.ndarray:
 @pytest.mark.parametrize("jf_type", KQ)
 @pytest.mark.parametrize("rows,cols,n", [
     (96, 256, 1),       # one block of K, one partial tile
-    (96, 2048, 5),      # one unit per CTA: every tile split across 8 CTAs
-    (300, 2560, 32),    # 3 row tiles x 10 blocks, a full token tile
-    (1000, 11008, 33),  # 8 x 2 tiles x 43 blocks over 148 CTAs: tiles straddle CTAs
+    (96, 2048, 5),      # one tile split into 8 one-block slices
+    (300, 2560, 32),    # 3 row tiles x 10 blocks, a full token tile: uneven slices
+    (1000, 11008, 32),  # clusters: 8 tiles x 43 blocks in slices of 5 and 6 blocks
+    (1000, 11008, 33),  # stream-K over 8 tiles of 64 tokens x 43 blocks: ranges straddle tiles
     (200, 1024, 100),   # 2 x 2 tiles of 64 tokens, partial token tile
     (520, 2048, 130),   # 5 x 3 tiles of 64 tokens
+    (19000, 256, 20),   # stream-K over 149 tiles of one block
+    (9600, 2560, 24),   # stream-K over 75 tiles x 10 blocks: ranges straddle tiles
 ])
 def test_tc_matches_oracle_and_cuda_core(K, jf_type, rows, cols, n):
     raw = random_blocks(jf_type, rows, cols, 7 + rows + jf_type, extreme_rows=(0, rows - 1))
@@ -150,8 +156,16 @@ def test_tc_encoder_weights_with_epilogues(K, jf_type):
     assert np.array_equal(bits(got), bits(ref + res_np))
 
 
-def test_tc_workspace_reuse_leaves_counters_zero(K):
-    jf_type, rows, cols, n = jfm.JF_TENSOR_Q4_K, 1000, 11008, 33
+@pytest.mark.parametrize("jf_type,rows,cols,n,clustered", [
+    (jfm.JF_TENSOR_Q4_K, 1000, 11008, 32, True),
+    (jfm.JF_TENSOR_Q4_K, 1000, 11008, 33, False),
+    (jfm.JF_TENSOR_Q6_K, 2048, 2048, 32, True),
+    (jfm.JF_TENSOR_Q4_K, 20000, 2048, 33, False),
+])
+def test_tc_repeated_calls_are_identical(K, jf_type, rows, cols, n, clustered):
+    """Split tiles are added in a fixed order, so repeated calls give the same
+    bits. Stream-K launches leave their arrival counters at zero; clustered
+    launches add the slices on chip and never write the workspace."""
     raw = random_blocks(jf_type, rows, cols, 99)
     w = K.DeviceWeight(jf_type, rows, cols, raw)
     x = activations(n, cols, 5)
@@ -159,10 +173,13 @@ def test_tc_workspace_reuse_leaves_counters_zero(K):
     for _ in range(3):
         again, _, ws = run_tc(K, w, x, workspace=ws)
         assert np.array_equal(bits(again), bits(first))
-    # partial slots: two per SM, sized for the widest token tile (64)
-    partial_bytes = 2 * torch.cuda.get_device_properties(0).multi_processor_count * 128 * 64 * 8
-    counters = ws[partial_bytes:].view(torch.int32)
-    assert int(counters.abs().sum().item()) == 0
+    if clustered:
+        assert int(ws.sum().item()) == 0
+    else:
+        # partial slots: two per SM, sized for the widest token tile (64)
+        partial_bytes = 2 * torch.cuda.get_device_properties(0).multi_processor_count * 128 * 64 * 8
+        counters = ws[partial_bytes:].view(torch.int32)
+        assert int(counters.abs().sum().item()) == 0
 
 
 def test_tc_shapes_share_one_workspace(K):
