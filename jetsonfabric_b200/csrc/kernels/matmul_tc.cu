@@ -1100,22 +1100,37 @@ __global__ void __launch_bounds__(Roles<BN>::kThreads) __maxnreg__(Roles<BN>::kR
             else if constexpr (TYPE == JF_TENSOR_Q6_K) return uint32_t(__ldg(reinterpret_cast<const uint16_t *>(p2) + block));
             else return __ldg(reinterpret_cast<const uint32_t *>(p2) + block);
         };
-        // the output value (tile row tr, token column tc) of tile (tm, tn):
-        // this row's segment, its epilogue and the store
-        auto store_out = [&](uint32_t tm, uint32_t tn, uint32_t tr, uint32_t tc, double sum) {
-            const uint32_t row = tm * kRows + tr, tok = tn * BN + tc;
-            if (row >= p.w.rows || tok >= p.n) return;
+        // one output row: its segment's output, epilogue and row stride, looked
+        // up once per row; store(tok, sum) then writes token tok of the row
+        struct OutRow {
+            float * out;
+            const float * bias;
+            const float * residual;
+            uint32_t ld, r, ep;
+            bool valid;
+        };
+        auto out_row = [&](uint32_t row) {
+            OutRow o;
+            o.valid = row < p.w.rows;
             int k = 0;
 #pragma unroll
             for (int j = 0; j < JFB_MATMUL_MAX_SEGMENTS - 1; ++j) k += (j < int(p.nseg) - 1 && row >= p.seg_end[j]) ? 1 : 0;
             const uint32_t seg_begin_row = k == 0 ? 0u : p.seg_end[k - 1];
-            const uint32_t ld = p.seg_end[k] - seg_begin_row, r = row - seg_begin_row;
-            const uint32_t ep = p.seg_epilogue[k];
-            const uint64_t at = uint64_t(tok) * ld + r;
+            o.ld = p.seg_end[k] - seg_begin_row;
+            o.r = row - seg_begin_row;
+            o.ep = p.seg_epilogue[k];
+            o.out = p.seg_out[k];
+            o.bias = p.seg_bias[k];
+            o.residual = p.seg_residual[k];
+            return o;
+        };
+        auto store = [&](const OutRow & o, uint32_t tok, double sum) {
+            if (!o.valid || tok >= p.n) return;
+            const uint64_t at = uint64_t(tok) * o.ld + o.r;
             float v = __double2float_rn(sum);
-            if (ep == JFB_EPILOGUE_BIAS) v = __fadd_rn(v, p.seg_bias[k][r]);
-            else if (ep == JFB_EPILOGUE_RESIDUAL) v = __fadd_rn(v, p.seg_residual[k][at]);
-            p.seg_out[k][at] = v;
+            if (o.ep == JFB_EPILOGUE_BIAS) v = __fadd_rn(v, o.bias[o.r]);
+            else if (o.ep == JFB_EPILOGUE_RESIDUAL) v = __fadd_rn(v, o.residual[at]);
+            o.out[at] = v;
         };
         uint32_t i = 0, es = 0, eph = 0, tix = 0;  // unit, ring slot, segment (tile slice) of this CTA
         uint32_t seg_b = 0;                         // first block of the current segment
@@ -1266,7 +1281,11 @@ __global__ void __launch_bounds__(Roles<BN>::kThreads) __maxnreg__(Roles<BN>::kR
                     }
                 }
 #pragma unroll
-                for (int t = 0; t < kCols; ++t) store_out(cur.tm, cur.tn, uint32_t(m), uint32_t(col0 + t), sum_get(t));
+                {
+                    const OutRow orow = out_row(cur.tm * kRows + uint32_t(m));
+#pragma unroll
+                    for (int t = 0; t < kCols; ++t) store(orow, cur.tn * BN + uint32_t(col0 + t), sum_get(t));
+                }
                 continue;
             }
             if constexpr (R::kClusters) {
@@ -1280,12 +1299,14 @@ __global__ void __launch_bounds__(Roles<BN>::kThreads) __maxnreg__(Roles<BN>::kR
                     break;
                 }
                 // this CTA's share of the tile's outputs, element o = token * kRows + row
+                // (the pass stride 256 is a multiple of kRows: a thread keeps its row)
                 const uint32_t share = kTileOut / csize;
                 const double * buf = sbuf(bi);
+                const OutRow orow = out_row(cur.tm * kRows + (wk.rank * share + et) % kRows);
                 for (uint32_t o = wk.rank * share + et; o < (wk.rank + 1) * share; o += 32 * R::kEpiWarps) {
                     double v = 0.0;
                     for (uint32_t c = 0; c < csize; ++c) v += dsmem_f64(dsmem_addr(buf + o, c));
-                    store_out(cur.tm, cur.tn, o % kRows, o / kRows, v);
+                    store(orow, cur.tn * BN + o / kRows, v);
                 }
                 asm volatile("fence.acq_rel.cluster;" ::: "memory");
                 __syncwarp();
