@@ -1,13 +1,15 @@
 /*
  * Model-package side of the jetsonfabric_b200 C ABI (host only, no CUDA):
- * the seeded synthetic Qwen2 package writer used by tests and the benchmark.
+ * the GGUF importer and the seeded synthetic Qwen2 package writer used by
+ * tests and the benchmark.
  *
  * The reference builds test packages with a GGML-based GGUF fixture writer
  * (runtime/compiler/model_fixture.cpp:76-133) and converts real models with a
  * GGML-based importer (runtime/compiler/jf_model_compile.cpp:547-645). Neither
- * can be built without GGML. This entry point writes JFM v2 packages directly:
- * GGUF metadata segment, one input, one output and one segment per layer, with
- * the manifest hashes the loader verifies.
+ * can be built without GGML. These entry points write JFM v2 packages
+ * directly: GGUF metadata segment, an optional shared segment, one input, one
+ * output and one segment per layer, with the manifest hashes the loader
+ * verifies.
  */
 #ifndef JFB_MODEL_H
 #define JFB_MODEL_H
@@ -73,6 +75,28 @@ jfb_status jfb_write_synthetic_package(
     const char * directory,
     jfb_synth_report * report
 );
+
+typedef struct jfb_import_report {
+    uint32_t layer_count;
+    uint32_t reserved;
+    uint64_t tensor_count;
+    uint64_t tensor_bytes;         /* sum of tensor payload bytes */
+    uint64_t package_bytes;        /* every package file, manifest included */
+    uint8_t source_sha256[32];
+    char architecture[64];         /* general.architecture, NUL-terminated */
+} jfb_import_report;
+
+/* Converts an unsplit GGUF (v2 or v3) into a new JFM v2 package directory
+ * `package_dir`, replacing the reference's jf-model-compile
+ * (runtime/compiler/jf_model_compile.cpp:547-645): the same segment
+ * assignment, byte layout and manifest, built in an exclusive staging
+ * directory next to the output and published by one no-replace rename.
+ * Fails (and leaves nothing behind) if the output exists, the source is not a
+ * regular file, the GGUF is malformed or split, a tensor type has no JFM v2
+ * geometry, a layer or the input has no tensors, output.weight is missing
+ * (tied embeddings), or the source changes while it is being read.
+ * `report` may be NULL. */
+jfb_status jfb_import_gguf(const char * gguf_path, const char * package_dir, jfb_import_report * report);
 
 /* Encodes `count` floats (a multiple of 256) into GGML K-quant blocks of the
  * given JFM type (Q2_K, Q4_K or Q6_K) with this library's encoders. Exposed so

@@ -32,6 +32,7 @@ JFM_SOURCES = [
     CSRC / "jfm" / "jfm_loader.c",
     CSRC / "jfm" / "sha256.c",
     CSRC / "jfm" / "synth_package.cpp",
+    CSRC / "jfm" / "gguf_import.cpp",
 ]
 
 

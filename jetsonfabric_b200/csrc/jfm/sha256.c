@@ -4,15 +4,11 @@
  * own sha256.c, runtime/engines/native/src/sha256.c, called from engine.c:262-276).
  */
 #include "jetsonfabric/engine.h"
+#include "sha256_stream.h"
 
 #include <string.h>
 
-typedef struct sha256_state {
-    uint32_t h[8];
-    uint64_t total_bytes;
-    uint8_t pending[64];
-    size_t pending_bytes;
-} sha256_state;
+typedef jfb_sha256_stream sha256_state;
 
 /* First 32 bits of the fractional parts of the cube roots of the first 64
  * primes (FIPS 180-4 section 4.2.2). */
@@ -119,3 +115,11 @@ void jf_sha256_buffer(const void * data, size_t size, uint8_t digest[32]) {
     sha256_feed(&state, (const uint8_t *) data, size);
     sha256_end(&state, digest);
 }
+
+void jfb_sha256_stream_begin(jfb_sha256_stream * s) { sha256_begin(s); }
+
+void jfb_sha256_stream_feed(jfb_sha256_stream * s, const void * data, size_t size) {
+    sha256_feed(s, (const uint8_t *) data, size);
+}
+
+void jfb_sha256_stream_end(jfb_sha256_stream * s, uint8_t digest[32]) { sha256_end(s, digest); }

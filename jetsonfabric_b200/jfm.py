@@ -66,6 +66,12 @@ class SynthReport(C.Structure):
     _fields_ = [("weight_bytes", C.c_uint64), ("tensor_count", C.c_uint64), ("file_bytes", C.c_uint64)]
 
 
+class ImportReport(C.Structure):
+    _fields_ = [("layer_count", C.c_uint32), ("reserved", C.c_uint32), ("tensor_count", C.c_uint64),
+                ("tensor_bytes", C.c_uint64), ("package_bytes", C.c_uint64), ("source_sha256", C.c_uint8 * 32),
+                ("architecture", C.c_char * 64)]
+
+
 class JfmError(RuntimeError):
     def __init__(self, code: int, message: str):
         super().__init__(message)
@@ -112,6 +118,8 @@ def lib() -> C.CDLL:
         L.jfb_write_synthetic_package.restype = Status
         L.jfb_quantize_blocks.argtypes = [C.c_uint32, C.c_void_p, C.c_size_t, C.c_void_p, C.c_size_t]
         L.jfb_quantize_blocks.restype = Status
+        L.jfb_import_gguf.argtypes = [C.c_char_p, C.c_char_p, C.POINTER(ImportReport)]
+        L.jfb_import_gguf.restype = Status
         _lib = L
     return _lib
 
@@ -126,6 +134,16 @@ def sha256(data: bytes) -> bytes:
     buf = C.create_string_buffer(data, len(data))
     lib().jf_sha256_buffer(buf, len(data), C.byref(out))
     return bytes(out)
+
+
+def import_gguf(gguf_path: str | Path, package_dir: str | Path) -> dict:
+    """Converts a GGUF file into a new JFM v2 package directory (jfb_import_gguf);
+    the equivalent of the reference's `jf-model-compile --input --output`."""
+    rep = ImportReport()
+    _check(lib().jfb_import_gguf(str(gguf_path).encode(), str(package_dir).encode(), C.byref(rep)))
+    return {"format": "jfm-v2", "architecture": rep.architecture.decode(), "source_sha256": bytes(rep.source_sha256).hex(),
+            "layer_count": rep.layer_count, "tensor_count": rep.tensor_count, "tensor_bytes": rep.tensor_bytes,
+            "package_bytes": rep.package_bytes}
 
 
 def type_layout(jf_type: int) -> tuple[int, int]:
@@ -262,3 +280,28 @@ QWEN2_PRESETS = {
                 feed_forward_length=27648, vocabulary_size=152064, layer_type=JF_TENSOR_Q2_K,
                 embedding_type=JF_TENSOR_Q2_K, more_bits_q6k=False),
 }
+
+
+def main(argv: list[str] | None = None) -> int:
+    """`python -m jetsonfabric_b200.jfm --input model.gguf --output model.jfm`: the
+    command line of the reference's jf-model-compile (jf_model_compile.cpp:374-396),
+    printing the same JSON summary on success."""
+    import argparse
+    import json
+    import sys
+
+    ap = argparse.ArgumentParser(prog="jetsonfabric_b200.jfm", description="Convert a GGUF file to a JFM v2 package")
+    ap.add_argument("--input", required=True)
+    ap.add_argument("--output", required=True)
+    args = ap.parse_args(argv)
+    try:
+        report = import_gguf(args.input, args.output)
+    except JfmError as e:
+        print(f"jf-model-compile: {e}", file=sys.stderr)
+        return 1
+    print(json.dumps(report, indent=2))
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())
