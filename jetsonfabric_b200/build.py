@@ -33,6 +33,7 @@ JFM_SOURCES = [
     CSRC / "jfm" / "sha256.c",
     CSRC / "jfm" / "synth_package.cpp",
     CSRC / "jfm" / "gguf_import.cpp",
+    CSRC / "tokenizer" / "bpe_tokenizer.cpp",
 ]
 
 

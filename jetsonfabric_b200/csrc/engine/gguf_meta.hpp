@@ -27,15 +27,21 @@ enum class GgufType : std::uint32_t {
 
 struct GgufValue {
     GgufType type = GgufType::U8;
-    std::uint64_t u = 0;   // unsigned / bool payload
+    std::uint64_t u = 0;   // unsigned / bool payload; element count of an array
     std::int64_t i = 0;    // signed payload
     double f = 0.0;        // float payload
     std::string s;         // string payload
+    // arrays, kept only when the reader is asked to: string elements, or
+    // integer and bool elements (as int64)
+    GgufType element = GgufType::U8;
+    std::vector<std::string> strings;
+    std::vector<std::int64_t> integers;
 };
 
 class GgufMetadata {
 public:
-    explicit GgufMetadata(std::span<const std::byte> blob) : data_(blob) {
+    explicit GgufMetadata(std::span<const std::byte> blob, bool keep_arrays = false)
+        : data_(blob), keep_arrays_(keep_arrays) {
         if (blob.size() < 24 || std::memcmp(blob.data(), "GGUF", 4) != 0) {
             throw std::runtime_error("JFM metadata is not a GGUF header");
         }
@@ -96,7 +102,18 @@ private:
             const auto element = static_cast<GgufType>(read<std::uint32_t>());
             const std::uint64_t count = read<std::uint64_t>();
             if (element == GgufType::ARRAY) throw std::runtime_error("nested GGUF arrays are not supported");
-            for (std::uint64_t k = 0; k < count; ++k) (void) read_value(element);  // skipped
+            if (count > data_.size()) throw std::runtime_error("GGUF array is truncated");
+            v.element = element;
+            for (std::uint64_t k = 0; k < count; ++k) {
+                GgufValue e = read_value(element);
+                if (!keep_arrays_) continue;
+                if (element == GgufType::STRING) v.strings.push_back(std::move(e.s));
+                else if (element == GgufType::F32 || element == GgufType::F64) v.integers.push_back(std::int64_t(e.f));
+                else v.integers.push_back(e.type == GgufType::I8 || e.type == GgufType::I16 || e.type == GgufType::I32 ||
+                                                  e.type == GgufType::I64
+                                              ? e.i
+                                              : std::int64_t(e.u));
+            }
             v.u = count;
             break;
         }
@@ -106,6 +123,7 @@ private:
     }
 
     std::span<const std::byte> data_;
+    bool keep_arrays_ = false;
     std::size_t pos_ = 0;
     std::map<std::string, GgufValue> values_;
 };

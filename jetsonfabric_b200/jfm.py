@@ -120,6 +120,17 @@ def lib() -> C.CDLL:
         L.jfb_quantize_blocks.restype = Status
         L.jfb_import_gguf.argtypes = [C.c_char_p, C.c_char_p, C.POINTER(ImportReport)]
         L.jfb_import_gguf.restype = Status
+        L.jfb_tokenizer_open.argtypes = [C.c_char_p, C.POINTER(C.c_void_p)]
+        L.jfb_tokenizer_open.restype = Status
+        L.jfb_tokenizer_close.argtypes = [C.c_void_p]
+        L.jfb_tokenizer_close.restype = None
+        L.jfb_tokenizer_tokenize.argtypes = [C.c_void_p, C.c_char_p, C.c_size_t, C.POINTER(C.c_int32), C.c_size_t,
+                                             C.POINTER(C.c_size_t)]
+        L.jfb_tokenizer_tokenize.restype = Status
+        L.jfb_tokenizer_token_piece.argtypes = [C.c_void_p, C.c_int32, C.c_char_p, C.c_size_t, C.POINTER(C.c_size_t)]
+        L.jfb_tokenizer_token_piece.restype = Status
+        L.jfb_tokenizer_is_end_token.argtypes = [C.c_void_p, C.c_int32]
+        L.jfb_tokenizer_is_end_token.restype = C.c_int
         _lib = L
     return _lib
 
@@ -144,6 +155,48 @@ def import_gguf(gguf_path: str | Path, package_dir: str | Path) -> dict:
     return {"format": "jfm-v2", "architecture": rep.architecture.decode(), "source_sha256": bytes(rep.source_sha256).hex(),
             "layer_count": rep.layer_count, "tensor_count": rep.tensor_count, "tensor_bytes": rep.tensor_bytes,
             "package_bytes": rep.package_bytes}
+
+
+class Tokenizer:
+    """The package's text tokenizer (jfb_tokenizer_*): the reference tokenizer
+    interface's tokenize / token_piece / is_end_token (tokenizer.hpp:9-16)."""
+
+    def __init__(self, package_dir: str | Path):
+        h = C.c_void_p()
+        _check(lib().jfb_tokenizer_open(str(package_dir).encode(), C.byref(h)))
+        self._h = h
+
+    def close(self) -> None:
+        if self._h:
+            lib().jfb_tokenizer_close(self._h)
+            self._h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def tokenize(self, text: str | bytes) -> list[int]:
+        data = text.encode() if isinstance(text, str) else bytes(text)
+        cap = len(data) + 8
+        while True:
+            buf = (C.c_int32 * cap)()
+            n = C.c_size_t()
+            _check(lib().jfb_tokenizer_tokenize(self._h, data, len(data), buf, cap, C.byref(n)))
+            if n.value <= cap:
+                return list(buf[:n.value])
+            cap = n.value
+
+    def token_piece(self, token: int) -> bytes:
+        n = C.c_size_t()
+        _check(lib().jfb_tokenizer_token_piece(self._h, token, None, 0, C.byref(n)))
+        buf = C.create_string_buffer(max(n.value, 1))
+        _check(lib().jfb_tokenizer_token_piece(self._h, token, buf, n.value, C.byref(n)))
+        return buf.raw[:n.value]
+
+    def is_end_token(self, token: int) -> bool:
+        return bool(lib().jfb_tokenizer_is_end_token(self._h, token))
 
 
 def type_layout(jf_type: int) -> tuple[int, int]:
