@@ -428,6 +428,18 @@ __global__ void __launch_bounds__(kDThreads, 1) dmma_attention_kernel(
     const uint16_t * kbase = slot.k + uint64_t(layer) * slot.capacity * kvd + kvh * D;
     const uint16_t * vbase = slot.v + uint64_t(layer) * slot.capacity * kvd + kvh * D;
     float * xrow = xs + row_local * 8 * lay.kcp;
+    if (R == 1) {
+        // decode-sized calls: this CTA's K and V rows into L2 while the
+        // previous kernel finishes. The newest row may still be in flight
+        // from that kernel; a prefetch cannot make it stale, as L2 is the
+        // point every SM's stores reach and the rows are read after the wait.
+        constexpr uint32_t kLines = (D * 2 + 127) / 128;
+        for (uint32_t i = threadIdx.x; i < nk * kLines; i += kDThreads) {
+            const uint64_t at = uint64_t(kc0 + i / kLines) * kvd + (i % kLines) * 64;
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(kbase + at));
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(vbase + at));
+        }
+    }
     pdl_wait();
 
     // ---- scores of this warp's key groups. Four independent accumulator
