@@ -552,17 +552,10 @@ __global__ void __launch_bounds__(kDThreads, 1) dmma_attention_kernel(
         ginv[threadIdx.x] = t > 0.0 ? __double2float_rn(__ddiv_rn(1.0, t)) : 0.0f;
     }
     __syncthreads();
-    for (uint32_t pr = uint32_t(warp); pr < R * 8; pr += kDWarps) {
-        const uint32_t rl = pr / 8, h = pr % 8;
-        if (h >= G) continue;
-        const uint32_t keys = nk_s[rl];
-        float * xr = xs + (rl * 8 + h) * lay.kcp;
-        const float inv = ginv[pr];
-        for (uint32_t j = uint32_t(lane); j < keys; j += 32) xr[j] = __half2float(__float2half_rn(__fmul_rn(xr[j], inv)));
-    }
-    __syncthreads();
 
-    // ---- P V over this warp's keys: o[t][i] = O[head gq][dim 16 (2 tq + i) + t]
+    // ---- P V over this warp's keys: o[t][i] = O[head gq][dim 16 (2 tq + i) + t],
+    // each probability p = f16(e * (1 / sum)) formed as it is used (the zeroed
+    // key tail stays 0)
     double o[NT][2];
 #pragma unroll
     for (int t = 0; t < NT; ++t) o[t][0] = o[t][1] = 0.0;
@@ -570,6 +563,7 @@ __global__ void __launch_bounds__(kDThreads, 1) dmma_attention_kernel(
         const uint32_t k_begin = 8 * g_begin, k_end = 8 * g_end;  // multiples of 8, within the zeroed tail
         const float * prow = xrow + gq * lay.kcp;
         const bool live = uint32_t(gq) < G;
+        const float inv = live ? ginv[row_local * 8 + uint32_t(gq)] : 0.0f;
         auto load_v = [&](uint32_t kk, uint4 (&raw)[NT / 8]) {
             const uint32_t j = kk + uint32_t(tq);  // this lane's V row (relative to kc0)
 #pragma unroll
@@ -579,7 +573,8 @@ __global__ void __launch_bounds__(kDThreads, 1) dmma_attention_kernel(
             }
         };
         auto pv_step = [&](uint32_t kk, const uint4 (&cur)[NT / 8]) {
-            const double a = live ? double(prow[kk + uint32_t(tq)]) * kTwo1008 : 0.0;
+            const double a =
+                live ? double(__half2float(__float2half_rn(__fmul_rn(prow[kk + uint32_t(tq)], inv)))) * kTwo1008 : 0.0;
 #pragma unroll
             for (int c = 0; c < NT / 8; ++c) {
                 const uint32_t w[4] = {cur[c].x, cur[c].y, cur[c].z, cur[c].w};
