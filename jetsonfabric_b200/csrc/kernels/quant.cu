@@ -43,8 +43,17 @@ __global__ void __launch_bounds__(kThreads) rmsnorm_quant_kernel(
     constexpr int kRounds = kMaxRowChunks / 8;  // 2048 values per round
     __shared__ double red[kThreads / 32];
     pdl_trigger();
-    pdl_wait();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // the norm weight is written by no earlier kernel: its loads overlap the
+    // wait for the previous one
+    float wv[kRounds][8];
+#pragma unroll
+    for (int c = 0; c < kRounds; ++c) {
+        const uint32_t base = uint32_t(warp + 8 * c) * kQK + 8 * lane;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) wv[c][j] = base + j < cols ? w[base + j] : 0.0f;
+    }
+    pdl_wait();
     const uint32_t row = blockIdx.x;
     const uint64_t src_row = row_index != nullptr ? uint64_t(row_index[row]) : uint64_t(row);
     const float * xr = x + src_row * cols;
@@ -72,7 +81,7 @@ __global__ void __launch_bounds__(kThreads) rmsnorm_quant_kernel(
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
             const uint32_t i = base + j;
-            y.v[j] = i < cols ? __fmul_rn(__fmul_rn(v[c][j], scale), w[i]) : 0.0f;
+            y.v[j] = i < cols ? __fmul_rn(__fmul_rn(v[c][j], scale), wv[c][j]) : 0.0f;
             if (out_f32 != nullptr && i < cols) out_f32[uint64_t(row) * cols + i] = y.v[j];
         }
         if (quantize) q8k_block_warp(y, q8_dest(q8, row, blk, cols / kQK));

@@ -39,11 +39,14 @@ __global__ void __launch_bounds__(kThreads) rope_kv_kernel(float * __restrict__ 
     const uint32_t hd = heads * head_dim, kvd = kv_heads * head_dim;
     const uint32_t idx = blockIdx.y * kThreads + threadIdx.x;
     const uint32_t qitems = heads * pairs;
+    // this item's (cos, sin): the table is written by no earlier kernel
+    float2 c = make_float2(0.0f, 0.0f);
+    if (idx < qitems) c = cs[idx % pairs];
+    else if (idx < qitems + kvd && (idx - qitems) % head_dim < rope_dims) c = cs[(idx - qitems) % head_dim % pairs];
     pdl_wait();                                // q, k, v come from the projection before this kernel
     if (idx < qitems) {
         const uint32_t h = idx / pairs, i = idx % pairs;
         float * x = q + uint64_t(r) * hd + h * head_dim;
-        const float2 c = cs[i];
         const float x0 = x[i], x1 = x[i + pairs];
         x[i] = __fsub_rn(__fmul_rn(x0, c.x), __fmul_rn(x1, c.y));
         x[i + pairs] = __fadd_rn(__fmul_rn(x0, c.y), __fmul_rn(x1, c.x));
@@ -54,7 +57,6 @@ __global__ void __launch_bounds__(kThreads) rope_kv_kernel(float * __restrict__ 
         float y;
         if (e < rope_dims) {
             const uint32_t i = e % pairs;
-            const float2 c = cs[i];
             const float x0 = kr[h * head_dim + i], x1 = kr[h * head_dim + i + pairs];
             y = e < pairs ? __fsub_rn(__fmul_rn(x0, c.x), __fmul_rn(x1, c.y))
                           : __fadd_rn(__fmul_rn(x0, c.y), __fmul_rn(x1, c.x));
