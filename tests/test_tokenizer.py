@@ -27,6 +27,8 @@ tokenizers = pytest.importorskip("tokenizers")
 
 QWEN2_PATTERN = (r"(?i:'s|'t|'re|'ve|'m|'ll|'d)|[^\r\n\p{L}\p{N}]?\p{L}+|\p{N}| ?[^\s\p{L}\p{N}]+[\r\n]*"
                  r"|\s*[\r\n]+|\s+(?!\S)|\s+")
+# the "llama-bpe" pre-tokenizer: the same pattern with digits in runs of up to three
+LLAMA_BPE_PATTERN = QWEN2_PATTERN.replace(r"|\p{N}|", r"|\p{N}{1,3}|")
 SPECIALS = ["<|endoftext|>", "<|im_start|>", "<|im_end|>"]
 
 WORDS = ["the", "The", "quick", "brown", "fox", "jumps", "over", "lazy", "dog", "don't", "I'LL", "we've", "You'Re",
@@ -74,15 +76,14 @@ def gguf_metadata(kv: list) -> bytes:
     return bytes(out + b"\0" * (-len(out) % 32))
 
 
-@pytest.fixture(scope="module")
-def trained():
+def train(pattern: str):
     from tokenizers import Regex, Tokenizer, decoders, models, pre_tokenizers, trainers
 
     rng = random.Random(7)
     corpus = [random_text(rng, 40) for _ in range(400)]
     hf = Tokenizer(models.BPE())
     hf.pre_tokenizer = pre_tokenizers.Sequence([
-        pre_tokenizers.Split(Regex(QWEN2_PATTERN), behavior="isolated", invert=False),
+        pre_tokenizers.Split(Regex(pattern), behavior="isolated", invert=False),
         pre_tokenizers.ByteLevel(add_prefix_space=False, trim_offsets=False, use_regex=False)])
     hf.decoder = decoders.ByteLevel()
     trainer = trainers.BpeTrainer(vocab_size=1200, special_tokens=SPECIALS, show_progress=False,
@@ -94,6 +95,11 @@ def trained():
     tokens = [t for t, _ in vocab]
     merges = [m if isinstance(m, str) else " ".join(m) for m in model["merges"]]
     return hf, tokens, merges
+
+
+@pytest.fixture(scope="module")
+def trained():
+    return train(QWEN2_PATTERN)
 
 
 def write_package(tmp_path, tokens, merges, extra=(), pre="qwen2", model="gpt2"):
@@ -126,6 +132,23 @@ def test_matches_hf_byte_level_bpe(trained, tmp_path):
     texts = EDGE_CASES + [random_text(rng, rng.randint(1, 60)) for _ in range(300)]
     for text in texts:
         assert tok.tokenize(text) == hf.encode(text).ids, repr(text)
+
+
+def test_llama_bpe_pre_tokenizer_matches_hf(tmp_path):
+    """The "llama-bpe" pre-tokenizer (digit runs of up to three) against the
+    same published pattern in Hugging Face `tokenizers`, on a vocabulary
+    trained with it."""
+    hf, tokens, merges = train(LLAMA_BPE_PATTERN)
+    assert LLAMA_BPE_PATTERN != QWEN2_PATTERN
+    tok = jfm.Tokenizer(write_package(tmp_path, tokens, merges, pre="llama-bpe"))
+    rng = random.Random(13)
+    digits = ["1234567", "x12345y", "2026-12-02", "3.14159265", "1,000,000", "１２３４５", "42 42 4242", "007"]
+    texts = EDGE_CASES + digits + [random_text(rng, rng.randint(1, 60)) for _ in range(200)]
+    for text in texts:
+        assert tok.tokenize(text) == hf.encode(text).ids, repr(text)
+    # the two pre-tokenizers split digit runs differently
+    qwen2 = jfm.Tokenizer(write_package(tmp_path / "q", tokens, merges, pre="qwen2"))
+    assert len(qwen2.tokenize("1234567")) >= len(tok.tokenize("1234567"))
 
 
 def test_pieces_round_trip_the_text(trained, tmp_path):
