@@ -16,6 +16,7 @@ malformed GGUF headers all fail and leave nothing behind.
 from __future__ import annotations
 
 import hashlib
+import shutil
 import struct
 from pathlib import Path
 
@@ -301,6 +302,44 @@ def test_rejects_malformed_headers(tmp_path):
     expect_failure(tmp_path, good[:200], "past the end")
     # a payload that runs past the end of the file
     expect_failure(tmp_path, good[:-16], "exceeds the source GGUF")
+
+
+def test_truncated_and_corrupted_sources_fail_cleanly(tmp_path):
+    """Every prefix of a valid GGUF and seeded single-byte corruptions of it:
+    the importer either publishes a package or raises JfmError, never reads
+    out of bounds, and never leaves a staging directory or a partial
+    package behind."""
+    import random
+
+    good = gguf_bytes(qwen2_kv(2), small_model())
+    src = tmp_path / "x.gguf"
+    out = tmp_path / "x.jfm"
+
+    def attempt(data: bytes) -> bool:
+        src.write_bytes(data)
+        try:
+            jfm.import_gguf(src, out)
+        except jfm.JfmError:
+            assert not out.exists()
+            assert not list(tmp_path.glob("x.jfm.tmp.*"))
+            return False
+        assert not list(tmp_path.glob("x.jfm.tmp.*"))
+        with jfm.Model(out):
+            pass
+        shutil.rmtree(out)
+        return True
+
+    for n in range(len(good)):
+        assert not attempt(good[:n]), n
+    rng = random.Random(5)
+    published = 0
+    for _ in range(300):
+        data = bytearray(good)
+        at = rng.randrange(len(data))
+        data[at] ^= 1 << rng.randrange(8)
+        published += attempt(bytes(data))
+    assert 0 < published < 300  # payload flips still import; header flips are rejected
+    assert attempt(good)
 
 
 def test_command_line(tmp_path, capsys):

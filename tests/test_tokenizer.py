@@ -178,6 +178,25 @@ def test_end_tokens_and_bos(trained, tmp_path):
     assert jfm.Tokenizer(kv_bos).tokenize("hi")[0] == tokens.index("<|endoftext|>")
 
 
+def test_truncated_metadata_is_rejected(trained, tmp_path):
+    """Prefixes of a tokenizer's metadata.gguf (every 5th length and the last
+    64) raise JfmError; none reads past the end."""
+    _, tokens, merges = trained
+    d = write_package(tmp_path, tokens, merges)
+    meta = (d / "metadata.gguf").read_bytes()
+    cut = tmp_path / "cut"
+    cut.mkdir()
+    lengths = sorted(set(range(0, len(meta), 5)) | set(range(max(0, len(meta) - 64), len(meta))))
+    for n in lengths:
+        (cut / "metadata.gguf").write_bytes(meta[:n])
+        try:
+            jfm.Tokenizer(cut)
+        except jfm.JfmError:
+            continue
+        # only a prefix that ends in the zero padding after the last value can parse
+        assert meta[n:].strip(b"\0") == b"", n
+
+
 def test_rejections(trained, tmp_path):
     _, tokens, merges = trained
     with pytest.raises(jfm.JfmError, match="metadata.gguf"):
