@@ -152,6 +152,23 @@ def test_rejects_invalid_inputs(tmp_path):
     _rejects(dup_name, jfm.JF_STATUS_FORMAT_ERROR)
 
 
+@pytest.mark.parametrize("name", ["manifest.jfm", "input.jfs", "layer-00000.jfs", "layer-00001.jfs", "output.jfs",
+                                  "metadata.gguf"])
+def test_truncated_golden_files_are_rejected(tmp_path, name):
+    """Every proper prefix of each golden package file, opened for the whole
+    model without hash verification: the structural checks alone reject it
+    (no mapping past the end of a file)."""
+    package = decode_golden(tmp_path / "pkg")
+    full = (package / name).read_bytes()
+    with jfm.Model(package, 0, 2, verify_hashes=False):
+        pass
+    for n in range(len(full)):
+        (package / name).write_bytes(full[:n])
+        with pytest.raises(jfm.JfmError):
+            jfm.Model(package, 0, 2, verify_hashes=False)
+    (package / name).write_bytes(full)
+
+
 def test_reference_fixture_residency(fixture_package):
     """compiler_integration_test.cmake:29-52: 27 tensors total, 13 on stage 0-1."""
     with jfm.Model(fixture_package, 0, 1) as first:
