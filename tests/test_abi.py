@@ -1,5 +1,5 @@
 """The C-ABI libraries load without a GPU and export every symbol their
-headers declare (include/jetsonfabric/engine.h, include/jfb/*.h)."""
+headers declare (every C header under include/)."""
 from __future__ import annotations
 
 import ctypes as C
@@ -9,9 +9,10 @@ from pathlib import Path
 import pytest
 
 REPO = Path(__file__).resolve().parent.parent
-HEADERS = [REPO / "include" / "jetsonfabric" / "engine.h", REPO / "include" / "jfb" / "jfb_kernels.h",
-           REPO / "include" / "jfb" / "jfb_engine.h", REPO / "include" / "jfb" / "jfb_model.h",
-           REPO / "include" / "jfb" / "jfb_status.h"]
+HEADERS = sorted((REPO / "include").glob("*/*.h"))
+# the host-only library (loader, importer, tokenizer) and the headers it serves
+JFM_HEADERS = [REPO / "include" / "jetsonfabric" / "engine.h", REPO / "include" / "jfb" / "jfb_model.h",
+               REPO / "include" / "jfb" / "jfb_tokenizer.h"]
 
 
 def declared_functions(header: Path) -> list[str]:
@@ -19,6 +20,12 @@ def declared_functions(header: Path) -> list[str]:
     text = re.sub(r"//[^\n]*", "", text)
     names = re.findall(r"\b((?:jf|jfb)_[a-z0-9_]+)\s*\(", text)
     return sorted(set(n for n in names if not n.endswith("_t")))
+
+
+def test_headers_are_all_listed():
+    names = {h.name for h in HEADERS}
+    assert {"engine.h", "jfb_kernels.h", "jfb_engine.h", "jfb_model.h", "jfb_status.h", "jfb_tokenizer.h"} <= names
+    assert all(declared_functions(h) for h in HEADERS if h.name != "jfb_status.h")
 
 
 def test_jfb_library_exports_every_declared_symbol():
@@ -32,7 +39,7 @@ def test_jfb_library_exports_every_declared_symbol():
 def test_jfm_library_exports_loader_abi():
     from jetsonfabric_b200 import jfm
     lib = jfm.lib()
-    for h in [HEADERS[0], HEADERS[3]]:
+    for h in JFM_HEADERS:
         missing = [n for n in declared_functions(h) if not hasattr(lib, n)]
         assert not missing, missing
 

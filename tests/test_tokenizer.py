@@ -197,6 +197,66 @@ def test_truncated_metadata_is_rejected(trained, tmp_path):
         assert meta[n:].strip(b"\0") == b"", n
 
 
+CPP_CONSUMER = r"""
+#include "jetsonfabric/tokenizer.hpp"
+
+#include <cstdio>
+#include <stdexcept>
+#include <string>
+
+int main(int argc, char ** argv) {
+    if (argc != 3) return 2;
+    const auto tok = jetsonfabric::native::open_package_tokenizer(argv[1]);
+    const std::string text = argv[2];
+    std::string joined;
+    for (const std::int32_t id : tok->tokenize(text)) {
+        std::printf("%d ", id);
+        joined += tok->token_piece(id);
+    }
+    std::printf("\n%s\n%d\n", joined == text ? "round-trip" : "mismatch", tok->is_end_token(-1) ? 1 : 0);
+    try {
+        (void) tok->tokenize("");
+        std::printf("accepted\n");
+    } catch (const std::invalid_argument &) {
+        std::printf("invalid_argument\n");
+    }
+    try {
+        (void) jetsonfabric::native::open_package_tokenizer(std::string(argv[1]) + "/missing");
+        std::printf("accepted\n");
+    } catch (const std::invalid_argument &) {
+        std::printf("invalid_argument\n");
+    }
+    return 0;
+}
+"""
+
+
+def test_cpp_interface_matches_the_c_abi(trained, tmp_path):
+    """A C++ caller of the reference's Tokenizer interface
+    (include/jetsonfabric/tokenizer.hpp) linked against libjfm.so gets the
+    ids of the C ABI, the documented exceptions, and round-tripping pieces."""
+    import shutil
+    import subprocess
+    from pathlib import Path
+
+    if shutil.which("g++") is None:
+        pytest.skip("no C++ compiler")
+    jfm.lib()  # builds libjfm.so if needed
+    repo = Path(__file__).resolve().parent.parent
+    lib_dir = repo / "jetsonfabric_b200" / "lib"
+    src = tmp_path / "consumer.cpp"
+    src.write_text(CPP_CONSUMER)
+    exe = tmp_path / "consumer"
+    subprocess.run(["g++", "-std=c++20", "-O1", f"-I{repo / 'include'}", str(src), "-o", str(exe), f"-L{lib_dir}",
+                    "-ljfm", f"-Wl,-rpath,{lib_dir}"], check=True)
+    _, tokens, merges = trained
+    d = write_package(tmp_path, tokens, merges)
+    text = "Hello world, naïve café <|im_start|>user 12345"
+    out = subprocess.run([str(exe), str(d), text], check=True, capture_output=True, text=True).stdout.split("\n")
+    assert [int(x) for x in out[0].split()] == jfm.Tokenizer(d).tokenize(text)
+    assert out[1:5] == ["round-trip", "1", "invalid_argument", "invalid_argument"]
+
+
 def test_rejections(trained, tmp_path):
     _, tokens, merges = trained
     with pytest.raises(jfm.JfmError, match="metadata.gguf"):
