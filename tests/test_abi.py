@@ -51,3 +51,68 @@ def test_engine_module_fails_loudly_without_a_device():
     from jetsonfabric_b200 import engine
     with pytest.raises((engine.NativeExecutionError, engine.InvalidArgument)):
         engine.NativeEngine(REPO / "does-not-exist", "cuda")
+
+
+ENGINE_CONSUMER = r"""
+#include "jetsonfabric/native_inference.hpp"
+
+#include <cstdio>
+#include <cstring>
+#include <stdexcept>
+
+using namespace jetsonfabric::native;
+
+static const char * open_engine(const char * path, Backend backend) {
+    try {
+        NativeEngine engine(path, backend, 1);
+        return engine.model_info().architecture.empty() ? "opened-empty" : "opened";
+    } catch (const std::invalid_argument &) {
+        return "invalid_argument";
+    } catch (const std::exception &) {
+        return "exception";
+    }
+}
+
+int main(int argc, char ** argv) {
+    if (argc != 2) return 2;
+    std::printf("%s %s\n", backend_name(Backend::Cpu), backend_name(Backend::Cuda));
+    std::printf("%s %s %s\n", attention_kernel_name(AttentionKernel::Automatic),
+                attention_kernel_name(AttentionKernel::Unfused), attention_kernel_name(AttentionKernel::Flash));
+    EngineOptions options;
+    std::printf("%s %u\n", options.backend == Backend::Cpu ? "cpu-default" : "other", options.layer_start);
+    std::printf("%s\n", open_engine(argv[1], Backend::Cpu));
+    std::printf("%s\n", open_engine((std::string(argv[1]) + "/missing").c_str(), Backend::Cuda));
+    return 0;
+}
+"""
+
+
+def test_engine_cpp_api_compiles_links_and_rejects_without_a_device(tmp_path):
+    """A caller written against the reference's engine header
+    (include/jetsonfabric/native_inference.hpp) compiles, links against
+    libjfb.so and runs without a GPU: the name helpers return the reference's
+    strings, Backend::Cpu is rejected with std::invalid_argument (no CPU
+    fallback), and a missing package raises a std::exception."""
+    import shutil
+    import subprocess
+
+    torch = pytest.importorskip("torch")
+    if torch.cuda.is_available():
+        pytest.skip("a CUDA device is present")
+    if shutil.which("g++") is None:
+        pytest.skip("no C++ compiler")
+    from jetsonfabric_b200 import build_cuda
+    lib = build_cuda.build()
+    src = tmp_path / "engine_consumer.cpp"
+    src.write_text(ENGINE_CONSUMER)
+    exe = tmp_path / "engine_consumer"
+    subprocess.run(["g++", "-std=c++20", "-O1", f"-I{REPO / 'include'}", str(src), "-o", str(exe),
+                    f"-L{lib.parent}", "-ljfb", f"-Wl,-rpath,{lib.parent}"], check=True)
+    golden = REPO / "tests" / "golden" / "jfm-v2-golden"
+    package = tmp_path / "pkg"
+    package.mkdir()
+    for hexfile in golden.glob("*.hex"):
+        (package / hexfile.stem).write_bytes(bytes.fromhex("".join(hexfile.read_text().split())))
+    out = subprocess.run([str(exe), str(package)], check=True, capture_output=True, text=True).stdout.split("\n")
+    assert out[:4] == ["cpu cuda", "automatic unfused flash", "cpu-default 0", "invalid_argument"]
+    assert out[4] in ("invalid_argument", "exception")
