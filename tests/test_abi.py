@@ -116,3 +116,19 @@ def test_engine_cpp_api_compiles_links_and_rejects_without_a_device(tmp_path):
     out = subprocess.run([str(exe), str(package)], check=True, capture_output=True, text=True).stdout.split("\n")
     assert out[:4] == ["cpu cuda", "automatic unfused flash", "cpu-default 0", "invalid_argument"]
     assert out[4] in ("invalid_argument", "exception")
+
+
+@pytest.mark.parametrize("header", HEADERS, ids=lambda h: h.name)
+@pytest.mark.parametrize("compiler", [("gcc", "-std=c11", "c"), ("g++", "-std=c++20", "c++")], ids=["c11", "c++20"])
+def test_header_compiles_alone(header, compiler):
+    """Each C header is self-contained and warning-free as C (what cgo and
+    other FFI generators parse) and as C++."""
+    import shutil
+    import subprocess
+
+    cc, std, lang = compiler
+    if shutil.which(cc) is None:
+        pytest.skip(f"no {cc}")
+    rel = header.relative_to(REPO / "include")
+    subprocess.run([cc, std, "-x", lang, "-Wall", "-Wextra", "-Werror", f"-I{REPO / 'include'}", "-fsyntax-only", "-"],
+                   input=f'#include "{rel}"\n', text=True, check=True)
