@@ -132,3 +132,41 @@ def test_header_compiles_alone(header, compiler):
     rel = header.relative_to(REPO / "include")
     subprocess.run([cc, std, "-x", lang, "-Wall", "-Wextra", "-Werror", f"-I{REPO / 'include'}", "-fsyntax-only", "-"],
                    input=f'#include "{rel}"\n', text=True, check=True)
+
+
+CGO_SIDE = r"""
+#include <stdint.h>
+#include <stdlib.h>
+
+#include "jfb/jfb_engine.h"
+#include "jfb/jfb_model.h"
+
+/* what the cgo stubs of the integration guide touch, written in C */
+int open_stage(const char * pkg, uint32_t start, uint32_t end, int device, jfb_engine ** eng) {
+    jfb_engine_options opts = {0};
+    opts.backend = 1;
+    opts.layer_start = start;
+    opts.layer_end = end;
+    opts.device = (int32_t) device;
+    jfb_status st = jfb_engine_open(pkg, &opts, eng);
+    return st.code != 0 ? (int) st.message[0] : 0;
+}
+
+int import_gguf(const char * src, const char * dst) {
+    jfb_import_report rep;
+    jfb_status st = jfb_import_gguf(src, dst, &rep);
+    return st.code != JFB_STATUS_OK ? (int) st.message[0] : 0;
+}
+"""
+
+
+def test_cgo_stub_calls_compile_as_c():
+    """The fields, calls and constants the integration guide's cgo stubs use
+    exist with those types in the C headers."""
+    import shutil
+    import subprocess
+
+    if shutil.which("gcc") is None:
+        pytest.skip("no gcc")
+    subprocess.run(["gcc", "-std=c11", "-x", "c", "-Wall", "-Wextra", "-Werror", f"-I{REPO / 'include'}",
+                    "-fsyntax-only", "-"], input=CGO_SIDE, text=True, check=True)
