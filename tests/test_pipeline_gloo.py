@@ -7,7 +7,7 @@ This covers the host side of the multi-GPU path, which the benchmark drives
 with the engine over NCCL:
 - the even layer split;
 - micro-batching;
-- message order on the activation and token links (world sizes 2 and 3,
+- message order on the activation and token links (world sizes 2, 3 and 4,
   more and fewer micro-batches than stages).
 """
 from __future__ import annotations
@@ -138,7 +138,7 @@ def _chained_reference(package, prompts, world, steps):
     return out
 
 
-@pytest.mark.parametrize("world,micro", [(2, 2), (2, 3), (3, 2)])
+@pytest.mark.parametrize("world,micro", [(2, 2), (2, 3), (3, 2), (4, 4)])
 def test_pipeline_matches_chained_stages(small_q4k_package, tmp_path, world, micro):
     import torch.multiprocessing as mp
 
