@@ -1,13 +1,16 @@
 #!/usr/bin/env python
 """Aggregate decode throughput of the native Qwen2 Q4_K_M stage engine on B200.
 
-Workload (configs[1] of the benchmark definition): Qwen2-architecture 3B
-Q4_K_M (36 layers, hidden 2048, 16/2 heads, FFN 11008, vocabulary 151,936),
-seeded N(0, 0.02) weights quantized with this repository's K-quant encoders,
-32 concurrent requests of 512 uniform-random prompt tokens, 256 greedy output
-tokens each. One "step" serves the whole batch: one batched prefill of all
-prompts, then 255 batched decode steps. The weights (2.1 GB) are larger than
-L2 (126 MB), so every decode step streams them from HBM.
+Workload (configs[2] of the benchmark definition, the metric's "Qwen2 Q4_K
+pipeline at 1/2/4/8 B200"): Qwen2-architecture 7B Q4_K_M (28 layers, hidden
+3584, 28/4 heads, FFN 18944, vocabulary 152,064), seeded N(0, 0.02) weights
+quantized with this repository's K-quant encoders, 64 concurrent sequences of
+1024 uniform-random prompt tokens, 256 greedy output tokens each. One "step"
+serves the whole batch: one batched prefill of all prompts, then 255 batched
+decode steps. The weights (4.68 GB) and the KV caches (up to 4.7 GB) are far
+larger than L2 (126 MB), so every decode step streams them from HBM.
+`--preset` selects the other configurations (1.5b, 3b, 14b, 32b) with their
+own default batch shapes.
 
     value      aggregate output tok/s, device-timed (CUDA events on the
                engine stream), prompts already resident in HBM
@@ -17,8 +20,11 @@ L2 (126 MB), so every decode step streams them from HBM.
     roofline   the decode matmuls (weight-streaming K-quant x Q8_K dot
                products, the dominant kernel family) of one decode step at
                the workload's batch, bytes / CUDA-event time vs measured HBM
+    parity     a bounded sample through the same engine (sequence 0's first
+               32 prompt tokens, 8 greedy tokens) against the CPU oracle
     cpu_baseline  the CPU oracle (this repository's restatement of the
-               reference's GGML-CPU path) on a bounded sample
+               reference's GGML-CPU path) on that sample, with its prefill
+               and decode token rates
 
 --impl reference runs the CPU oracle on the host cores instead (the
 reference's own native engine needs GGML, which cannot be built here).
@@ -42,6 +48,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import threading
 import time
 from pathlib import Path
@@ -49,19 +56,40 @@ from pathlib import Path
 REPO = Path(__file__).resolve().parent
 sys.path.insert(0, str(REPO))
 
-PRESETS = {
-    "3b": dict(layer_count=36, embedding_length=2048, head_count=16, kv_head_count=2, feed_forward_length=11008,
-               vocabulary_size=151936),
-    "1.5b": dict(layer_count=28, embedding_length=1536, head_count=12, kv_head_count=2, feed_forward_length=8960,
-                 vocabulary_size=151936),
-    "7b": dict(layer_count=28, embedding_length=3584, head_count=28, kv_head_count=4, feed_forward_length=18944,
-               vocabulary_size=152064),
-}
+from jetsonfabric_b200.jfm import QWEN2_PRESETS as PRESETS  # noqa: E402
+
+# default batch shape of each preset: (concurrency, prompt tokens, output
+# tokens, session capacity or 0 for prompt + output - 1), from the benchmark
+# configurations: cfg 1 1.5B C2 p128 o128; cfg 2 3B C32 p512 o256; cfg 3 7B
+# C64 p1024 o256; cfg 4 14B 128 streams of 4096-token prompts with the KV
+# cache reserved for 8192 positions; cfg 5 32B Q2_K 256 sequences p2048 o512
+WORKLOADS = {"1.5b": (2, 128, 128, 0), "3b": (32, 512, 256, 0), "7b": (64, 1024, 256, 0),
+             "14b": (128, 4096, 256, 8192), "32b": (256, 2048, 512, 0)}
 METRIC = "aggregate decode tok/s + p50 ITL, Qwen2 Q4_K pipeline at 1/2/4/8 B200"
-# weight shapes of the 3B workload (type, rows, cols) for --matmul-shape
-MATMUL_SHAPES = {"ffn_gate": (11, 11008, 2048), "ffn_down_q6": (13, 2048, 11008), "attn_q": (11, 2048, 2048),
-                 "attn_k": (11, 256, 2048), "output_q6": (13, 151936, 2048)}
+
+
+def matmul_shapes(preset: str) -> dict:
+    """Weight shapes (type, rows, cols) of one layer and the head, for --matmul-shape."""
+    m = PRESETS[preset]
+    h, f, v = m["embedding_length"], m["feed_forward_length"], m["vocabulary_size"]
+    kvd = h // m["head_count"] * m["kv_head_count"]
+    lt = m.get("layer_type", 11)
+    return {"ffn_gate": (lt, f, h), "ffn_down_q6": (13, h, f), "attn_q": (lt, h, h), "attn_k": (lt, kvd, h),
+            "output_q6": (13, v, h)}
+
+
+MATMUL_SHAPE_NAMES = ["attn_k", "attn_q", "ffn_down_q6", "ffn_gate", "output_q6"]
 UNIT = "tok/s"
+DTYPE = "q4_k/q6_k/q2_k x q8_k int8 dot, f32 block terms, f64 sums; f16 KV with f64 attention sums"
+
+
+def workload_name(args) -> str:
+    return f"{model_label(args.preset)} c{args.concurrency} p{args.prompt_tokens} o{args.output_tokens}"
+
+
+def model_name(args) -> str:
+    kind = "Q2_K (Q6_K output)" if PRESETS[args.preset].get("layer_type") == 9 else "Q4_K_M"
+    return f"Qwen2-arch {args.preset} {kind}"
 
 
 def parse():
@@ -70,27 +98,41 @@ def parse():
     p.add_argument("--steps", type=int, default=3)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--preset", default="3b", choices=sorted(PRESETS))
-    p.add_argument("--concurrency", type=int, default=32)
-    p.add_argument("--prompt-tokens", type=int, default=512)
-    p.add_argument("--output-tokens", type=int, default=256)
+    p.add_argument("--preset", default="7b", choices=sorted(PRESETS))
+    p.add_argument("--concurrency", type=int, default=None)
+    p.add_argument("--prompt-tokens", type=int, default=None)
+    p.add_argument("--output-tokens", type=int, default=None)
+    p.add_argument("--capacity", type=int, default=None, help="KV positions reserved per session")
     p.add_argument("--seed", type=int, default=2026)
-    p.add_argument("--package-dir", default=os.environ.get("JFB_BENCH_DIR", "/tmp/jfb_bench"))
+    p.add_argument("--package-dir", default=os.environ.get("JFB_BENCH_DIR",
+                                                           os.path.join(tempfile.gettempdir(), "jfb_bench")))
+    p.add_argument("--skip-parity", action="store_true")
     p.add_argument("--skip-e2e", action="store_true")
     p.add_argument("--skip-cpu", action="store_true")
     p.add_argument("--micro-batches", type=int, default=0, help="pipeline micro-batches (default: one per stage)")
     p.add_argument("--replicas", action="store_true", help="N > 1: full-model replicas instead of a pipeline")
-    p.add_argument("--matmul-shape", choices=sorted(MATMUL_SHAPES), default=None,
+    p.add_argument("--matmul-shape", choices=MATMUL_SHAPE_NAMES, default=None,
                    help="time only the tcgen05 K-quant matmul on one weight shape of the workload (profiling target)")
     p.add_argument("--matmul-rows", type=int, default=32, help="activation rows for --matmul-shape")
     p.add_argument("--attention-shape", choices=["decode", "prefill"], default=None,
                    help="time only jfb_attention on the workload's decode (32 rows x 768 keys) or prefill "
                         "(32 x 512 causal rows) shape (profiling target)")
-    return p.parse_args()
+    a = p.parse_args()
+    c, pt, ot, cap = WORKLOADS[a.preset]
+    a.concurrency = c if a.concurrency is None else a.concurrency
+    a.prompt_tokens = pt if a.prompt_tokens is None else a.prompt_tokens
+    a.output_tokens = ot if a.output_tokens is None else a.output_tokens
+    need = a.prompt_tokens + a.output_tokens - 1
+    a.capacity = max(need, cap) if a.capacity is None else max(need, a.capacity)
+    return a
+
+
+def model_label(preset: str) -> str:
+    return f"qwen2-{preset}-" + ("q2k" if PRESETS[preset].get("layer_type") == 9 else "q4km")
 
 
 def package_path(args) -> Path:
-    return Path(args.package_dir) / f"qwen2-{args.preset}-q4km-seed{args.seed}.jfm"
+    return Path(args.package_dir) / f"{model_label(args.preset)}-seed{args.seed}.jfm"
 
 
 def ensure_package(args, rank: int) -> Path:
@@ -99,7 +141,7 @@ def ensure_package(args, rank: int) -> Path:
     done = path / ".complete"
     if rank == 0 and not done.exists():
         path.mkdir(parents=True, exist_ok=True)
-        ctx = max(4096, args.prompt_tokens + args.output_tokens)
+        ctx = max(4096, args.capacity)
         jfm.write_synthetic_package(path, **PRESETS[args.preset], context_length=ctx, seed=args.seed,
                                     draw_norms=False, draw_biases=True)
         done.write_text("ok")
@@ -187,7 +229,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     eng = E.NativeEngine(pkg, "cuda", device=local_rank)
     info = eng.model_info()
     C, P, O = args.concurrency, args.prompt_tokens, args.output_tokens
-    capacity = P + O - 1
+    capacity = args.capacity
     prompts = prompts_for(args, info.vocabulary_size)
     sessions = [eng.create_session(capacity) for _ in range(C)]
     handles = eng._handles(sessions)
@@ -287,18 +329,29 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
 
     result = None
     if rank == 0:
-        cpu = None if (args.skip_cpu or world > 1) else cpu_baseline(args, pkg)
+        cpu = parity = None
+        if not (args.skip_cpu and args.skip_parity):
+            prompt = sample_prompt(args, info.vocabulary_size)
+            gpu_tokens = gpu_sample_tokens(eng, prompt)
+            threads = os.cpu_count() or 1
+            runner = OracleRunner(pkg, threads)
+            res = runner.sample(prompt)
+            runner.close()
+            parity = None if args.skip_parity else parity_line(gpu_tokens, res["tokens"])
+            cpu = None if (args.skip_cpu or world > 1) else cpu_line(args, res, threads)
         result = {
             "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_per_step, 3), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "q4_k/q6_k x q8_k int8 dot, f32 accumulate",
+            "scaling": "weak" if world > 1 else "strong", "vs_baseline": None, "dtype": DTYPE,
             "data": "synthetic (seeded N(0,0.02) weights, uniform-random prompt ids)",
-            "config": {"workload": f"qwen2-{args.preset}-q4km c{C} p{P} o{O}", "model": f"Qwen2-arch {args.preset} Q4_K_M",
+            "config": {"workload": workload_name(args), "model": model_name(args),
                        "layers": info.layer_count, "hidden": info.embedding_length, "concurrency": C,
-                       "prompt_tokens": P, "output_tokens": O, "weight_bytes": info.weight_bytes,
+                       "prompt_tokens": P, "output_tokens": O, "session_capacity": capacity,
+                       "weight_bytes": info.weight_bytes,
                        "global_batch": C * world, "seq_len": P + O,
                        "parallelism": "replicas" if world > 1 else "single stage",
-                       "l2": "weights (2.1 GB) exceed L2 every decode step"},
+                       "l2": f"weights ({info.weight_bytes / 1e9:.2f} GB) exceed L2 (126 MB) every decode step"},
+            "parity": parity,
             "ttft_p50_ms": round(statistics.median(prefills), 3),
             "itl_p50_ms": round(statistics.median(gaps), 4),
             "decode_tok_s": round(C * world / (statistics.mean(gaps) / 1000.0), 1),
@@ -312,6 +365,11 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         dist.barrier()
         dist.destroy_process_group()
     return result
+
+
+def progress(rank: int, phase: str) -> None:
+    """One line per phase on stderr, so that a stalled run shows where it stopped."""
+    print(f"[bench rank {rank}] {phase} {time.strftime('%H:%M:%S')}", file=sys.stderr, flush=True)
 
 
 def run_pipeline(args, rank: int, world: int, local_rank: int) -> dict | None:
@@ -339,7 +397,7 @@ def run_pipeline(args, rank: int, world: int, local_rank: int) -> dict | None:
     micro = args.micro_batches or world
     batches = PL.split_batches(C, micro)
     prompts = prompts_for(args, preset["vocabulary_size"]).tolist()
-    stage = PL.EngineStage(eng, prompts, batches, capacity=P + O - 1)
+    stage = PL.EngineStage(eng, prompts, batches, capacity=args.capacity)
     last = rank == world - 1
     launches = {"n": 0}
 
@@ -381,8 +439,10 @@ def run_pipeline(args, rank: int, world: int, local_rank: int) -> dict | None:
                     gaps.append(marks[(t - 1, m)].elapsed_time(marks[(t, m)]))
         return total, ttft, gaps
 
+    progress(rank, "warm-up")
     for _ in range(max(args.warmup, 0)):
         one_run()
+    progress(rank, "timed")
     totals, ttfts, gaps = [], [], []
     launches["n"] = 0
     with ClockSampler(local_rank) as clocks:
@@ -405,6 +465,7 @@ def run_pipeline(args, rank: int, world: int, local_rank: int) -> dict | None:
     value = C * O / (ms_per_step / 1000.0)
 
     # roofline of the first stage's decode matmuls: one timed decode pass of micro-batch 0
+    progress(rank, "roofline pass")
     timing: dict = {}
     if rank == 0:
         stage.reset()
@@ -423,10 +484,11 @@ def run_pipeline(args, rank: int, world: int, local_rank: int) -> dict | None:
     # end to end: host-buffer C ABI, host activations over gloo
     e2e = None
     if not args.skip_e2e:
-        hgroups = PL.make_groups(world, backend="gloo")
+        progress(rank, "e2e (host buffers over gloo)")
+        hgroups = PL.make_groups(world, backend="gloo", timeout_s=300)
         PL.warm_groups(rank, world, hgroups)
         hlink = PL.TorchLink(rank, world, hgroups)
-        hstage = PL.HostEngineStage(eng, prompts, batches, capacity=P + O - 1)
+        hstage = PL.HostEngineStage(eng, prompts, batches, capacity=args.capacity)
         times = []
         for _ in range(max(1, args.steps)):
             hstage.reset()
@@ -444,6 +506,37 @@ def run_pipeline(args, rank: int, world: int, local_rank: int) -> dict | None:
                "h2d_bytes_per_step": C * P * 4 + (O - 1) * C * 4 + hop_bytes,
                "d2h_bytes_per_step": O * C * 4 + hop_bytes}
 
+    # parity: the bounded sample through the same pipeline (one micro-batch of
+    # one sequence); the first stage receives every greedy token from the last
+    parity = None
+    if not args.skip_parity:
+        progress(rank, "parity sample")
+        prompt = sample_prompt(args, preset["vocabulary_size"])
+        n_out = CPU_SAMPLE["output_tokens"]
+        pstage = PL.EngineStage(eng, [prompt], [[0]], capacity=len(prompt) + n_out + 1)
+        received = []
+        if rank == 0:
+            plain = pstage.forward
+
+            def recording(m, prefill, inputs):
+                if not prefill:
+                    received.append(inputs)
+                return plain(m, prefill, inputs)
+
+            pstage.forward = recording
+        with torch.cuda.stream(pstage.stream):
+            PL.run_schedule(rank, world, [[0]], [len(prompt)], n_out + 1, pstage, link)
+        torch.cuda.synchronize()
+        pstage.close()
+        if rank == 0:
+            gpu_tokens = [int(t.cpu().item()) for t in received]
+            runner = OracleRunner(pkg, os.cpu_count() or 1)
+            res = runner.sample(prompt)
+            runner.close()
+            parity = parity_line(gpu_tokens, res["tokens"])
+            parity["path"] = f"pp{world} pipeline, NCCL boundary"
+        dist.barrier()
+
     result = None
     if rank == 0:
         peaks = measured_peaks()
@@ -458,15 +551,16 @@ def run_pipeline(args, rank: int, world: int, local_rank: int) -> dict | None:
         result = {
             "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_per_step, 3), "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "q4_k/q6_k x q8_k int8 dot, f32 accumulate",
+            "scaling": "strong", "vs_baseline": None, "dtype": DTYPE,
             "data": "synthetic (seeded N(0,0.02) weights, uniform-random prompt ids)",
-            "config": {"workload": f"qwen2-{args.preset}-q4km c{C} p{P} o{O}", "model": f"Qwen2-arch {args.preset} Q4_K_M",
+            "config": {"workload": workload_name(args), "model": model_name(args),
                        "concurrency": C, "prompt_tokens": P, "output_tokens": O, "global_batch": C, "seq_len": P + O,
                        "parallelism": f"pp{world}", "stages": ranges, "micro_batches": [len(b) for b in batches],
                        "boundary": "F16 codec over NCCL send/recv (NVLink)",
                        "l2": "weights exceed L2 every decode step"},
             "ttft_p50_ms": round(float(lat[0].item()), 3), "itl_p50_ms": round(float(lat[1].item()), 4),
             "decode_tok_s": round(C / (float(lat[2].item()) / 1000.0), 1),
+            "parity": parity,
             "e2e": e2e, "roofline": roof, "cpu_baseline": None, "clocks": clocks.summary(),
             "gpu_launches": int(float(launch_total.item()) / max(1, args.steps) * args.steps),
         }
@@ -486,7 +580,7 @@ def run_matmul_shape(args) -> dict:
     from jetsonfabric_b200 import jfm
     from jetsonfabric_b200 import kernels as K
 
-    t, rows, cols = MATMUL_SHAPES[args.matmul_shape]
+    t, rows, cols = matmul_shapes(args.preset)[args.matmul_shape]
     n = args.matmul_rows
     raw = jfm.quantize_blocks(t, np.random.default_rng(args.seed).normal(0, 0.02, rows * cols).astype(np.float32))
     copies = max(1, int(np.ceil(256e6 / len(raw))))
@@ -512,15 +606,19 @@ def run_matmul_shape(args) -> dict:
 
 
 def run_attention_shape(args) -> dict:
-    """jfb_attention alone on the 3B workload's attention shape: random F16
-    KV caches for 32 sequences, 16 query heads over 2 KV heads (head_dim 128),
-    Q8_K output fused; `warmup` untimed then `steps` timed launches (CUDA
-    events on the launching stream)."""
+    """jfb_attention alone on the preset's attention shape: random F16 KV
+    caches for `concurrency` sequences with the preset's heads (head_dim
+    128), Q8_K output fused. decode: one row per sequence at position
+    prompt + output/2; prefill: every causal row of the prompt. `warmup`
+    untimed then `steps` timed launches (CUDA events on the launching
+    stream)."""
     import torch
     from jetsonfabric_b200 import kernels as K
 
-    heads, kvh, hd, n_seq = 16, 2, 128, args.concurrency
-    ctx = 768 if args.attention_shape == "decode" else 512
+    m = PRESETS[args.preset]
+    heads, kvh, n_seq = m["head_count"], m["kv_head_count"], args.concurrency
+    hd = m["embedding_length"] // heads
+    ctx = args.prompt_tokens + args.output_tokens // 2 if args.attention_shape == "decode" else args.prompt_tokens
     rows_per_seq = 1 if args.attention_shape == "decode" else ctx
     kvd = kvh * hd
     gen = torch.Generator(device="cuda").manual_seed(args.seed)
@@ -569,40 +667,68 @@ def traffic_from_profiles():
 # CPU oracle (reference arm and cpu_baseline)
 # ---------------------------------------------------------------------------------
 
-CPU_SAMPLE = {"sequences": 2, "prompt_tokens": 16, "output_tokens": 4}
+CPU_SAMPLE = {"sequences": 1, "prompt_tokens": 32, "output_tokens": 8}
 
 
-def oracle_sample(pkg: Path, args, threads: int) -> tuple[float, float, list[float], float]:
-    """Serves CPU_SAMPLE with the oracle; returns (seconds, ttft_ms, itl_ms list, tokens)."""
-    import numpy as np
-    from oracle import binding as ob
-    ob.set_threads(threads)
-    stage = ob.OracleStage(pkg)
-    rng = np.random.default_rng(args.seed)
-    n, P, O = CPU_SAMPLE["sequences"], CPU_SAMPLE["prompt_tokens"], CPU_SAMPLE["output_tokens"]
-    t0 = time.perf_counter()
-    ttft, gaps = [], []
-    for _ in range(n):
-        prompt = rng.integers(0, stage.vocab, P).tolist()
-        s = stage.session(P + O)
-        a = time.perf_counter()
-        tok = s.forward(True, tokens=prompt)["token"]
-        ttft.append((time.perf_counter() - a) * 1000)
+def sample_prompt(args, vocab: int) -> list[int]:
+    """The bounded sample: the first CPU_SAMPLE prompt tokens of sequence 0."""
+    return prompts_for(args, vocab)[0, :CPU_SAMPLE["prompt_tokens"]].tolist()
+
+
+class OracleRunner:
+    """The CPU oracle over the whole model, loaded once, serving CPU_SAMPLE."""
+
+    def __init__(self, pkg: Path, threads: int):
+        from oracle import binding as ob
+        ob.set_threads(threads)
+        self.threads = threads
+        self.stage = ob.OracleStage(pkg)
+
+    def sample(self, prompt: list[int]) -> dict:
+        O = CPU_SAMPLE["output_tokens"]
+        s = self.stage.session(len(prompt) + O)
+        t0 = time.perf_counter()
+        tokens = [s.forward(True, tokens=prompt)["token"]]
+        t1 = time.perf_counter()
+        gaps = []
         for _ in range(O - 1):
             b = time.perf_counter()
-            tok = s.forward(False, tokens=[tok])["token"]
-            gaps.append((time.perf_counter() - b) * 1000)
-    seconds = time.perf_counter() - t0
-    stage.close()
-    return seconds, statistics.median(ttft), gaps, float(n * O)
+            tokens.append(s.forward(False, tokens=[tokens[-1]])["token"])
+            gaps.append(time.perf_counter() - b)
+        seconds = time.perf_counter() - t0
+        del s
+        return {"seconds": seconds, "prefill_s": t1 - t0, "gaps_s": gaps, "tokens": tokens}
+
+    def close(self):
+        self.stage.close()
 
 
-def cpu_baseline(args, pkg: Path) -> dict:
-    threads = os.cpu_count() or 1
-    seconds, _, _, tokens = oracle_sample(pkg, args, threads)
-    return {"value": round(tokens / seconds, 3), "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": f"{CPU_SAMPLE['sequences']} sequences x {CPU_SAMPLE['prompt_tokens']} prompt tokens x "
-                      f"{CPU_SAMPLE['output_tokens']} output tokens of the {args.preset} workload (oracle, OpenMP)"}
+def cpu_line(args, res: dict, threads: int) -> dict:
+    O, P = CPU_SAMPLE["output_tokens"], CPU_SAMPLE["prompt_tokens"]
+    return {"value": round(O / res["seconds"], 4), "unit": UNIT, "cores": threads, "kind": "port",
+            "prefill_tok_s": round(P / res["prefill_s"], 2),
+            "decode_tok_s": round(1.0 / statistics.mean(res["gaps_s"]), 3) if res["gaps_s"] else None,
+            "sample": f"sequence 0 of the {model_label(args.preset)} workload: its first {P} prompt tokens, "
+                      f"{O} greedy output tokens, one sequence (CPU oracle, OpenMP over {threads} threads); "
+                      "value = output tokens / wall time of the sample"}
+
+
+def parity_line(gpu_tokens: list[int], cpu_tokens: list[int]) -> dict:
+    return {"status": "ok" if gpu_tokens == cpu_tokens else "fail", "gpu_tokens": gpu_tokens,
+            "oracle_tokens": cpu_tokens,
+            "sample": f"sequence 0's first {CPU_SAMPLE['prompt_tokens']} prompt tokens, "
+                      f"{CPU_SAMPLE['output_tokens']} greedy tokens through the benched engine vs the CPU oracle"}
+
+
+def gpu_sample_tokens(eng, prompt: list[int]) -> list[int]:
+    """CPU_SAMPLE through the benched single-stage engine (a fresh session)."""
+    O = CPU_SAMPLE["output_tokens"]
+    s = eng.create_session(len(prompt) + O)
+    tokens = [s.prefill_greedy(prompt)]
+    for _ in range(O - 1):
+        tokens.append(s.decode_greedy(tokens[-1]))
+    s.close()
+    return tokens
 
 
 def run_reference(args, rank: int) -> dict | None:
@@ -610,29 +736,30 @@ def run_reference(args, rank: int) -> dict | None:
         return None
     pkg = ensure_package(args, 0)
     threads = os.cpu_count() or 1
+    runner = OracleRunner(pkg, threads)
+    prompt = sample_prompt(args, PRESETS[args.preset]["vocabulary_size"])
     for _ in range(max(args.warmup, 0)):
-        oracle_sample(pkg, args, threads)
-    times, ttfts, gaps, toks = [], [], [], 0.0
-    for _ in range(args.steps):
-        s, t, g, n = oracle_sample(pkg, args, threads)
-        times.append(s)
-        ttfts.append(t)
-        gaps.extend(g)
-        toks = n
-    seconds = statistics.mean(times)
-    value = toks / seconds
+        runner.sample(prompt)
+    results = [runner.sample(prompt) for _ in range(args.steps)]
+    runner.close()
+    seconds = statistics.mean(r["seconds"] for r in results)
+    value = CPU_SAMPLE["output_tokens"] / seconds
+    merged = {"seconds": seconds, "prefill_s": statistics.mean(r["prefill_s"] for r in results),
+              "gaps_s": [g for r in results for g in r["gaps_s"]]}
+    cpu = cpu_line(args, merged, threads)
+    cpu["value"] = round(value, 4)
     return {
-        "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(seconds * 1000, 1), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "q4_k/q6_k x q8_k int8 dot, f32 accumulate", "impl": "reference",
+        "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(seconds * 1000, 1), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": DTYPE, "impl": "reference",
         "data": "synthetic (seeded N(0,0.02) weights, uniform-random prompt ids)",
-        "config": {"workload": f"qwen2-{args.preset}-q4km c{args.concurrency} p{args.prompt_tokens} o{args.output_tokens}",
-                   "model": f"Qwen2-arch {args.preset} Q4_K_M", "sample": CPU_SAMPLE},
-        "ttft_p50_ms": round(statistics.median(ttfts), 1), "itl_p50_ms": round(statistics.median(gaps), 1),
-        "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": threads, "kind": "port",
-                         "sample": f"{CPU_SAMPLE} per step; the reference's GGML CPU backend cannot be built "
-                                   "offline, so its C restatement (oracle/) runs"},
-        "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "config": {"workload": workload_name(args), "model": model_name(args), "sample": CPU_SAMPLE,
+                   "note": "each step serves the bounded sample; the reference's GGML CPU backend cannot be built "
+                           "offline, so its C restatement (oracle/) runs on the host cores"},
+        "ttft_p50_ms": round(statistics.median(r["prefill_s"] for r in results) * 1000, 1),
+        "itl_p50_ms": round(statistics.median(merged["gaps_s"]) * 1000, 1) if merged["gaps_s"] else None,
+        "cpu_baseline": cpu,
+        "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
 
 

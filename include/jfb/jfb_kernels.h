@@ -201,9 +201,18 @@ jfb_status jfb_rope_kv_append(float * q, const float * k, const float * v, uint3
  * (cosf/sinf of pos * theta_scale^i, angles by repeated multiplication). */
 void jfb_rope_table_host(float * table, uint32_t positions, uint32_t rope_dims, float freq_base);
 
-/* Scratch bytes jfb_attention needs for n query rows with at most max_keys
- * keys each. */
+/* Scratch bytes jfb_attention's four-launch form needs for n query rows with
+ * at most max_keys keys each (UINT64_MAX beyond 65535 * 64 keys, which no
+ * call supports). */
 uint64_t jfb_attention_scratch_bytes(uint32_t n, uint32_t heads, uint32_t head_dim, uint32_t max_keys);
+
+/* Scratch bytes one jfb_attention call with these dimensions needs on the
+ * current device: 0 when the call runs as the single launch (no scratch
+ * read or written; scratch may then be NULL), else
+ * jfb_attention_scratch_bytes. Lets a caller size its scratch per call
+ * instead of for the worst case. */
+uint64_t jfb_attention_call_scratch_bytes(uint32_t n, uint32_t heads, uint32_t kv_heads, uint32_t head_dim,
+                                          uint32_t max_keys);
 
 /* Causal GQA attention of query rows over the F16 caches
  * (qwen2_architecture.cpp:425-470, GGML-CPU semantics of the unfused path):
@@ -212,9 +221,11 @@ uint64_t jfb_attention_scratch_bytes(uint32_t n, uint32_t heads, uint32_t head_d
  * f16 products summed in double and rounded to f32 once; x = score *
  * 1/sqrt(head_dim); softmax with exp(x - max) summed in double over all keys,
  * p = e * (float)(1/sum) rounded to f16; output = exact p*v products summed
- * in double, rounded once. Four launches: scores (+chunk maxima), row
- * statistics, P V partials, combine (+Q8_K quantization of the result when
- * out_q8 != NULL). */
+ * in double, rounded once. One launch on the FP64 tensor cores where the
+ * shape allows (no scratch used), else four launches: scores (+chunk maxima),
+ * row statistics, P V partials, combine (+Q8_K quantization of the result
+ * when out_q8 != NULL). max_keys above 65535 * 64 is rejected; a row whose
+ * pos[r] + 1 exceeds max_keys is clamped to the keys the call was sized for. */
 jfb_status jfb_attention(const float * q, uint32_t n, const int32_t * seq, const int32_t * pos, uint32_t heads,
                          uint32_t kv_heads, uint32_t head_dim, uint32_t max_keys, const jfb_kv_slot * slots,
                          uint32_t layer, void * scratch, uint64_t scratch_bytes, float * out,

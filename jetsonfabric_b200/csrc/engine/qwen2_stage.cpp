@@ -461,6 +461,7 @@ void Qwen2Stage::check_device_errors() {
 
 Qwen2Stage::~Qwen2Stage() {
     free_scratch();
+    if (attn_scratch_ != nullptr) cudaFree(attn_scratch_);
     if (meta_uploaded_ != nullptr) cudaEventDestroy(meta_uploaded_);
     for (const TimedLaunch & t : timed_) {
         cudaEventDestroy(t.start);
@@ -508,7 +509,7 @@ void Qwen2Stage::free_scratch() {
                      static_cast<void *>(k_), static_cast<void *>(v_), static_cast<void *>(attn_),
                      static_cast<void *>(gate_), static_cast<void *>(up_), static_cast<void *>(q8_.qs),
                      static_cast<void *>(q8_.d), static_cast<void *>(q8_.bsums), static_cast<void *>(q8_.qs_f16),
-                     static_cast<void *>(q8_.bsums_f16), static_cast<void *>(q8_.d_t), attn_scratch_,
+                     static_cast<void *>(q8_.bsums_f16), static_cast<void *>(q8_.d_t),
                      static_cast<void *>(logits_), static_cast<void *>(tokens_dev_),
                      static_cast<void *>(error_flag_), meta_dev_, tc_workspace_}) {
         if (p != nullptr) cudaFree(p);
@@ -516,19 +517,38 @@ void Qwen2Stage::free_scratch() {
     if (meta_host_ != nullptr) cudaFreeHost(meta_host_);
     hidden_ = xf_ = q_ = k_ = v_ = attn_ = gate_ = up_ = logits_ = nullptr;
     q8_ = jfb_q8k{};
-    attn_scratch_ = meta_dev_ = meta_host_ = nullptr;
+    meta_dev_ = meta_host_ = nullptr;
     tokens_dev_ = error_flag_ = nullptr;
     tc_workspace_ = nullptr;
     tc_workspace_bytes_ = 0;
-    cap_rows_ = cap_seqs_ = cap_keys_ = 0;
+    cap_rows_ = cap_seqs_ = 0;
     scratch_bytes_ = 0;
 }
 
-void Qwen2Stage::ensure_scratch(std::uint32_t rows, std::uint32_t seqs, std::uint32_t max_keys) {
-    if (rows <= cap_rows_ && seqs <= cap_seqs_ && max_keys <= cap_keys_) return;
+void Qwen2Stage::ensure_attention_scratch(std::uint64_t bytes) {
+    if (bytes <= attn_scratch_bytes_) return;
+    // rare: only calls beyond the single-launch attention's limits get here
+    cuda_check(cudaStreamSynchronize(m_.stream()), "synchronise before attention scratch growth");
+    if (attn_scratch_ != nullptr) cudaFree(attn_scratch_);
+    attn_scratch_ = nullptr;
+    attn_scratch_bytes_ = 0;
+    cuda_check(cudaMalloc(&attn_scratch_, bytes), "allocate native attention scratch");
+    attn_scratch_bytes_ = bytes;
+}
+
+void Qwen2Stage::ensure_scratch(std::uint32_t rows, std::uint32_t seqs) {
+    // Sizes depend only on the rows and sequences of a call, never on the
+    // positions, so a decode loop reaches a steady state after its first
+    // call: nothing is freed or allocated (no device-wide synchronisation)
+    // while this stage's sends to a neighbour stage may be in flight.
+    if (rows <= cap_rows_ && seqs <= cap_seqs_) return;
     cuda_check(cudaStreamSynchronize(m_.stream()), "synchronise before scratch growth");
-    const std::uint32_t R = std::max(rows, cap_rows_), S = std::max(seqs, cap_seqs_);
-    const std::uint32_t K = std::max(max_keys, cap_keys_);
+    // grow by at least half again, so that slowly growing batches
+    // reallocate a logarithmic number of times
+    auto grow = [](std::uint32_t need, std::uint32_t have) {
+        return need <= have ? have : std::max(need, have + have / 2);
+    };
+    const std::uint32_t R = grow(rows, cap_rows_), S = grow(seqs, cap_seqs_);
     free_scratch();
     const Qwen2HParams & hp = m_.hparams();
     const std::uint64_t h = hp.info.embedding_length, kvd = hp.kv_dim(), f = hp.feed_forward_length;
@@ -556,8 +576,6 @@ void Qwen2Stage::ensure_scratch(std::uint32_t rows, std::uint32_t seqs, std::uin
     alloc(&q8_.qs_f16, std::uint64_t(R) * wide * 2);
     alloc(&q8_.bsums_f16, std::uint64_t(R) * (wide / 16 + 1) * 2);
     alloc(&q8_.d_t, std::uint64_t(q8_.d_stride) * (wide / 256 + 1) * 4);
-    attn_scratch_bytes_ = jfb_attention_scratch_bytes(R, hp.head_count, hp.head_dim(), K);
-    alloc(&attn_scratch_, attn_scratch_bytes_);
     if (m_.last_stage()) alloc(&logits_, std::uint64_t(S) * m_.vocabulary() * 4);
     alloc(&tokens_dev_, std::uint64_t(S) * 4);
     alloc(&error_flag_, 4);
@@ -593,7 +611,6 @@ void Qwen2Stage::ensure_scratch(std::uint32_t rows, std::uint32_t seqs, std::uin
     }
     cap_rows_ = R;
     cap_seqs_ = S;
-    cap_keys_ = K;
     scratch_bytes_ = total;
 }
 
@@ -609,7 +626,18 @@ void Qwen2Stage::forward(std::span<const SequenceRows> seqs, const ForwardIo & i
         max_keys = std::max(max_keys, s.start + s.rows);
     }
     if (S == 0 || R == 0) return;
-    ensure_scratch(R, S, max_keys);
+    ensure_scratch(R, S);
+    if (jfb_attention_call_scratch_bytes(R, hp.head_count, hp.kv_head_count, hp.head_dim(), max_keys) > 0) {
+        // beyond the single-launch attention's limits: scratch for the next
+        // multiple of 1024 keys (within the sessions' capacity), so that a
+        // decode loop grows it once per 1024 positions at most
+        std::uint32_t cap = max_keys;
+        for (const SequenceRows & s : seqs) cap = std::max(cap, s.cache->capacity());
+        const std::uint32_t keys = std::min(cap, (max_keys + 1023u) / 1024u * 1024u);
+        const std::uint64_t bytes = jfb_attention_scratch_bytes(R, hp.head_count, hp.head_dim(), keys);
+        if (bytes == UINT64_MAX) throw std::invalid_argument("native Qwen2 attention span is too long");
+        ensure_attention_scratch(bytes);
+    }
     cudaStream_t st = m_.stream();
     // the previous call's metadata upload may still be queued: wait until the
     // GPU has consumed the pinned staging buffer before rewriting it

@@ -172,7 +172,8 @@ public:
     KernelTiming collect_timing();
 
 private:
-    void ensure_scratch(std::uint32_t rows, std::uint32_t seqs, std::uint32_t max_keys);
+    void ensure_scratch(std::uint32_t rows, std::uint32_t seqs);
+    void ensure_attention_scratch(std::uint64_t bytes);
     void free_scratch();
 
     DeviceModel & m_;
@@ -203,7 +204,7 @@ private:
     void * meta_host_ = nullptr;
     std::uint64_t meta_bytes_ = 0;
     cudaEvent_t meta_uploaded_ = nullptr;  // the pinned staging buffer is free again
-    std::uint32_t cap_rows_ = 0, cap_seqs_ = 0, cap_keys_ = 0;
+    std::uint32_t cap_rows_ = 0, cap_seqs_ = 0;
     std::uint64_t scratch_bytes_ = 0;
     std::uint64_t launches_ = 0;
     // kernel timing

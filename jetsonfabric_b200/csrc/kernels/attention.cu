@@ -35,6 +35,7 @@ constexpr int kThreads = 128;
 constexpr int kChunk = 64;      // keys per CTA
 constexpr int kMaxGroup = 16;   // query heads per kv head
 constexpr int kMaxHeadDim = 256;
+constexpr uint32_t kMaxSplits = 65535;  // grid z of the four-launch form
 
 struct Scratch {
     float * scores;      // [n][heads][keys_cap]
@@ -65,6 +66,15 @@ uint64_t scratch_size(uint32_t n, uint32_t heads, uint32_t head_dim, uint32_t sp
            align_up(uint64_t(n) * heads * sizeof(float2)) + uint64_t(n) * heads * splits * head_dim * sizeof(double);
 }
 
+// Keys of row r: positions 0..pos[r], clamped to the splits * kChunk keys the
+// scratch was carved for, so a position beyond the call's max_keys (a broken
+// caller contract) reads and writes nothing outside this call's scratch.
+__device__ __forceinline__ uint32_t split_row_keys(int32_t p, uint32_t splits) {
+    const uint64_t keys = uint64_t(uint32_t(p)) + 1u;
+    const uint64_t cap = uint64_t(splits) * kChunk;
+    return uint32_t(keys < cap ? keys : cap);
+}
+
 // Launch 1: x_j = f32(sum_d k_jd * f16(q_d)) * scale for the chunk's keys.
 __global__ void __launch_bounds__(kThreads) scores_kernel(const float * __restrict__ q, const int32_t * __restrict__ seq,
                                                         const int32_t * __restrict__ pos, uint32_t heads, uint32_t kv_heads,
@@ -75,7 +85,7 @@ __global__ void __launch_bounds__(kThreads) scores_kernel(const float * __restri
     pdl_trigger();
     pdl_wait();
     const uint32_t r = blockIdx.x, kvh = blockIdx.y, split = blockIdx.z;
-    const uint32_t keys = uint32_t(pos[r]) + 1u;
+    const uint32_t keys = split_row_keys(pos[r], splits);
     const uint32_t j0 = split * kChunk;
     if (j0 >= keys) return;
     const uint32_t j1 = min(keys, j0 + kChunk);
@@ -167,7 +177,7 @@ __global__ void __launch_bounds__(kThreads) stats_kernel(const int32_t * __restr
     pdl_trigger();
     pdl_wait();
     const uint32_t r = blockIdx.x, h = blockIdx.y;
-    const uint32_t keys = uint32_t(pos[r]) + 1u;
+    const uint32_t keys = split_row_keys(pos[r], splits);
     const uint32_t used = (keys + kChunk - 1) / kChunk;
     const uint64_t rh = uint64_t(r) * heads + h;
     float mx = -INFINITY;
@@ -194,7 +204,7 @@ __global__ void __launch_bounds__(kThreads) pv_kernel(const int32_t * __restrict
     pdl_trigger();
     pdl_wait();
     const uint32_t r = blockIdx.x, kvh = blockIdx.y, split = blockIdx.z;
-    const uint32_t keys = uint32_t(pos[r]) + 1u;
+    const uint32_t keys = split_row_keys(pos[r], splits);
     const uint32_t j0 = split * kChunk;
     if (j0 >= keys) return;
     const uint32_t j1 = min(keys, j0 + kChunk);
@@ -244,7 +254,7 @@ __global__ void __launch_bounds__(256) combine_kernel(const int32_t * __restrict
     pdl_wait();
     const uint32_t r = blockIdx.x;
     const uint32_t D = head_dim, width = heads * D;
-    const uint32_t used = (uint32_t(pos[r]) + kChunk) / kChunk;
+    const uint32_t used = (split_row_keys(pos[r], splits) + kChunk - 1) / kChunk;
     for (uint32_t i = threadIdx.x; i < width; i += blockDim.x) {
         const uint32_t h = i / D, d = i % D;
         const double * base = sc.partial + ((uint64_t(r) * heads + h) * splits) * D + d;
@@ -754,15 +764,24 @@ int device_sms() {
 using namespace jfb;
 
 extern "C" uint64_t jfb_attention_scratch_bytes(uint32_t n, uint32_t heads, uint32_t head_dim, uint32_t max_keys) {
-    const uint32_t splits = (max_keys + kChunk - 1) / kChunk;
-    return scratch_size(n, heads, head_dim, splits);
+    const uint64_t splits = (uint64_t(max_keys) + kChunk - 1) / kChunk;
+    if (splits > kMaxSplits) return UINT64_MAX;  // beyond any supported call
+    return scratch_size(n, heads, head_dim, uint32_t(splits));
+}
+
+extern "C" uint64_t jfb_attention_call_scratch_bytes(uint32_t n, uint32_t heads, uint32_t kv_heads, uint32_t head_dim,
+                                                     uint32_t max_keys) {
+    if (n == 0 || kv_heads == 0 || heads % kv_heads != 0 || max_keys == 0) return 0;
+    if (uint64_t(max_keys) > uint64_t(kMaxSplits) * kChunk) return UINT64_MAX;
+    if (dmma_plan(n, heads, kv_heads, head_dim, max_keys, device_sms()).ok) return 0;
+    return jfb_attention_scratch_bytes(n, heads, head_dim, max_keys);
 }
 
 extern "C" jfb_status jfb_attention(const float * q, uint32_t n, const int32_t * seq, const int32_t * pos,
                                     uint32_t heads, uint32_t kv_heads, uint32_t head_dim, uint32_t max_keys,
                                     const jfb_kv_slot * slots, uint32_t layer, void * scratch, uint64_t scratch_bytes,
                                     float * out, const jfb_q8k * out_q8, void * stream) {
-    if (q == nullptr || seq == nullptr || pos == nullptr || slots == nullptr || out == nullptr || scratch == nullptr) {
+    if (q == nullptr || seq == nullptr || pos == nullptr || slots == nullptr || out == nullptr) {
         return status_error(JFB_STATUS_INVALID_ARGUMENT, "attention operands are required");
     }
     if (heads == 0 || kv_heads == 0 || heads % kv_heads != 0 || heads / kv_heads > uint32_t(kMaxGroup) ||
@@ -776,16 +795,18 @@ extern "C" jfb_status jfb_attention(const float * q, uint32_t n, const int32_t *
         const jfb_status tc = check_q8_tensor_core(out_q8, n);
         if (tc.code != JFB_STATUS_OK) return tc;
     }
-    if (scratch_bytes < jfb_attention_scratch_bytes(n, heads, head_dim, max_keys)) {
-        return status_error(JFB_STATUS_INVALID_ARGUMENT, "attention scratch is too small");
+    // every ceil-division below stays far from the uint32 range
+    if (uint64_t(max_keys) > uint64_t(kMaxSplits) * kChunk || kv_heads > 65535u || heads > 65535u) {
+        return status_error(JFB_STATUS_INVALID_ARGUMENT, "attention grid too large");
     }
     if (n == 0) return status_ok();
     const uint32_t splits = (max_keys + kChunk - 1) / kChunk;
-    if (splits > 65535u || kv_heads > 65535u || heads > 65535u) {
-        return status_error(JFB_STATUS_INVALID_ARGUMENT, "attention grid too large");
-    }
     cudaStream_t s = as_stream(stream);
     const DmmaPlan plan = dmma_plan(n, heads, kv_heads, head_dim, max_keys, device_sms());
+    // only the four-launch form below uses the scratch
+    if (!plan.ok && (scratch == nullptr || scratch_bytes < jfb_attention_scratch_bytes(n, heads, head_dim, max_keys))) {
+        return status_error(JFB_STATUS_INVALID_ARGUMENT, "attention scratch is too small");
+    }
     if (plan.ok) {
         const bool fused_q8 = out_q8 != nullptr && ((heads / kv_heads) * head_dim) % kQK == 0;
         const jfb_q8k q8_fused = fused_q8 ? *out_q8 : jfb_q8k{};
@@ -859,6 +880,9 @@ extern "C" jfb_status jfb_attention_static_scratch(const float * q, uint32_t n, 
                                                    float * out, const jfb_q8k * out_q8, void * stream) {
     if (heads == 0 || head_dim == 0 || max_keys == 0) {
         return status_error(JFB_STATUS_INVALID_ARGUMENT, "attention dimensions are unsupported");
+    }
+    if (uint64_t(max_keys) > uint64_t(kMaxSplits) * kChunk) {
+        return status_error(JFB_STATUS_INVALID_ARGUMENT, "attention grid too large");
     }
     const uint64_t needed = jfb_attention_scratch_bytes(n, heads, head_dim, max_keys);
     if (needed > JFB_ATTENTION_STATIC_SCRATCH_BYTES) {

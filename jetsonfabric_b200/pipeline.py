@@ -104,8 +104,10 @@ class TorchLink:
     one for the token link (last, first); every rank must create all of them
     in the same order (see `make_groups`). Works for NCCL with CUDA tensors
     (operations ordered against the current CUDA stream) and for gloo with
-    CPU tensors. Sends are asynchronous; their handles are kept until
-    `flush` so the sent buffers stay alive."""
+    CPU tensors. Sends are asynchronous; each handle (and its buffer) is
+    kept until the send has completed, and dropped at the next send after
+    that, so a long schedule holds only the sends still in flight; `flush`
+    waits for the rest."""
 
     def __init__(self, rank: int, world: int, groups: dict):
         import torch.distributed as dist
@@ -117,13 +119,19 @@ class TorchLink:
         self.tok_group = groups.get("tok")
         self.pending = []
 
+    def _drop_completed(self) -> None:
+        # never blocks: a send that has not completed stays pending
+        self.pending = [(w, buf) for w, buf in self.pending if not w.is_completed()]
+
     def send_next(self, payload) -> None:
+        self._drop_completed()
         self.pending.append((self.dist.isend(payload, self.rank + 1, group=self.next_group), payload))
 
     def recv_prev(self, payload) -> None:
         self.dist.irecv(payload, self.rank - 1, group=self.prev_group).wait()
 
     def send_tokens(self, tokens) -> None:
+        self._drop_completed()
         self.pending.append((self.dist.isend(tokens, 0, group=self.tok_group), tokens))
 
     def recv_tokens(self, tokens) -> None:
@@ -135,16 +143,21 @@ class TorchLink:
         self.pending.clear()
 
 
-def make_groups(world: int, backend: str | None = None) -> dict:
-    """The two-rank groups of `TorchLink`, created collectively by every rank."""
+def make_groups(world: int, backend: str | None = None, timeout_s: float | None = None) -> dict:
+    """The two-rank groups of `TorchLink`, created collectively by every rank.
+    `timeout_s` bounds every operation on them (a peer that never posts the
+    matching operation ends the wait with an error instead of a hang)."""
+    import datetime
+
     import torch.distributed as dist
 
     groups = {}
     if world < 2:
         return groups
+    kw = {} if timeout_s is None else {"timeout": datetime.timedelta(seconds=timeout_s)}
     for r in range(world - 1):
-        groups[("act", r)] = dist.new_group([r, r + 1], backend=backend)
-    groups["tok"] = dist.new_group([world - 1, 0], backend=backend)
+        groups[("act", r)] = dist.new_group([r, r + 1], backend=backend, **kw)
+    groups["tok"] = dist.new_group([world - 1, 0], backend=backend, **kw)
     return groups
 
 

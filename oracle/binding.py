@@ -66,6 +66,10 @@ def lib() -> C.CDLL:
         L.orc_dequantize_row.argtypes = [C.c_uint32, C.c_void_p, C.c_void_p, C.c_int64]
         L.orc_quantize_row_q8_k.argtypes = [C.c_void_p, C.c_void_p, C.c_int64]
         L.orc_matmul.argtypes = [C.POINTER(OrcTensor), C.c_void_p, C.c_int64, C.c_void_p]
+        for name in ("orc_dot_kquant_scalar", "orc_dot_kquant_vector"):
+            getattr(L, name).argtypes = [C.c_uint32, C.c_void_p, C.c_void_p, C.c_int64]
+            getattr(L, name).restype = C.c_float
+        L.orc_q8k_block_bytes.restype = C.c_size_t
         L.orc_rms_norm.argtypes = [C.c_void_p, C.c_void_p, C.c_int64, C.c_float, C.c_void_p]
         L.orc_rope_neox.argtypes = [C.c_void_p, C.c_int64, C.c_int64, C.c_int64, C.c_int32, C.c_float]
         L.orc_argmax.argtypes = [C.c_void_p, C.c_int64]

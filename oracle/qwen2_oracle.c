@@ -21,6 +21,7 @@
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
+#include <immintrin.h>
 #ifdef _OPENMP
 #include <omp.h>
 #endif
@@ -362,6 +363,149 @@ static float dot_q2_k(const uint8_t * w, const q8k_block * a, int64_t nb) {
     return (float) sum;
 }
 
+/* ---- the same dot products, vectorised ------------------------------------
+ * orc_matmul unpacks each weight row once into codes in element order (Q4_K
+ * and Q2_K codes as stored, Q6_K codes + 32, all in [0, 63]) with one scale
+ * and one min per 16-value group, then forms every integer sub-block sum with
+ * AVX2 byte products. Integer sums are exact in any order, so isum and msum
+ * equal the scalar loops' values above (dot_q{4,6,2}_k, kept as the readable
+ * statement and checked against this path by tests/test_oracle.py); the float
+ * block terms are then rounded and summed exactly as there. */
+typedef struct unpacked_row {
+    uint8_t * codes;  /* [nb * 256], 32-byte aligned */
+    int16_t * scale;  /* [nb * 16] per 16-value group */
+    int16_t * min;    /* [nb * 16] (Q4_K, Q2_K) */
+    float * d;        /* [nb] */
+    float * dmin;     /* [nb] (Q4_K, Q2_K) */
+} unpacked_row;
+
+static void unpack_row(uint32_t type, const uint8_t * w, int64_t nb, unpacked_row * u) {
+    const __m256i lo4 = _mm256_set1_epi8(0x0f), lo2 = _mm256_set1_epi8(0x03);
+    for (int64_t b = 0; b < nb; ++b) {
+        uint8_t * c = u->codes + 256 * b;
+        int16_t * sc = u->scale + 16 * b, * mn = u->min + 16 * b;
+        uint16_t hd, hm;
+        if (type == T_Q4_K) {
+            const uint8_t * blk = w + 144 * b;
+            memcpy(&hd, blk, 2);
+            memcpy(&hm, blk + 2, 2);
+            for (int j = 0; j < 8; ++j) {
+                int s, m;
+                q4k_scale_min(blk + 4, j, &s, &m);
+                sc[2 * j] = sc[2 * j + 1] = (int16_t) s;
+                mn[2 * j] = mn[2 * j + 1] = (int16_t) m;
+            }
+            /* element 64c + l (l < 32): low nibble of qs[32c + l]; 64c + 32 + l: high nibble */
+            for (int q = 0; q < 4; ++q) {
+                const __m256i x = _mm256_loadu_si256((const __m256i *) (blk + 16 + 32 * q));
+                _mm256_store_si256((__m256i *) (c + 64 * q), _mm256_and_si256(x, lo4));
+                _mm256_store_si256((__m256i *) (c + 64 * q + 32), _mm256_and_si256(_mm256_srli_epi16(x, 4), lo4));
+            }
+            u->d[b] = orc_f16_to_f32(hd);
+            u->dmin[b] = orc_f16_to_f32(hm);
+        } else if (type == T_Q6_K) {
+            const uint8_t * blk = w + 210 * b;
+            memcpy(&hd, blk + 208, 2);
+            for (int g = 0; g < 16; ++g) {
+                sc[g] = (int16_t) (int8_t) blk[192 + g];
+                mn[g] = 0;
+            }
+            /* element 128h + r: low nibble (r / 64) of ql[64h + r % 64], bits 2 (r / 32) of qh[32h + r % 32] */
+            for (int h = 0; h < 2; ++h) {
+                const __m256i l0 = _mm256_loadu_si256((const __m256i *) (blk + 64 * h));
+                const __m256i l1 = _mm256_loadu_si256((const __m256i *) (blk + 64 * h + 32));
+                const __m256i hh = _mm256_loadu_si256((const __m256i *) (blk + 128 + 32 * h));
+                const __m256i lows[4] = {_mm256_and_si256(l0, lo4), _mm256_and_si256(l1, lo4),
+                                         _mm256_and_si256(_mm256_srli_epi16(l0, 4), lo4),
+                                         _mm256_and_si256(_mm256_srli_epi16(l1, 4), lo4)};
+                for (int s = 0; s < 4; ++s) {
+                    const __m256i hi = _mm256_and_si256(_mm256_srli_epi16(hh, 2 * s), lo2);
+                    _mm256_store_si256((__m256i *) (c + 128 * h + 32 * s),
+                                       _mm256_or_si256(lows[s], _mm256_slli_epi16(hi, 4)));
+                }
+            }
+            u->d[b] = orc_f16_to_f32(hd);
+            u->dmin[b] = 0.0f;
+        } else {
+            const uint8_t * blk = w + 84 * b;
+            memcpy(&hd, blk + 80, 2);
+            memcpy(&hm, blk + 82, 2);
+            for (int g = 0; g < 16; ++g) {
+                sc[g] = (int16_t) (blk[g] & 15);
+                mn[g] = (int16_t) (blk[g] >> 4);
+            }
+            /* element 128h + 32s + l: bits 2s of qs[32h + l] */
+            for (int h = 0; h < 2; ++h) {
+                const __m256i x = _mm256_loadu_si256((const __m256i *) (blk + 16 + 32 * h));
+                for (int s = 0; s < 4; ++s) {
+                    _mm256_store_si256((__m256i *) (c + 128 * h + 32 * s), _mm256_and_si256(_mm256_srli_epi16(x, 2 * s), lo2));
+                }
+            }
+            u->d[b] = orc_f16_to_f32(hd);
+            u->dmin[b] = orc_f16_to_f32(hm);
+        }
+    }
+}
+
+static int32_t hsum_i32(__m256i v) {
+    __m128i s = _mm_add_epi32(_mm256_castsi256_si128(v), _mm256_extracti128_si256(v, 1));
+    s = _mm_add_epi32(s, _mm_shuffle_epi32(s, 0x4e));
+    s = _mm_add_epi32(s, _mm_shuffle_epi32(s, 0xb1));
+    return _mm_cvtsi128_si32(s);
+}
+
+static float dot_unpacked(uint32_t type, const unpacked_row * u, const q8k_block * a, int64_t nb) {
+    double sum = 0.0;
+    for (int64_t b = 0; b < nb; ++b) {
+        const uint8_t * c = u->codes + 256 * b;
+        const int16_t * sc = u->scale + 16 * b;
+        __m256i acc = _mm256_setzero_si256();
+        for (int v = 0; v < 8; ++v) {
+            /* 16 pair sums code*q (|sum| <= 2*63*127), then times the group scale, pairs summed in int32 */
+            const __m256i p = _mm256_maddubs_epi16(_mm256_load_si256((const __m256i *) (c + 32 * v)),
+                                                   _mm256_loadu_si256((const __m256i *) (a[b].qs + 32 * v)));
+            const __m256i s = _mm256_set_m128i(_mm_set1_epi16(sc[2 * v + 1]), _mm_set1_epi16(sc[2 * v]));
+            acc = _mm256_add_epi32(acc, _mm256_madd_epi16(p, s));
+        }
+        int32_t isum = hsum_i32(acc);
+        const __m256i bs = _mm256_loadu_si256((const __m256i *) a[b].bsums);
+        if (type == T_Q6_K) {
+            /* codes carry +32: sum (q6 + 32) q = sum q6 q + 32 bsum */
+            isum -= 32 * hsum_i32(_mm256_madd_epi16(_mm256_loadu_si256((const __m256i *) sc), bs));
+            const float c6 = (u->d[b] * a[b].d) * (float) isum;
+            sum += (double) c6;
+        } else {
+            const int32_t msum = hsum_i32(_mm256_madd_epi16(_mm256_loadu_si256((const __m256i *) (u->min + 16 * b)), bs));
+            const float d = u->d[b] * a[b].d;
+            const float dmin = u->dmin[b] * a[b].d;
+            const float cb = d * (float) isum - dmin * (float) msum;
+            sum += (double) cb;
+        }
+    }
+    return (float) sum;
+}
+
+float orc_dot_kquant_scalar(uint32_t type, const void * w, const void * a, int64_t nb) {
+    if (type == T_Q4_K) return dot_q4_k(w, a, nb);
+    if (type == T_Q6_K) return dot_q6_k(w, a, nb);
+    return dot_q2_k(w, a, nb);
+}
+
+float orc_dot_kquant_vector(uint32_t type, const void * w, const void * a, int64_t nb) {
+    unpacked_row u;
+    u.codes = aligned_alloc(32, (size_t) nb * 256);
+    u.scale = malloc(sizeof(int16_t) * 16 * (size_t) nb);
+    u.min = malloc(sizeof(int16_t) * 16 * (size_t) nb);
+    u.d = malloc(sizeof(float) * (size_t) nb);
+    u.dmin = malloc(sizeof(float) * (size_t) nb);
+    unpack_row(type, w, nb, &u);
+    const float v = dot_unpacked(type, &u, a, nb);
+    free(u.codes); free(u.scale); free(u.min); free(u.d); free(u.dmin);
+    return v;
+}
+
+size_t orc_q8k_block_bytes(void) { return sizeof(q8k_block); }
+
 /* ggml_mul_mat on the CPU backend (qwen2_architecture.cpp:347-371 builds it):
  * src1 rows are converted to the weight's vec_dot_type first (Q8_K for
  * K-quants, F16 for F16 weights, none for F32), then every output element is
@@ -374,16 +518,20 @@ void orc_matmul(const orc_tensor * w, const float * x, int64_t rows, float * y) 
         const size_t bb = block_bytes(w->type);
         q8k_block * act = malloc(sizeof(q8k_block) * (size_t) (nb * rows));
         for (int64_t r = 0; r < rows; ++r) orc_quantize_row_q8_k(x + r * K, act + r * nb, K);
-#pragma omp parallel for schedule(static)
-        for (int64_t n = 0; n < N; ++n) {
-            const uint8_t * wr = base + (size_t) n * (size_t) nb * bb;
-            for (int64_t r = 0; r < rows; ++r) {
-                float v;
-                if (w->type == T_Q4_K) v = dot_q4_k(wr, act + r * nb, nb);
-                else if (w->type == T_Q6_K) v = dot_q6_k(wr, act + r * nb, nb);
-                else v = dot_q2_k(wr, act + r * nb, nb);
-                y[r * N + n] = v;
+#pragma omp parallel
+        {
+            unpacked_row u;
+            u.codes = aligned_alloc(32, (size_t) nb * 256);
+            u.scale = malloc(sizeof(int16_t) * 16 * (size_t) nb);
+            u.min = malloc(sizeof(int16_t) * 16 * (size_t) nb);
+            u.d = malloc(sizeof(float) * (size_t) nb);
+            u.dmin = malloc(sizeof(float) * (size_t) nb);
+#pragma omp for schedule(static)
+            for (int64_t n = 0; n < N; ++n) {
+                unpack_row(w->type, base + (size_t) n * (size_t) nb * bb, nb, &u);
+                for (int64_t r = 0; r < rows; ++r) y[r * N + n] = dot_unpacked(w->type, &u, act + r * nb, nb);
             }
+            free(u.codes); free(u.scale); free(u.min); free(u.d); free(u.dmin);
         }
         free(act);
         return;

@@ -65,6 +65,12 @@ void orc_set_threads(int threads);
 void orc_dequantize_row(uint32_t type, const void * src, float * dst, int64_t k);
 /* GGML block_q8_K: float d, int8 qs[256], int16 bsums[16]  (292 bytes) */
 void orc_quantize_row_q8_k(const float * x, void * blocks, int64_t k);
+/* One row of nb K-quant blocks (type 9, 11 or 13) times nb Q8_K blocks: the
+ * readable scalar loops and the vectorised path orc_matmul runs. The two must
+ * agree bit for bit (the integer sums are exact in any order). */
+float orc_dot_kquant_scalar(uint32_t type, const void * w, const void * a, int64_t nb);
+float orc_dot_kquant_vector(uint32_t type, const void * w, const void * a, int64_t nb);
+size_t orc_q8k_block_bytes(void);
 /* y[r * ne1 + n] = sum_k W[n, k] * x[r * ne0 + k] with GGML-CPU mul_mat semantics */
 void orc_matmul(const orc_tensor * w, const float * x, int64_t rows, float * y);
 void orc_rms_norm(const float * x, const float * weight, int64_t n, float eps, float * y);

@@ -46,6 +46,43 @@ def test_dequant_bit_exact_on_package_tensors(small_q4k_package):
             assert np.array_equal(mine.view(np.uint32), ref.view(np.uint32)), t.name
 
 
+BLOCK_BYTES = {jfm.JF_TENSOR_Q4_K: 144, jfm.JF_TENSOR_Q6_K: 210, jfm.JF_TENSOR_Q2_K: 84}
+# byte offsets of the f16 block scales (d, dmin) inside each block
+SCALE_OFFSETS = {jfm.JF_TENSOR_Q4_K: (0, 2), jfm.JF_TENSOR_Q6_K: (208,), jfm.JF_TENSOR_Q2_K: (80, 82)}
+
+
+@pytest.mark.parametrize("jf_type", list(GGUF_TYPES))
+def test_vectorised_dot_matches_scalar_dot(jf_type):
+    """orc_matmul's AVX2 path forms the same integer sums as the scalar
+    restatement of ggml_vec_dot_*_q8_K: random raw blocks over the full code,
+    scale and min ranges, random Q8_K blocks with codes in [-127, 127]."""
+    import ctypes as C
+    L = ob.lib()
+    assert L.orc_q8k_block_bytes() == 292
+    rng = np.random.default_rng(100 + jf_type)
+    for nb in (1, 3, 14, 74):
+        for trial in range(8):
+            w = rng.integers(0, 256, nb * BLOCK_BYTES[jf_type], dtype=np.uint8).reshape(nb, -1)
+            for off in SCALE_OFFSETS[jf_type]:
+                w[:, off:off + 2] = np.frombuffer(rng.normal(0, 0.05, nb).astype(np.float16).tobytes(),
+                                                  dtype=np.uint8).reshape(nb, 2)
+            if trial == 0:  # extreme codes and scales
+                w[:, :] = 0xFF
+                for off in SCALE_OFFSETS[jf_type]:
+                    w[:, off:off + 2] = np.frombuffer(np.float16(0.5).tobytes(), dtype=np.uint8)
+            qs = rng.integers(-127, 128, (nb, 256)).astype(np.int8)
+            if trial == 1:
+                qs[:] = -127
+            a = np.zeros((nb, 292), dtype=np.uint8)
+            a[:, 0:4] = np.frombuffer(rng.uniform(1e-4, 1e-1, nb).astype(np.float32).tobytes(), dtype=np.uint8).reshape(nb, 4)
+            a[:, 4:260] = qs.view(np.uint8)
+            a[:, 260:292] = qs.astype(np.int16).reshape(nb, 16, 16).sum(axis=2).astype(np.int16).view(np.uint8).reshape(nb, 32)
+            wp, ap = np.ascontiguousarray(w), np.ascontiguousarray(a)
+            s = L.orc_dot_kquant_scalar(jf_type, wp.ctypes.data, ap.ctypes.data, nb)
+            v = L.orc_dot_kquant_vector(jf_type, wp.ctypes.data, ap.ctypes.data, nb)
+            assert np.float32(s).view(np.uint32) == np.float32(v).view(np.uint32), (nb, trial, s, v)
+
+
 def test_q8_k_quantization_properties():
     rng = np.random.default_rng(3)
     x = rng.normal(0, 1, 256 * 8).astype(np.float32)
