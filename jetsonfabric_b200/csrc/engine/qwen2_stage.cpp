@@ -167,6 +167,7 @@ double matmul_bytes(const jfb_weight & w, std::uint32_t n, std::uint32_t epilogu
 
 DeviceModel::DeviceModel(const std::string & package_path, std::uint32_t layer_start, std::uint32_t layer_end) {
     cuda_check(cudaGetDevice(&device_), "query CUDA device");
+    kv_pool_ = std::make_shared<KvPool>(device_);
     cudaDeviceProp prop{};
     cuda_check(cudaGetDeviceProperties(&prop, device_), "query CUDA device properties");
     device_name_ = prop.name;
@@ -416,24 +417,83 @@ DeviceModel::~DeviceModel() {
 
 // ---- KV cache ----------------------------------------------------------------
 
-KvCache::KvCache(const DeviceModel & model, std::uint32_t capacity) : capacity_(capacity) {
-    const std::uint64_t elems = std::uint64_t(model.layers()) * capacity * model.hparams().kv_dim();
-    bytes_ = 2 * elems * sizeof(std::uint16_t);
-    cuda_check(cudaMalloc(&k_, elems * sizeof(std::uint16_t)), "could not allocate native Qwen2 KV cache");
-    const cudaError_t e = cudaMalloc(&v_, elems * sizeof(std::uint16_t));
-    if (e != cudaSuccess) {
-        cudaFree(k_);
-        k_ = nullptr;
-        cuda_check(e, "could not allocate native Qwen2 KV cache");
+namespace {
+constexpr std::uint64_t kKvMinChunk = 64ull << 20;    // smallest chunk taken from the device
+constexpr std::uint64_t kKvMaxChunk = 2ull << 30;     // largest chunk (unless one cache is larger)
+constexpr std::uint64_t kKvFreeMargin = 512ull << 20;  // device memory a new chunk must leave free
+}  // namespace
+
+KvPool::~KvPool() {
+    for (void * c : chunks_) cudaFree(c);
+}
+
+std::uint64_t KvPool::reserved_bytes() const {
+    std::lock_guard lock(mu_);
+    return reserved_;
+}
+
+void * KvPool::acquire(std::uint64_t bytes) {
+    std::lock_guard lock(mu_);
+    auto it = free_.find(bytes);
+    if (it != free_.end() && !it->second.empty()) {
+        void * p = it->second.back();
+        it->second.pop_back();
+        return p;
     }
+    if (left_ < bytes) {
+        // a new chunk: room for about eight more caches of this size
+        std::uint64_t want = std::max(bytes, std::min(kKvMaxChunk, std::max(kKvMinChunk, 8 * bytes)));
+        int prev = -1;
+        cuda_check(cudaGetDevice(&prev), "query the current device");
+        cuda_check(cudaSetDevice(device_), "select the stage device");
+        std::size_t free_bytes = 0, total_bytes = 0;
+        cudaError_t e = cudaMemGetInfo(&free_bytes, &total_bytes);
+        if (e == cudaSuccess && free_bytes < want + kKvFreeMargin) want = bytes;  // only what this cache needs
+        void * chunk = nullptr;
+        if (e == cudaSuccess && free_bytes >= want + kKvFreeMargin) e = cudaMalloc(&chunk, want);
+        else if (e == cudaSuccess) e = cudaErrorMemoryAllocation;
+        cudaSetDevice(prev);
+        if (e != cudaSuccess || chunk == nullptr) {
+            (void) cudaGetLastError();
+            throw std::runtime_error("could not allocate native Qwen2 KV cache");
+        }
+        chunks_.push_back(chunk);
+        reserved_ += want;
+        // the unused tail of the previous chunk serves no later cache of this
+        // size; keep it for smaller ones
+        if (left_ >= 256) free_[left_].push_back(cursor_);
+        cursor_ = static_cast<std::uint8_t *>(chunk);
+        left_ = want;
+    }
+    void * p = cursor_;
+    cursor_ += bytes;
+    left_ -= bytes;
+    return p;
+}
+
+void KvPool::release(void * p, std::uint64_t bytes) {
+    std::lock_guard lock(mu_);
+    free_[bytes].push_back(p);
+}
+
+KvCache::KvCache(const DeviceModel & model, std::uint32_t capacity) : pool_(model.kv_pool()), capacity_(capacity) {
+    const std::uint64_t elems = std::uint64_t(model.layers()) * capacity * model.hparams().kv_dim();
+    const std::uint64_t half = align256(elems * sizeof(std::uint16_t));
+    bytes_ = 2 * elems * sizeof(std::uint16_t);
+    block_ = 2 * half;
+    auto * base = static_cast<std::uint8_t *>(pool_->acquire(block_));
+    k_ = reinterpret_cast<std::uint16_t *>(base);
+    v_ = reinterpret_cast<std::uint16_t *>(base + half);
     // the reference clears its cache buffer at allocation (qwen2_architecture.cpp:1091)
-    cuda_check(cudaMemsetAsync(k_, 0, elems * sizeof(std::uint16_t), model.stream()), "clear KV cache");
-    cuda_check(cudaMemsetAsync(v_, 0, elems * sizeof(std::uint16_t), model.stream()), "clear KV cache");
+    const cudaError_t e = cudaMemsetAsync(base, 0, block_, model.stream());
+    if (e != cudaSuccess) {
+        pool_->release(base, block_);
+        cuda_check(e, "clear KV cache");
+    }
 }
 
 KvCache::~KvCache() {
-    if (k_ != nullptr) cudaFree(k_);
-    if (v_ != nullptr) cudaFree(v_);
+    if (k_ != nullptr) pool_->release(k_, block_);
 }
 
 // ---- stage forward ----------------------------------------------------------

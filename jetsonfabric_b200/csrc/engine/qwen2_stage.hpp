@@ -9,7 +9,9 @@
 
 #include <cstdint>
 #include <memory>
+#include <mutex>
 #include <span>
+#include <unordered_map>
 #include <string>
 #include <vector>
 
@@ -43,6 +45,8 @@ struct LayerWeights {
     const float * ffn_norm = nullptr;
 };
 
+class KvPool;
+
 // Throws std::runtime_error with `what` and the CUDA error string.
 void cuda_check(cudaError_t e, const char * what);
 // Throws std::runtime_error for a failing jfb_status.
@@ -72,6 +76,8 @@ public:
     const LayerWeights & layer(std::uint32_t i) const { return layer_weights_[i]; }
     // GGML rope cache (cos, sin) for positions [0, context_length), device
     const float * rope_table() const { return rope_table_; }
+    // the stage's KV cache memory (shared with the caches it handed out)
+    const std::shared_ptr<KvPool> & kv_pool() const { return kv_pool_; }
 
     const std::string & source_sha256() const { return source_sha256_; }
     const std::string & device_name() const { return device_name_; }
@@ -88,12 +94,42 @@ private:
     void * arena_ = nullptr;
     std::uint64_t arena_bytes_ = 0;
     float * rope_table_ = nullptr;
+    std::shared_ptr<KvPool> kv_pool_;
     jfb_weight token_embd_{}, output_{};
     const float * output_norm_ = nullptr;
     const float * output_bias_ = nullptr;
     std::vector<LayerWeights> layer_weights_;
     std::string source_sha256_, device_name_;
     std::uint64_t weight_bytes_ = 0, total_weight_bytes_ = 0, tensor_count_ = 0;
+};
+
+// Device memory for the KV caches of one stage's sessions. The reference
+// allocates one cache buffer per session (qwen2_architecture.cpp:1056-1092);
+// here sessions take their caches from large chunks that the stage keeps until
+// it is destroyed, and a closed session's cache goes back to a free list by
+// size for the next session of that size. Opening or closing a session
+// therefore never calls cudaFree, which would synchronise the whole device
+// (and, in a pipeline, wait behind transfers that need a peer stage's
+// progress). A new chunk is admitted only while the device keeps a margin of
+// free memory; past that, a session that needs new memory is refused with the
+// reference's allocation error.
+class KvPool {
+public:
+    explicit KvPool(int device) : device_(device) {}
+    ~KvPool();
+    KvPool(const KvPool &) = delete;
+    KvPool & operator=(const KvPool &) = delete;
+    void * acquire(std::uint64_t bytes);
+    void release(void * p, std::uint64_t bytes);
+    std::uint64_t reserved_bytes() const;
+
+private:
+    int device_;
+    mutable std::mutex mu_;
+    std::vector<void *> chunks_;
+    std::uint8_t * cursor_ = nullptr;
+    std::uint64_t left_ = 0, reserved_ = 0;
+    std::unordered_map<std::uint64_t, std::vector<void *>> free_;
 };
 
 // Per-session F16 KV cache: K and V, each [layers][capacity][kv_dim].
@@ -108,10 +144,12 @@ public:
     std::uint64_t bytes() const { return bytes_; }
 
 private:
+    std::shared_ptr<KvPool> pool_;
     std::uint16_t * k_ = nullptr;
     std::uint16_t * v_ = nullptr;
     std::uint32_t capacity_ = 0;
     std::uint64_t bytes_ = 0;
+    std::uint64_t block_ = 0;  // bytes taken from the pool (K and V together)
 };
 
 // One sequence's slice of a batched forward call: `rows` consecutive rows

@@ -244,3 +244,25 @@ def test_wide_batched_decode_matches_oracle(E, small_q4k_package):
             for g, t in zip(got, cur):
                 g.append(t)
         assert got == ref
+
+
+def test_closed_sessions_return_their_kv_memory(E, small_q4k_package):
+    """Session caches come from the stage's KV pool: closing a session returns
+    its cache for the next session of that size, so a second wave of sessions
+    takes no new device memory (and no session close calls cudaFree)."""
+    with E.NativeEngine(small_q4k_package, "cuda") as eng:
+        free_after_first = None
+        for wave in range(3):
+            sessions = [eng.create_session(200) for _ in range(12)]
+            assert sessions[0].prefill_greedy([1, 2, 3]) >= 0
+            for s in sessions:
+                s.close()
+            torch.cuda.synchronize()
+            free = torch.cuda.mem_get_info()[0]
+            if wave == 0:
+                free_after_first = free
+            else:
+                assert free == free_after_first, (wave, free_after_first - free)
+        # a fresh cache reads as zeros, as the reference's cleared buffer does
+        s = eng.create_session(200)
+        assert s.prefill_greedy([1, 2, 3]) == eng.generate([1, 2, 3], 1).sampled_tokens[0]
