@@ -10,6 +10,8 @@
 // blocks straight from registers.
 #include "common.cuh"
 
+#include <algorithm>
+
 namespace jfb {
 namespace {
 
@@ -89,16 +91,20 @@ __global__ void __launch_bounds__(kThreads) rmsnorm_quant_kernel(
 }
 
 // One warp per Q8_K block: grid (ceil(blocks / 8), rows).
-__global__ void __launch_bounds__(kThreads) quantize_kernel(const float * __restrict__ x, uint32_t cols, jfb_q8k q8) {
+// grid (ceil(blocks / 8), min(rows, 65535)); rows beyond the grid's y extent
+// are taken in strides of gridDim.y (warp-uniform loop)
+__global__ void __launch_bounds__(kThreads) quantize_kernel(const float * __restrict__ x, uint32_t n, uint32_t cols,
+                                                         jfb_q8k q8) {
     pdl_trigger();
     pdl_wait();
     const uint32_t blk = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (blk >= cols / kQK) return;  // warp-uniform
-    const uint32_t row = blockIdx.y;
-    const float4 * src = reinterpret_cast<const float4 *>(x + uint64_t(row) * cols + blk * kQK + 8 * lane);
-    const float4 a = src[0], b = src[1];
-    const Vals8 y = {{a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w}};
-    q8k_block_warp(y, q8_dest(q8, row, blk, cols / kQK));
+    for (uint32_t row = blockIdx.y; row < n; row += gridDim.y) {
+        const float4 * src = reinterpret_cast<const float4 *>(x + uint64_t(row) * cols + blk * kQK + 8 * lane);
+        const float4 a = src[0], b = src[1];
+        const Vals8 y = {{a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w}};
+        q8k_block_warp(y, q8_dest(q8, row, blk, cols / kQK));
+    }
 }
 
 // silu(g) * u with silu(g) = g / (1 + e^-g), each step rounded
@@ -107,26 +113,28 @@ __device__ __forceinline__ float swiglu(float g, float u) {
     return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, exp_cw(-g))), u);
 }
 
-// One warp per 256 values: grid (ceil(cols / 2048), rows). With Q8_K output
-// (cols a multiple of 256) each warp quantizes its block; the f32-only form
-// also takes rows of any length.
+// One warp per 256 values: grid (ceil(cols / 2048), min(rows, 65535)), rows
+// beyond the grid's y extent in strides of gridDim.y. With Q8_K output (cols
+// a multiple of 256) each warp quantizes its block; the f32-only form also
+// takes rows of any length.
 __global__ void __launch_bounds__(kThreads) swiglu_quant_kernel(const float * __restrict__ gate, const float * __restrict__ up,
-                                                             uint32_t cols, float * __restrict__ out_f32, jfb_q8k q8,
-                                                             int quantize) {
+                                                             uint32_t n, uint32_t cols, float * __restrict__ out_f32,
+                                                             jfb_q8k q8, int quantize) {
     pdl_trigger();
     pdl_wait();
     const uint32_t blk = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (blk * kQK >= cols) return;  // warp-uniform
-    const uint32_t row = blockIdx.y;
-    const uint64_t base = uint64_t(row) * cols + blk * kQK + 8 * lane;
-    Vals8 y;
+    for (uint32_t row = blockIdx.y; row < n; row += gridDim.y) {
+        const uint64_t base = uint64_t(row) * cols + blk * kQK + 8 * lane;
+        Vals8 y;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-        const bool in = blk * kQK + 8 * lane + j < cols;
-        y.v[j] = in ? swiglu(gate[base + j], up[base + j]) : 0.0f;
-        if (out_f32 != nullptr && in) out_f32[base + j] = y.v[j];
+        for (int j = 0; j < 8; ++j) {
+            const bool in = blk * kQK + 8 * lane + j < cols;
+            y.v[j] = in ? swiglu(gate[base + j], up[base + j]) : 0.0f;
+            if (out_f32 != nullptr && in) out_f32[base + j] = y.v[j];
+        }
+        if (quantize) q8k_block_warp(y, q8_dest(q8, row, blk, cols / kQK));
     }
-    if (quantize) q8k_block_warp(y, q8_dest(q8, row, blk, cols / kQK));
 }
 
 jfb_status check_q8(const jfb_q8k * q8, uint32_t n, uint32_t cols) {
@@ -169,9 +177,8 @@ extern "C" jfb_status jfb_quantize_q8k(const float * x, uint32_t n, uint32_t col
     jfb_status s = check_q8(out, n, cols);
     if (s.code != JFB_STATUS_OK) return s;
     if (n == 0) return status_ok();
-    if (n > 65535u) return status_error(JFB_STATUS_INVALID_ARGUMENT, "Q8_K rows above 65535 per call");
-    const cudaError_t e = launch_k(quantize_kernel, dim3((cols / kQK + 7) / 8, n), dim3(kThreads), 0, as_stream(stream), x,
-                                   cols, *out);
+    const cudaError_t e = launch_k(quantize_kernel, dim3((cols / kQK + 7) / 8, std::min(n, 65535u)), dim3(kThreads), 0,
+                                   as_stream(stream), x, n, cols, *out);
     if (e != cudaSuccess) return status_error(JFB_STATUS_CUDA_ERROR, "jfb_quantize_q8k: %s", cudaGetErrorString(e));
     return launch_status("jfb_quantize_q8k");
 }
@@ -185,9 +192,9 @@ extern "C" jfb_status jfb_swiglu_quant(const float * gate, const float * up, uin
     if (s.code != JFB_STATUS_OK) return s;
     if (n == 0 || cols == 0) return status_ok();
     const jfb_q8k q8 = out_q8 != nullptr ? *out_q8 : jfb_q8k{};
-    if (n > 65535u) return status_error(JFB_STATUS_INVALID_ARGUMENT, "swiglu rows above 65535 per call");
-    const cudaError_t e = launch_k(swiglu_quant_kernel, dim3((cols + 8 * kQK - 1) / (8 * kQK), n), dim3(kThreads), 0,
-                                   as_stream(stream), gate, up, cols, out_f32, q8, out_q8 != nullptr ? 1 : 0);
+    const cudaError_t e = launch_k(swiglu_quant_kernel, dim3((cols + 8 * kQK - 1) / (8 * kQK), std::min(n, 65535u)),
+                                   dim3(kThreads), 0, as_stream(stream), gate, up, n, cols, out_f32, q8,
+                                   out_q8 != nullptr ? 1 : 0);
     if (e != cudaSuccess) return status_error(JFB_STATUS_CUDA_ERROR, "jfb_swiglu_quant: %s", cudaGetErrorString(e));
     return launch_status("jfb_swiglu_quant");
 }
