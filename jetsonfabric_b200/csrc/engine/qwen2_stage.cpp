@@ -499,6 +499,14 @@ KvCache::~KvCache() {
 // ---- stage forward ----------------------------------------------------------
 
 Qwen2Stage::Qwen2Stage(DeviceModel & model) : m_(model) {
+    // rows per device pass: a larger batched prefill runs as several passes,
+    // which bounds the activation scratch (about 330 KB per row at the 7B
+    // widths); JFB_MAX_PASS_ROWS overrides the default
+    if (const char * v = std::getenv("JFB_MAX_PASS_ROWS")) {
+        const long n = std::strtol(v, nullptr, 10);
+        if (n < 1 || n > (1L << 24)) throw std::invalid_argument("JFB_MAX_PASS_ROWS must be between 1 and 16777216");
+        max_pass_rows_ = static_cast<std::uint32_t>(n);
+    }
     // JFB_MATMUL_PATH selects between the two bit-identical K-quant matmuls:
     // "auto" (default), "cuda-core" or "tensor-core".
     if (const char * path = std::getenv("JFB_MATMUL_PATH")) {
@@ -675,6 +683,74 @@ void Qwen2Stage::ensure_scratch(std::uint32_t rows, std::uint32_t seqs) {
 }
 
 void Qwen2Stage::forward(std::span<const SequenceRows> seqs, const ForwardIo & io) {
+    std::uint64_t total = 0;
+    for (const SequenceRows & s : seqs) {
+        if (s.rows == 0 || s.cache == nullptr || s.start + s.rows > s.cache->capacity()) {
+            throw std::invalid_argument("native Qwen2 rows are outside session capacity");
+        }
+        total += s.rows;
+    }
+    if (total <= max_pass_rows_) {
+        forward_pass(seqs, io);
+        return;
+    }
+    // Chunked pass (a large batched prefill): every row's result is computed
+    // exactly as in one pass, since a row depends only on the KV cache rows
+    // before it, which earlier passes have appended. Sequences are packed
+    // into passes of at most max_pass_rows_ rows; a longer sequence is cut
+    // into pieces of max_pass_rows_ rows, each a pass of its own, and only its
+    // last piece produces the sequence's output (the others send their
+    // sampled token to a scratch word).
+    struct Piece {
+        std::uint32_t seq, start, rows;
+        bool final;
+    };
+    std::vector<Piece> pieces;
+    for (std::uint32_t i = 0; i < seqs.size(); ++i) {
+        std::uint32_t done = 0;
+        while (seqs[i].rows - done > max_pass_rows_) {
+            pieces.push_back(Piece{i, seqs[i].start + done, max_pass_rows_, false});
+            done += max_pass_rows_;
+        }
+        pieces.push_back(Piece{i, seqs[i].start + done, seqs[i].rows - done, true});
+    }
+    const std::uint64_t h = m_.hparams().info.embedding_length, V = m_.vocabulary();
+    std::uint64_t row0 = 0;
+    std::vector<SequenceRows> pass;
+    for (std::size_t p = 0; p < pieces.size();) {
+        pass.clear();
+        std::uint64_t rows = 0;
+        const std::size_t first = p;
+        // a non-final piece is always a pass of its own
+        do {
+            pass.push_back(SequenceRows{seqs[pieces[p].seq].cache, pieces[p].start, pieces[p].rows});
+            rows += pieces[p].rows;
+            ++p;
+        } while (p < pieces.size() && pieces[first].final && pieces[p].final &&
+                 rows + pieces[p].rows <= max_pass_rows_);
+        ForwardIo pio = io;
+        pio.synchronize = false;
+        if (io.tokens != nullptr) pio.tokens = io.tokens + row0;
+        if (io.activations != nullptr) pio.activations = io.activations + row0 * h;
+        if (io.activations_out != nullptr) pio.activations_out = io.activations_out + row0 * h;
+        if (!pieces[first].final) {
+            pio.tokens_out = nullptr;  // the final stage samples into its scratch word
+            pio.logits_out = nullptr;
+        } else {
+            const std::uint32_t s0 = pieces[first].seq;
+            if (io.tokens_out != nullptr) pio.tokens_out = io.tokens_out + s0;
+            if (io.logits_out != nullptr) pio.logits_out = io.logits_out + std::uint64_t(s0) * V;
+        }
+        forward_pass(pass, pio);
+        row0 += rows;
+    }
+    if (io.synchronize) {
+        cuda_check(cudaStreamSynchronize(m_.stream()), "native Qwen2 stage computation failed");
+        check_device_errors();
+    }
+}
+
+void Qwen2Stage::forward_pass(std::span<const SequenceRows> seqs, const ForwardIo & io) {
     const Qwen2HParams & hp = m_.hparams();
     const std::uint32_t S = static_cast<std::uint32_t>(seqs.size());
     std::uint32_t R = 0, max_keys = 1;

@@ -210,6 +210,7 @@ public:
     KernelTiming collect_timing();
 
 private:
+    void forward_pass(std::span<const SequenceRows> seqs, const ForwardIo & io);
     void ensure_scratch(std::uint32_t rows, std::uint32_t seqs);
     void ensure_attention_scratch(std::uint64_t bytes);
     void free_scratch();
@@ -243,6 +244,7 @@ private:
     std::uint64_t meta_bytes_ = 0;
     cudaEvent_t meta_uploaded_ = nullptr;  // the pinned staging buffer is free again
     std::uint32_t cap_rows_ = 0, cap_seqs_ = 0;
+    std::uint32_t max_pass_rows_ = 65536;
     std::uint64_t scratch_bytes_ = 0;
     std::uint64_t launches_ = 0;
     // kernel timing

@@ -134,11 +134,15 @@ struct TypeTraits<JF_TENSOR_Q2_K> {
 // Warp roles for BN activation rows per tile.
 template <int BN>
 struct Roles {
-    static constexpr int kEpiWarps = 8;       // 4 TMEM lane quarters x 2 column halves
-    static constexpr int kCols = BN / 2;      // token columns per epilogue thread
+    // 4 TMEM lane quarters x 2 (32-token tiles) or 4 (64-token tiles) column
+    // groups: 16 token columns per epilogue thread either way, and four
+    // epilogue warps per SM sub-partition on 64-token tiles to hide the TMEM
+    // load latency of the per-block epilogue
+    static constexpr int kEpiWarps = BN == 64 ? 16 : 8;
+    static constexpr int kCols = BN * 4 / kEpiWarps;  // token columns per epilogue thread
     // converter groups: with two, group g converts half-block g of every
     // unit, so the two halves of a unit are converted concurrently
-    static constexpr int kGroups = BN == 32 ? 2 : 1;
+    static constexpr int kGroups = 2;
     static constexpr int kGroupWarps = BN == 32 ? 8 : 4;
     static constexpr int kConvWarps = kGroups * kGroupWarps;
     static constexpr int kParts = kGroupWarps * 32 / kRows;  // converter threads per weight row in a group
@@ -445,6 +449,17 @@ __device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
     asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
                  : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
                  : "r"(taddr));
+}
+// 4 consecutive f32 columns of this thread's TMEM lane (completes at tmem_wait_ld).
+__device__ __forceinline__ void tmem_ld4(uint32_t taddr, uint32_t (&r)[4]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(taddr));
+}
+template <int N>
+__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&r)[N]) {
+    if constexpr (N == 8) tmem_ld8(taddr, r);
+    else tmem_ld4(taddr, r);
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
@@ -1178,15 +1193,35 @@ __global__ void __launch_bounds__(Roles<BN>::kThreads) __maxnreg__(Roles<BN>::kR
             const float2 dw2 = f2(dw, dw), dmin2 = f2(dmin, dmin);
             const uint32_t base = tmem + lane_base + acc * (T::kAcc * BN) + col0;
 #pragma unroll
-            for (int ch = 0; ch < kCols / 8; ++ch) {
-                uint32_t r0[8], r1[8], r2[8];
-                tmem_ld8(base + 8 * ch, r0);
-                tmem_ld8(base + BN + 8 * ch, r1);
-                if constexpr (T::kAcc == 3) tmem_ld8(base + 2 * BN + 8 * ch, r2);
-                const float4 da0 = *reinterpret_cast<const float4 *>(da_s + 8 * ch);
-                const float4 da1 = *reinterpret_cast<const float4 *>(da_s + 8 * ch + 4);
+            // The unit's accumulator columns come in chunks of kCw, double
+            // buffered: chunk ch + 1 is requested before chunk ch is worked on,
+            // so its TMEM load latency overlaps that arithmetic (wait::ld
+            // waits for every earlier load of the thread, so the request is
+            // issued after the wait that completes chunk ch).
+            constexpr int kCw = R::kSmemSums ? 8 : 4;
+            constexpr int kChunks = kCols / kCw;
+            uint32_t rb[2][3][kCw];
+            auto request = [&](int ch, uint32_t (&r)[3][kCw]) {
+                tmem_ld_cols<kCw>(base + kCw * ch, r[0]);
+                tmem_ld_cols<kCw>(base + BN + kCw * ch, r[1]);
+                if constexpr (T::kAcc == 3) tmem_ld_cols<kCw>(base + 2 * BN + kCw * ch, r[2]);
+            };
+            request(0, rb[0]);
+#pragma unroll
+            for (int ch = 0; ch < kChunks; ++ch) {
+                uint32_t (&r0)[kCw] = rb[ch & 1][0];
+                uint32_t (&r1)[kCw] = rb[ch & 1][1];
+                uint32_t (&r2)[kCw] = rb[ch & 1][2];
+                float2 das[kCw / 2];
+#pragma unroll
+                for (int q = 0; q < kCw / 4; ++q) {
+                    const float4 d4 = *reinterpret_cast<const float4 *>(da_s + kCw * ch + 4 * q);
+                    das[2 * q] = f2(d4.x, d4.y);
+                    das[2 * q + 1] = f2(d4.z, d4.w);
+                }
                 tmem_wait_ld();
-                if (ch == kCols / 8 - 1) {
+                if (ch + 1 < kChunks) request(ch + 1, rb[(ch + 1) & 1]);
+                if (ch == kChunks - 1) {
                     // the accumulators and the ring slot may be reused now
                     tc_fence_before();
                     __syncwarp();
@@ -1195,9 +1230,8 @@ __global__ void __launch_bounds__(Roles<BN>::kThreads) __maxnreg__(Roles<BN>::kR
                         mbar_arrive(&epi_empty[es]);
                     }
                 }
-                const float2 das[4] = {f2(da0.x, da0.y), f2(da0.z, da0.w), f2(da1.x, da1.y), f2(da1.z, da1.w)};
 #pragma unroll
-                for (int k = 0; k < 4; ++k) {
+                for (int k = 0; k < kCw / 2; ++k) {
                     const float2 da2 = das[k];
                     const float2 a0 = f2(__uint_as_float(r0[2 * k]), __uint_as_float(r0[2 * k + 1]));
                     const float2 a1 = f2(__uint_as_float(r1[2 * k]), __uint_as_float(r1[2 * k + 1]));
@@ -1218,7 +1252,7 @@ __global__ void __launch_bounds__(Roles<BN>::kThreads) __maxnreg__(Roles<BN>::kR
                         const float2 t2 = mul2_rn(mul2_rn(dmin2, da2), a1);
                         c = f2(__fsub_rn(t1.x, t2.x), __fsub_rn(t1.y, t2.y));
                     }
-                    const int t = 8 * ch + 2 * k;
+                    const int t = kCw * ch + 2 * k;
                     sum_set(t, sum_get(t) + double(c.x));
                     sum_set(t + 1, sum_get(t + 1) + double(c.y));
                 }
@@ -1364,7 +1398,7 @@ Plan make_plan(uint32_t rows, uint32_t cols, uint32_t n) {
 constexpr uint32_t kMaxBN = 64;
 uint64_t partial_bytes() { return uint64_t(2) * uint64_t(sm_count()) * uint64_t(kRows) * kMaxBN * sizeof(double); }
 uint64_t workspace_bytes(const Plan & pl) {
-    return partial_bytes() + uint64_t(pl.tiles) * Roles<32>::kEpiWarps * sizeof(uint32_t);
+    return partial_bytes() + uint64_t(pl.tiles) * Roles<64>::kEpiWarps * sizeof(uint32_t);
 }
 
 // ---- tensor maps ----------------------------------------------------------------

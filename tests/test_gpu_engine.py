@@ -266,3 +266,44 @@ def test_closed_sessions_return_their_kv_memory(E, small_q4k_package):
         # a fresh cache reads as zeros, as the reference's cleared buffer does
         s = eng.create_session(200)
         assert s.prefill_greedy([1, 2, 3]) == eng.generate([1, 2, 3], 1).sampled_tokens[0]
+
+
+def test_large_batched_prefill_in_row_bounded_passes(E, small_q4k_package, monkeypatch):
+    """A batched prefill larger than the per-pass row bound runs as several
+    device passes (whole sequences packed together, a longer sequence cut into
+    pieces of its own): tokens and logits are bit-identical to one pass, for
+    the full model and for a stage split that hands activations on."""
+    rng = np.random.default_rng(12)
+    prompts = [rng.integers(0, 1024, n).tolist() for n in (5, 40, 17, 3, 33, 16)]
+    steps = 4
+
+    def run(eng):
+        sessions = [eng.create_session(len(p) + steps) for p in prompts]
+        cur = [r.sampled_token for r in eng.prefill_stage_batch(sessions, prompts)]
+        got = [[t] for t in cur]
+        for _ in range(steps - 1):
+            cur = [r.sampled_token for r in eng.decode_stage_batch(sessions, cur)]
+            for g, t in zip(got, cur):
+                g.append(t)
+        return got, eng.logits(prompts[1])
+
+    def split_run(a, b):
+        sa = [a.create_session(len(p) + 1) for p in prompts]
+        sb = [b.create_session(len(p) + 1) for p in prompts]
+        acts = a.prefill_stage_batch(sa, prompts)
+        return [o.sampled_token for o in b.prefill_stage_batch_activations(sb, [r.activation for r in acts])]
+
+    with E.NativeEngine(small_q4k_package, "cuda") as eng:
+        ref_tokens, ref_logits = run(eng)
+    a = E.NativeEngine(small_q4k_package, "cuda", layer_start=0, layer_end=2)
+    b = E.NativeEngine(small_q4k_package, "cuda", layer_start=2, layer_end=4)
+    ref_split = split_run(a, b)
+    assert ref_split == [t[0] for t in ref_tokens]
+    monkeypatch.setenv("JFB_MAX_PASS_ROWS", "16")
+    with E.NativeEngine(small_q4k_package, "cuda") as eng:
+        got_tokens, got_logits = run(eng)
+    a2 = E.NativeEngine(small_q4k_package, "cuda", layer_start=0, layer_end=2)
+    b2 = E.NativeEngine(small_q4k_package, "cuda", layer_start=2, layer_end=4)
+    assert split_run(a2, b2) == ref_split
+    assert got_tokens == ref_tokens
+    assert np.array_equal(got_logits.view(np.uint32), ref_logits.view(np.uint32))
