@@ -143,8 +143,10 @@ jfb_status jfb_matmul(const jfb_weight * weight, const jfb_q8k * x_q8, const flo
  * them and sums them in double. The kernel is persistent: one CTA per SM walks
  * a contiguous range of (tile, block) work (stream-K, tiles of 128 weight rows
  * x 32 activation rows for n <= 32, x 64 above). A tile shared by several CTAs
- * is finished by the last contributor, which sums the double partials in CTA
- * order. x_q8 must carry the tensor-core operands (qs_f16, bsums_f16, d_t),
+ * is finished by the last contributor: every contributor adds its double
+ * partials into the tile's workspace slot with f64 reductions, and the last
+ * one reads the sums, clears the slot and writes the outputs (double sums of
+ * the block terms are exact in any order). x_q8 must carry the tensor-core operands (qs_f16, bsums_f16, d_t),
  * all 16-byte aligned, with d_stride >= n.
  *
  * The workspace holds the partials and the per-tile arrival counters at

@@ -260,9 +260,14 @@ DeviceModel::DeviceModel(const std::string & package_path, std::uint32_t layer_s
     auto is_kq = [](std::uint32_t t) { return t == JF_TENSOR_Q4_K || t == JF_TENSOR_Q6_K || t == JF_TENSOR_Q2_K; };
     for (std::uint32_t l = layer_start_; l < layer_end_; ++l) {
         const std::string p = "blk." + std::to_string(l) + ".";
+        // (Q/K when V has another type, as on the layers whose V the Q4_K_M
+        // map keeps in Q6_K)
+        bool qkv_stacked = false;
         for (const auto & [gname, members] : std::vector<std::pair<std::string, std::vector<std::string>>>{
                  {p + "attn_qkv", {p + "attn_q.weight", p + "attn_k.weight", p + "attn_v.weight"}},
+                 {p + "attn_qk", {p + "attn_q.weight", p + "attn_k.weight"}},
                  {p + "ffn_gate_up", {p + "ffn_gate.weight", p + "ffn_up.weight"}}}) {
+            if (gname == p + "attn_qk" && qkv_stacked) continue;
             Group g;
             g.name = gname;
             g.members = members;
@@ -276,6 +281,7 @@ DeviceModel::DeviceModel(const std::string & package_path, std::uint32_t layer_s
                 g.raw_bytes += v.size;
             }
             if (!ok) continue;
+            if (gname == p + "attn_qkv") qkv_stacked = true;
             for (const std::string & m : members) grouped[m] = groups.size();
             groups.push_back(g);
         }
@@ -404,6 +410,7 @@ DeviceModel::DeviceModel(const std::string & package_path, std::uint32_t layer_s
         w.v_bias = vec(p + "attn_v.bias");
         w.ffn_norm = vec(p + "ffn_norm.weight");
         if (const auto it = fused.find(p + "attn_qkv"); it != fused.end()) w.qkv = it->second;
+        if (const auto it = fused.find(p + "attn_qk"); it != fused.end()) w.qk = it->second;
         if (const auto it = fused.find(p + "ffn_gate_up"); it != fused.end()) w.gate_up = it->second;
         layer_weights_.push_back(w);
     }
@@ -658,7 +665,7 @@ void Qwen2Stage::ensure_scratch(std::uint32_t rows, std::uint32_t seqs) {
     std::uint64_t tc = 0;
     for (std::uint32_t li = 0; li < m_.layers(); ++li) {
         const LayerWeights & lw = m_.layer(li);
-        for (const jfb_weight * x : {&lw.q, &lw.k, &lw.v, &lw.o, &lw.gate, &lw.up, &lw.down, &lw.qkv, &lw.gate_up}) {
+        for (const jfb_weight * x : {&lw.q, &lw.k, &lw.v, &lw.o, &lw.gate, &lw.up, &lw.down, &lw.qkv, &lw.qk, &lw.gate_up}) {
             if (x->type != 0) tc = std::max(tc, tc_need(*x, R));
         }
     }
@@ -887,6 +894,13 @@ void Qwen2Stage::forward_pass(std::span<const SequenceRows> seqs, const ForwardI
                      matmul_bytes(w.q, R, JFB_EPILOGUE_BIAS) + matmul_bytes(w.k, R, JFB_EPILOGUE_BIAS) +
                          matmul_bytes(w.v, R, JFB_EPILOGUE_BIAS));
             launches_ -= 2;
+        } else if (use_tc(w.qk, R)) {
+            const std::uint32_t qr = w.q.rows, kr = w.k.rows;
+            const jfb_matmul_segment segs[2] = {{qr, JFB_EPILOGUE_BIAS, w.q_bias, nullptr, q_},
+                                                {qr + kr, JFB_EPILOGUE_BIAS, w.k_bias, nullptr, k_}};
+            mm_fused(w.qk, R, segs, 2, matmul_bytes(w.q, R, JFB_EPILOGUE_BIAS) + matmul_bytes(w.k, R, JFB_EPILOGUE_BIAS));
+            mm(w.v, xf_, R, JFB_EPILOGUE_BIAS, w.v_bias, nullptr, v_);
+            launches_ -= 1;
         } else {
             mm(w.q, xf_, R, JFB_EPILOGUE_BIAS, w.q_bias, nullptr, q_);
             mm(w.k, xf_, R, JFB_EPILOGUE_BIAS, w.k_bias, nullptr, k_);

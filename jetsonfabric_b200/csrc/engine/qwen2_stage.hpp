@@ -36,8 +36,9 @@ struct Qwen2HParams {
 struct LayerWeights {
     jfb_weight q{}, k{}, v{}, o{}, gate{}, up{}, down{};
     // Q/K/V and gate/up stacked by rows when they share a K-quant type (type
-    // 0 otherwise); q, k, v, gate and up are then row views into them
-    jfb_weight qkv{}, gate_up{};
+    // 0 otherwise), or Q/K alone when only V differs; q, k, v, gate and up are
+    // then row views into them
+    jfb_weight qkv{}, qk{}, gate_up{};
     const float * attn_norm = nullptr;
     const float * q_bias = nullptr;
     const float * k_bias = nullptr;

@@ -1268,18 +1268,29 @@ __global__ void __launch_bounds__(Roles<BN>::kThreads) __maxnreg__(Roles<BN>::kR
             const uint32_t tile = cur.tile;
             if (csize == 1) {
                 if (seg_b != 0 || cur.b + 1 != nb) {
-                    // stream-K: part of a tile. Each warp writes its partials;
-                    // the last warp to arrive (per tile and warp) adds every
-                    // contributor's, in CTA order.
+                    // stream-K: part of a tile. Every contributor adds its double
+                    // partials into the tile's slot in the workspace (device-scope
+                    // f64 reductions, which return nothing to wait for); the last
+                    // warp to arrive (per tile and warp) reads the sums, clears the
+                    // slot for the next call and stores the outputs. The slot is
+                    // that of the tile's first contributor `lo`: 2 lo + 1 when lo's
+                    // range starts before the tile (the tile is lo's last), 2 lo
+                    // when it starts exactly at the tile; no CTA is the first
+                    // contributor of two split tiles, so slots are never shared.
+                    // The block terms' double sums are exact whatever the order of
+                    // the additions, as for the CPU's sequential sum.
                     const uint64_t g = gridDim.x;
-                    const uint32_t slot_p = 2 * blockIdx.x + (tile == first_tile ? 0 : 1);
-                    double * part = p.partial + uint64_t(slot_p) * (uint64_t(kRows) * BN);
-#pragma unroll
-                    for (int t = 0; t < kCols; ++t) part[(col0 + t) * kRows + m] = sum_get(t);
-                    __threadfence();
-                    __syncwarp();
                     const uint32_t lo = cta_of(uint64_t(tile) * nb, p.work, g);
                     const uint32_t hi = cta_of(uint64_t(tile + 1) * nb - 1, p.work, g);
+                    const uint64_t lo_slot =
+                        2 * uint64_t(lo) + (range_start(lo, p.work, g) == uint64_t(tile) * nb ? 0 : 1);
+                    double * slot = p.partial + lo_slot * (uint64_t(kRows) * BN) + col0 * kRows + m;
+#pragma unroll
+                    for (int t = 0; t < kCols; ++t) {
+                        asm volatile("red.global.add.f64 [%0], %1;" ::"l"(slot + t * kRows), "d"(sum_get(t)) : "memory");
+                    }
+                    __threadfence();
+                    __syncwarp();
                     uint32_t arrived = 0;
                     if (lane == 0) {
                         uint32_t * counter = p.counters + uint64_t(tile) * R::kEpiWarps + warp;
@@ -1289,29 +1300,13 @@ __global__ void __launch_bounds__(Roles<BN>::kThreads) __maxnreg__(Roles<BN>::kR
                     arrived = __shfl_sync(0xffffffffu, arrived, 0);
                     if (arrived != hi - lo + 1) continue;
                     __threadfence();
-                    // contributors after `lo` start inside this tile, so it is
-                    // their first tile (slot 2c); `lo` used slot 2lo + 1 unless
-                    // its range starts exactly at the tile
-                    const uint64_t lo_slot =
-                        2 * uint64_t(lo) + (range_start(lo, p.work, g) == uint64_t(tile) * nb ? 0 : 1);
-                    const double * lo_src = p.partial + lo_slot * (uint64_t(kRows) * BN) + col0 * kRows + m;
-                    const double * rest = p.partial + 2 * uint64_t(lo + 1) * (uint64_t(kRows) * BN) + col0 * kRows + m;
+                    double v[kCols];
 #pragma unroll
-                    for (int t0 = 0; t0 < kCols; t0 += 8) {
-                        double acc8[8];
+                    for (int t = 0; t < kCols; ++t) v[t] = __ldcg(slot + t * kRows);
 #pragma unroll
-                        for (int k = 0; k < 8; ++k) acc8[k] = 0.0 + __ldcg(lo_src + (t0 + k) * kRows);
-#pragma unroll 4
-                        for (uint32_t c = 0; c < hi - lo; ++c) {
-                            const double * src = rest + uint64_t(2 * c) * (uint64_t(kRows) * BN);
-                            double v[8];
-#pragma unroll
-                            for (int k = 0; k < 8; ++k) v[k] = __ldcg(src + (t0 + k) * kRows);
-#pragma unroll
-                            for (int k = 0; k < 8; ++k) acc8[k] += v[k];
-                        }
-#pragma unroll
-                        for (int k = 0; k < 8; ++k) sum_set(t0 + k, acc8[k]);
+                    for (int t = 0; t < kCols; ++t) {
+                        __stcg(slot + t * kRows, 0.0);
+                        sum_set(t, v[t]);
                     }
                 }
 #pragma unroll
