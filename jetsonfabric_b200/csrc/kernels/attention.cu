@@ -302,6 +302,9 @@ constexpr int kDThreads = 256;
 constexpr int kDWarps = kDThreads / 32;
 constexpr uint32_t kDMaxKeysRow8 = 512;    // KC limit with 8 rows per CTA
 constexpr uint32_t kDMaxKeysRow1 = 4096;   // KC limit with 1 row per CTA
+// KC limit with R rows per CTA (R = 1, 2, 4, 8): the score array is
+// R x 8 heads x (KC + 4) floats, about 128 KB at each limit
+__host__ __device__ constexpr uint32_t dmma_max_keys(uint32_t rows) { return kDMaxKeysRow1 / rows; }
 constexpr uint32_t kDMaxCluster = 8;       // portable cluster size
 
 __device__ __forceinline__ uint32_t cluster_rank() {
@@ -374,7 +377,8 @@ __host__ __device__ inline DmmaLayout dmma_layout(uint32_t rows, uint32_t kc, ui
     l.kc = kc;
     l.kcp = kc + 4;  // == 4 mod 8: the 8 head rows of a P fragment load hit distinct banks
     uint32_t x = rows * 8 * l.kcp * 4;
-    const uint32_t warp_partials = rows == 1 ? kDWarps * 8 * head_dim * 8 : 0;
+    // several warps per row (R < 8) add their P V partials through shared memory
+    const uint32_t warp_partials = rows < kDWarps ? kDWarps * 8 * head_dim * 8 : 0;
     const uint32_t out_rows = rows * 8 * head_dim * 4;
     x = x > warp_partials ? x : warp_partials;
     x = x > out_rows ? x : out_rows;
@@ -614,7 +618,8 @@ __global__ void __launch_bounds__(kDThreads, 1) dmma_attention_kernel(
     __syncthreads();  // every warp is done with the probabilities: the score array is reused below
 
     // ---- the CTA's partial sums [R][8][D]
-    if (R == 1) {
+    if (S > 1) {
+        // the S warps of a row add their partials in slice order
         double * wp = wpart + uint64_t(warp) * 8 * D + gq * D;
 #pragma unroll
         for (int t = 0; t < NT; ++t) {
@@ -622,9 +627,10 @@ __global__ void __launch_bounds__(kDThreads, 1) dmma_attention_kernel(
             for (int i = 0; i < 2; ++i) wp[NT * (2 * tq + i) + t] = o[t][i];
         }
         __syncthreads();
-        for (uint32_t e = threadIdx.x; e < 8 * D; e += kDThreads) {
+        for (uint32_t e = threadIdx.x; e < R * 8 * D; e += kDThreads) {
+            const uint32_t rl = e / (8 * D), at = e % (8 * D);
             double t = 0.0;
-            for (int w = 0; w < kDWarps; ++w) t += wpart[uint64_t(w) * 8 * D + e];  // warp (slice) order
+            for (uint32_t w = 0; w < S; ++w) t += wpart[uint64_t(rl * S + w) * 8 * D + at];
             octa[e] = t;
         }
     } else {
@@ -679,8 +685,17 @@ DmmaPlan dmma_plan(uint32_t n, uint32_t heads, uint32_t kv_heads, uint32_t head_
     DmmaPlan pl{};
     pl.ok = false;
     if ((head_dim != 64 && head_dim != 128) || heads / kv_heads > 8 || n == 0) return pl;
-    pl.rows = uint64_t(n) * kv_heads >= uint64_t(8) * uint64_t(sms) ? 8u : 1u;
-    const uint32_t kc_max = pl.rows == 8 ? kDMaxKeysRow8 : kDMaxKeysRow1;
+    // prefill-sized calls: as many rows per CTA as keep the longest row's keys
+    // in one CTA (8 rows up to 512 keys, 4 up to 1024, 2 up to 2048), so that
+    // no cluster CTA sits beside a partner that has all the keys of a causal
+    // row; beyond 2048 keys, 8 rows over a cluster. Decode-sized calls: 1 row.
+    if (uint64_t(n) * kv_heads >= uint64_t(8) * uint64_t(sms)) {
+        pl.rows = max_keys <= dmma_max_keys(8) ? 8u : max_keys <= dmma_max_keys(4) ? 4u
+                  : max_keys <= dmma_max_keys(2) ? 2u : 8u;
+    } else {
+        pl.rows = 1u;
+    }
+    const uint32_t kc_max = dmma_max_keys(pl.rows);
     const uint32_t c_min = (max_keys + kc_max - 1) / kc_max;
     if (c_min > kDMaxCluster) return pl;
     pl.tiles = (n + pl.rows - 1) / pl.rows;
@@ -713,7 +728,8 @@ jfb_status launch_dmma(const DmmaPlan & pl, const float * q, uint32_t n, const i
         std::lock_guard<std::mutex> lock(mu);
         if (attribute_bytes[dev] < pl.layout.total) {
             // the largest layout of any plan: one attribute for every later call
-            const uint32_t bytes = std::max<uint32_t>(pl.layout.total, dmma_layout(8, kDMaxKeysRow8, D).total);
+            uint32_t bytes = pl.layout.total;
+            for (uint32_t r = 1; r <= 8; r *= 2) bytes = std::max<uint32_t>(bytes, dmma_layout(r, dmma_max_keys(r), D).total);
             cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(bytes));
             if (e != cudaSuccess) {
                 return status_error(JFB_STATUS_CUDA_ERROR, "attention shared memory attribute: %s", cudaGetErrorString(e));

@@ -305,8 +305,11 @@ def _attention_case(K, rng, heads, kv_heads, hd, lengths, rows):
 
 @pytest.mark.parametrize("heads,kv_heads,lengths", [
     (16, 2, [300, 340]),   # 640 causal rows: 8 rows per CTA, one CTA per key range
-    (16, 2, [600, 100]),   # 700 rows, rows up to 600 keys: clusters of 2 CTAs
+    (16, 2, [600, 100]),   # 700 rows, rows up to 600 keys: 4 rows per CTA (two warps per row)
     (40, 8, [200]),        # 5 query heads per kv head: padded MMA rows, separate quantization
+    (28, 4, [900, 77]),    # the 7B heads (7 per kv head), rows up to 900 keys: 4 rows per CTA
+    (28, 4, [1100, 200]),  # rows up to 1100 keys: 2 rows per CTA (four warps per row)
+    (16, 2, [2100]),       # beyond 2048 keys: 8 rows per CTA over clusters of 5 CTAs
 ])
 def test_prefill_attention_matches_oracle(K, heads, kv_heads, lengths):
     """Every causal row of whole prompts in one call (the prefill shape)."""
