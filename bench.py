@@ -36,9 +36,10 @@ the last stage returns each micro-batch's greedy tokens to the first, and N
 micro-batches of sequences keep every stage busy. The workload is fixed as N
 grows (strong scaling); the value is its output tokens over the slowest
 rank's device time. TTFT and ITL are measured on the last stage. e2e runs
-the same pipeline through the host-buffer C ABI with host activations
-exchanged over gloo. --replicas instead gives every rank its own full-model
-replica (weak scaling, a comparison only).
+the same pipeline with the prompts copied in from pinned host memory every
+step and every sampled token copied back to host memory (wall clock, slowest
+rank). --replicas instead gives every rank its own full-model replica (weak
+scaling, a comparison only).
 """
 from __future__ import annotations
 
@@ -481,30 +482,37 @@ def run_pipeline(args, rank: int, world: int, local_rank: int) -> dict | None:
     torch.cuda.synchronize()
     dist.barrier()
 
-    # end to end: host-buffer C ABI, host activations over gloo
+    # end to end: the same pipeline through the stage API, fed from and read
+    # back to host memory. Each step the first stage copies every micro-batch's
+    # prompts from pinned host memory, and the last stage copies every sampled
+    # token to pinned host memory as it is produced; wall clock, slowest rank.
     e2e = None
     if not args.skip_e2e:
-        progress(rank, "e2e (host buffers over gloo)")
-        hgroups = PL.make_groups(world, backend="gloo", timeout_s=300)
-        PL.warm_groups(rank, world, hgroups)
-        hlink = PL.TorchLink(rank, world, hgroups)
-        hstage = PL.HostEngineStage(eng, prompts, batches, capacity=args.capacity)
+        progress(rank, "e2e (pinned host prompts in, host tokens out)")
+        host_prompts = [stage.prompt_dev[m].cpu().pin_memory() for m in range(len(batches))] if rank == 0 else []
+        host_tokens = torch.empty((O, C), dtype=torch.int32).pin_memory() if last else None
+        offsets = [mb[0] for mb in batches]
+
+        def to_host(step, m, out):
+            host_tokens[step, offsets[m]:offsets[m] + len(batches[m])].copy_(out, non_blocking=True)
+
         times = []
         for _ in range(max(1, args.steps)):
-            hstage.reset()
+            stage.reset()
+            torch.cuda.synchronize()
             dist.barrier()
             a = time.perf_counter()
-            PL.run_schedule(rank, world, batches, [P] * C, O, hstage, hlink)
+            with torch.cuda.stream(stage.stream):
+                for m, hp in enumerate(host_prompts):
+                    stage.prompt_dev[m].copy_(hp, non_blocking=True)
+                PL.run_schedule(rank, world, batches, [P] * C, O, stage, link, to_host if last else None)
+            torch.cuda.synchronize()
             times.append(time.perf_counter() - a)
-        hstage.close()
         sec = torch.tensor([statistics.mean(times)], device="cuda", dtype=torch.float64)
         dist.all_reduce(sec, op=dist.ReduceOp.MAX)
-        h = preset["embedding_length"]
-        rows = C * P + C * (O - 1)
-        hop_bytes = rows * h * 4 * (world - 1)  # f32 activations through the C ABI at every boundary
         e2e = {"value": C * O / float(sec.item()), "unit": UNIT,
-               "h2d_bytes_per_step": C * P * 4 + (O - 1) * C * 4 + hop_bytes,
-               "d2h_bytes_per_step": O * C * 4 + hop_bytes}
+               "h2d_bytes_per_step": C * P * 4, "d2h_bytes_per_step": O * C * 4,
+               "path": "stage API over the NCCL pipeline; prompts from pinned host memory, tokens to host memory"}
 
     # parity: the bounded sample through the same pipeline (one micro-batch of
     # one sequence); the first stage receives every greedy token from the last
