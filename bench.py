@@ -115,6 +115,8 @@ def parse():
     p.add_argument("--matmul-shape", choices=MATMUL_SHAPE_NAMES, default=None,
                    help="time only the tcgen05 K-quant matmul on one weight shape of the workload (profiling target)")
     p.add_argument("--matmul-rows", type=int, default=32, help="activation rows for --matmul-shape")
+    p.add_argument("--matmul-path", choices=["tensor-core", "cuda-core"], default="tensor-core",
+                   help="kernel for --matmul-shape: jfb_matmul_tc or the CUDA-core jfb_matmul (1-7 rows in the engine)")
     p.add_argument("--attention-shape", choices=["decode", "prefill"], default=None,
                    help="time only jfb_attention on the workload's decode (32 rows x 768 keys) or prefill "
                         "(32 x 512 causal rows) shape (profiling target)")
@@ -597,18 +599,26 @@ def run_matmul_shape(args) -> dict:
     K.quantize_q8k(torch.randn(n, cols, device="cuda"), q8)
     out = torch.empty(n, rows, device="cuda")
     ws = torch.zeros(K.matmul_tc_workspace_bytes(rows, cols, n), dtype=torch.uint8, device="cuda")
+    cuda_core = args.matmul_path == "cuda-core"
+
+    def launch(wt):
+        if cuda_core:
+            K.matmul(wt, n, out, x_q8=q8)
+        else:
+            K.matmul_tc(wt, n, out, q8, ws)
+
     for i in range(max(args.warmup, 0)):
-        K.matmul_tc(weights[i % copies], n, out, q8, ws)
+        launch(weights[i % copies])
     torch.cuda.synchronize()
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(2 * args.steps)]
     for i in range(args.steps):
         ev[2 * i].record()
-        K.matmul_tc(weights[i % copies], n, out, q8, ws)
+        launch(weights[i % copies])
         ev[2 * i + 1].record()
     torch.cuda.synchronize()
     us = sorted(ev[2 * i].elapsed_time(ev[2 * i + 1]) * 1000 for i in range(args.steps))
     med = us[len(us) // 2]
-    return {"kernel": "jfb_matmul_tc", "shape": args.matmul_shape, "type": t, "rows": rows, "cols": cols, "n": n,
+    return {"kernel": "jfb_matmul" if cuda_core else "jfb_matmul_tc", "shape": args.matmul_shape, "type": t, "rows": rows, "cols": cols, "n": n,
             "weight_bytes": len(raw), "launches": args.steps, "median_us": round(med, 2),
             "gbs": round(len(raw) / (med * 1e-6) / 1e9, 1), "l2": f"{copies} weight copies rotated"}
 

@@ -75,23 +75,56 @@ __device__ __forceinline__ int block_lanes_sum(int v) {
     return v;
 }
 
+// The weight bytes one lane reads for one 256-block (its 64 values plus the
+// block's scales), loaded one warp step ahead of their use so that a warp
+// keeps two steps of weight loads in flight.
+struct WRegs {
+    uint4 a, b, c, d, e;
+    uint32_t x;
+};
+
+template <uint32_t TYPE>
+__device__ __forceinline__ WRegs load_weights(const jfb_weight & w, uint64_t block, int c, bool valid) {
+    const uint8_t * p0 = static_cast<const uint8_t *>(w.plane[0]);
+    const uint8_t * p1 = static_cast<const uint8_t *>(w.plane[1]);
+    const uint8_t * p2 = static_cast<const uint8_t *>(w.plane[2]);
+    const uint4 zero = make_uint4(0, 0, 0, 0);
+    WRegs r{zero, zero, zero, zero, zero, 0u};
+    if (!valid) return r;
+    if constexpr (TYPE == JF_TENSOR_Q4_K) {
+        r.a = ldg16(p0 + block * 128 + 32 * c);
+        r.b = ldg16(p0 + block * 128 + 32 * c + 16);
+        r.c = ldg16(p1 + block * 16);
+    } else if constexpr (TYPE == JF_TENSOR_Q6_K) {
+        const int h = c >> 1, part = c & 1;
+        const uint8_t * blk = p0 + block * 192;
+        r.a = ldg16(blk + 64 * h + 32 * part);
+        r.b = ldg16(blk + 64 * h + 32 * part + 16);
+        r.c = ldg16(blk + 128 + 32 * h);
+        r.d = ldg16(blk + 128 + 32 * h + 16);
+        r.e = ldg16(p1 + block * 16);
+        r.x = uint32_t(__ldg(reinterpret_cast<const uint16_t *>(p2) + block));
+    } else {
+        const int h = c >> 1;
+        r.a = ldg16(p0 + block * 64 + 32 * h);
+        r.b = ldg16(p0 + block * 64 + 32 * h + 16);
+        r.c = ldg16(p1 + block * 16);
+        r.x = __ldg(reinterpret_cast<const uint32_t *>(p2) + block);
+    }
+    return r;
+}
+
 // One 256-block of one weight row against up to kGroup activation rows. The
 // four lanes of a block each own 64 values; their integer partial sums are
 // combined first so the block's float term is formed once, as on the CPU.
 // Every lane of the warp must call this (the shuffles are warp-wide);
 // `valid` is false for lanes whose block index is past the row end.
 template <uint32_t TYPE>
-__device__ __forceinline__ void lane_block(const jfb_weight & w, uint64_t block, int c, const ActView & a,
-                                           uint32_t b, uint32_t t0, int nt, bool valid, double * acc) {
-    const uint8_t * p0 = static_cast<const uint8_t *>(w.plane[0]);
-    const uint8_t * p1 = static_cast<const uint8_t *>(w.plane[1]);
-    const uint8_t * p2 = static_cast<const uint8_t *>(w.plane[2]);
+__device__ __forceinline__ void lane_block(const WRegs & wr, int c, const ActView & a, uint32_t b, uint32_t t0, int nt,
+                                           bool valid, double * acc) {
     const uint32_t nb = a.cols / kQK;
     if constexpr (TYPE == JF_TENSOR_Q4_K) {
-        const uint4 zero = make_uint4(0, 0, 0, 0);
-        const uint4 q0 = valid ? ldg16(p0 + block * 128 + 32 * c) : zero;
-        const uint4 q1 = valid ? ldg16(p0 + block * 128 + 32 * c + 16) : zero;
-        const uint4 hdr = valid ? ldg16(p1 + block * 16) : zero;
+        const uint4 q0 = wr.a, q1 = wr.b, hdr = wr.c;
         const float d = half_bits_to_float(uint16_t(hdr.x & 0xffffu));
         const float dmin = half_bits_to_float(uint16_t(hdr.x >> 16));
         int sc_lo, m_lo, sc_hi, m_hi;
@@ -135,14 +168,8 @@ __device__ __forceinline__ void lane_block(const jfb_weight & w, uint64_t block,
         }
     } else if constexpr (TYPE == JF_TENSOR_Q6_K) {
         const int h = c >> 1, part = c & 1;
-        const uint8_t * blk = p0 + block * 192;
-        const uint4 zero = make_uint4(0, 0, 0, 0);
-        const uint4 l0 = valid ? ldg16(blk + 64 * h + 32 * part) : zero;
-        const uint4 l1 = valid ? ldg16(blk + 64 * h + 32 * part + 16) : zero;
-        const uint4 h0 = valid ? ldg16(blk + 128 + 32 * h) : zero;
-        const uint4 h1 = valid ? ldg16(blk + 128 + 32 * h + 16) : zero;
-        const uint4 scv = valid ? ldg16(p1 + block * 16) : zero;
-        const float d = valid ? half_bits_to_float(uint16_t(p2[block * 2] | (p2[block * 2 + 1] << 8))) : 0.0f;
+        const uint4 l0 = wr.a, l1 = wr.b, h0 = wr.c, h1 = wr.d, scv = wr.e;
+        const float d = valid ? half_bits_to_float(uint16_t(wr.x)) : 0.0f;
         const uint32_t L[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
         const uint32_t H[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
         int qa[8], qb[8];
@@ -190,11 +217,8 @@ __device__ __forceinline__ void lane_block(const jfb_weight & w, uint64_t block,
         }
     } else {  // Q2_K
         const int h = c >> 1, sp = c & 1;
-        const uint4 zero = make_uint4(0, 0, 0, 0);
-        const uint4 c0 = valid ? ldg16(p0 + block * 64 + 32 * h) : zero;
-        const uint4 c1 = valid ? ldg16(p0 + block * 64 + 32 * h + 16) : zero;
-        const uint4 scv = valid ? ldg16(p1 + block * 16) : zero;
-        const uint32_t dd = valid ? __ldg(reinterpret_cast<const uint32_t *>(p2) + block) : 0u;
+        const uint4 c0 = wr.a, c1 = wr.b, scv = wr.c;
+        const uint32_t dd = wr.x;
         const float d = half_bits_to_float(uint16_t(dd & 0xffffu));
         const float dmin = half_bits_to_float(uint16_t(dd >> 16));
         const uint32_t Q[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
@@ -268,10 +292,17 @@ __global__ void __launch_bounds__(kWarps * 32) mmv_kquant_kernel(jfb_weight w, A
 #pragma unroll
     for (int t = 0; t < kGroup; ++t) acc[t] = 0.0;
     const int c = lane & 3;
-    for (uint32_t b0 = 0; b0 < nb; b0 += 8) {  // warp-uniform trip count (the block lanes shuffle)
-        const uint32_t b = b0 + uint32_t(lane >> 2);
-        const bool valid = b < nb;
-        lane_block<TYPE>(w, uint64_t(row) * nb + (valid ? b : 0), c, a, b, t0, nt, valid, acc);
+    // warp-uniform trip count (the block lanes shuffle); the next step's
+    // weights are requested before this step's arithmetic
+    uint32_t b = uint32_t(lane >> 2);
+    WRegs cur = load_weights<TYPE>(w, uint64_t(row) * nb + (b < nb ? b : 0), c, b < nb);
+    for (uint32_t b0 = 0; b0 < nb; b0 += 8) {
+        const uint32_t bn = b0 + 8 + uint32_t(lane >> 2);
+        WRegs nxt{};
+        if (b0 + 8 < nb) nxt = load_weights<TYPE>(w, uint64_t(row) * nb + (bn < nb ? bn : 0), c, bn < nb);
+        b = b0 + uint32_t(lane >> 2);
+        lane_block<TYPE>(cur, c, a, b, t0, nt, b < nb, acc);
+        cur = nxt;
     }
 #pragma unroll
     for (int t = 0; t < kGroup; ++t) {
