@@ -31,8 +31,12 @@ reference's own native engine needs GGML, which cannot be built here).
 
 With torchrun (N > 1) the same workload runs as an N-stage pipeline (one
 process and GPU per contiguous layer range, jetsonfabric_b200/pipeline.py):
-F16 activations cross each stage boundary over NCCL point-to-point (NVLink),
-the last stage returns each micro-batch's greedy tokens to the first, and N
+F16 activations cross each stage boundary over NCCL point-to-point (NVLink)
+as Stagewire v2 frames (jetsonfabric_b200/stagewire.py: payload CRC-32
+computed and stamped on the device, every received frame checked against its
+checksum on the device and against the decoder's rules on the host at the
+end of each run; --frames raw sends bare payloads), the last stage returns
+each micro-batch's greedy tokens to the first in the same frames, and N
 micro-batches of sequences keep every stage busy. The workload is fixed as N
 grows (strong scaling); the value is its output tokens over the slowest
 rank's device time. TTFT and ITL are measured on the last stage. e2e runs
@@ -112,6 +116,8 @@ def parse():
     p.add_argument("--skip-cpu", action="store_true")
     p.add_argument("--micro-batches", type=int, default=0, help="pipeline micro-batches (default: one per stage)")
     p.add_argument("--replicas", action="store_true", help="N > 1: full-model replicas instead of a pipeline")
+    p.add_argument("--frames", choices=["stagewire", "raw"], default="stagewire",
+                   help="N > 1 pipeline: stage traffic as Stagewire v2 frames (default) or bare payloads")
     p.add_argument("--matmul-shape", choices=MATMUL_SHAPE_NAMES, default=None,
                    help="time only the tcgen05 K-quant matmul on one weight shape of the workload (profiling target)")
     p.add_argument("--matmul-rows", type=int, default=32, help="activation rows for --matmul-shape")
@@ -395,12 +401,22 @@ def run_pipeline(args, rank: int, world: int, local_rank: int) -> dict | None:
     eng = E.NativeEngine(pkg, "cuda", layer_start=start, layer_end=end, device=local_rank)
     groups = PL.make_groups(world)
     PL.warm_groups(rank, world, groups, device=torch.device("cuda", local_rank))
-    link = PL.TorchLink(rank, world, groups)
+    torch_link = PL.TorchLink(rank, world, groups)
     C, P, O = args.concurrency, args.prompt_tokens, args.output_tokens
     micro = args.micro_batches or world
     batches = PL.split_batches(C, micro)
     prompts = prompts_for(args, preset["vocabulary_size"]).tolist()
     stage = PL.EngineStage(eng, prompts, batches, capacity=args.capacity)
+
+    def framed(plan_batches, lengths, steps):
+        if args.frames == "raw":
+            return torch_link
+        from jetsonfabric_b200 import stagewire as SW
+        plan = SW.FramePlan(model_id=model_name(args), stage_layers=ranges, batches=plan_batches,
+                            prompt_lengths=lengths, steps=steps, hidden=preset["embedding_length"])
+        return SW.StagewireLink(torch_link, rank, plan, device=torch.device("cuda", local_rank), stream=stage.stream)
+
+    link = framed(batches, [P] * C, O)
     last = rank == world - 1
     launches = {"n": 0}
 
@@ -524,6 +540,7 @@ def run_pipeline(args, rank: int, world: int, local_rank: int) -> dict | None:
         prompt = sample_prompt(args, preset["vocabulary_size"])
         n_out = CPU_SAMPLE["output_tokens"]
         pstage = PL.EngineStage(eng, [prompt], [[0]], capacity=len(prompt) + n_out + 1)
+        plink = framed([[0]], [len(prompt)], n_out + 1)
         received = []
         if rank == 0:
             plain = pstage.forward
@@ -535,7 +552,7 @@ def run_pipeline(args, rank: int, world: int, local_rank: int) -> dict | None:
 
             pstage.forward = recording
         with torch.cuda.stream(pstage.stream):
-            PL.run_schedule(rank, world, [[0]], [len(prompt)], n_out + 1, pstage, link)
+            PL.run_schedule(rank, world, [[0]], [len(prompt)], n_out + 1, pstage, plink)
         torch.cuda.synchronize()
         pstage.close()
         if rank == 0:
@@ -566,7 +583,8 @@ def run_pipeline(args, rank: int, world: int, local_rank: int) -> dict | None:
             "config": {"workload": workload_name(args), "model": model_name(args),
                        "concurrency": C, "prompt_tokens": P, "output_tokens": O, "global_batch": C, "seq_len": P + O,
                        "parallelism": f"pp{world}", "stages": ranges, "micro_batches": [len(b) for b in batches],
-                       "boundary": "F16 codec over NCCL send/recv (NVLink)",
+                       "boundary": ("F16 codec in Stagewire v2 frames (device CRC-32) over NCCL send/recv (NVLink)"
+                                    if args.frames == "stagewire" else "F16 codec over NCCL send/recv (NVLink)"),
                        "l2": "weights exceed L2 every decode step"},
             "ttft_p50_ms": round(float(lat[0].item()), 3), "itl_p50_ms": round(float(lat[1].item()), 4),
             "decode_tok_s": round(C / (float(lat[2].item()) / 1000.0), 1),

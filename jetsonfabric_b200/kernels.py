@@ -67,6 +67,10 @@ def _bind():
         "jfb_argmax": ([_VP, C.c_uint32, C.c_uint32, _VP, _VP], Status),
         "jfb_codec_f32_to_f16": ([_VP, _VP, C.c_uint64, _VP], Status),
         "jfb_codec_f16_to_f32": ([_VP, _VP, C.c_uint64, _VP], Status),
+        "jfb_crc32_scratch_bytes": ([C.c_uint64], C.c_uint64),
+        "jfb_crc32": ([_VP, C.c_uint64, _VP, _VP, C.c_uint64, _VP], Status),
+        "jfb_stagewire_stamp_crc": ([_VP, _VP, C.c_uint32, _VP], Status),
+        "jfb_stagewire_check_crc": ([_VP, _VP, C.c_uint32, _VP, _VP], Status),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)
@@ -195,6 +199,25 @@ def codec_f32_to_f16(x, out, stream=None):
 
 def codec_f16_to_f32(x, out, stream=None):
     check(_bind().jfb_codec_f16_to_f32(ptr(x), ptr(out), x.numel(), stream_ptr(stream)))
+
+
+def crc32_scratch_bytes(n: int) -> int:
+    return int(_bind().jfb_crc32_scratch_bytes(n))
+
+
+def crc32(data, crc_out, scratch, stream=None):
+    """crc_out[0] (a 4-byte device word) = CRC-32/IEEE of the bytes of `data`."""
+    n = data.numel() * data.element_size()
+    check(_bind().jfb_crc32(ptr(data), n, ptr(crc_out), ptr(scratch), scratch.numel() * scratch.element_size(),
+                            stream_ptr(stream)))
+
+
+def stagewire_stamp_crc(crc, frame, offset: int, stream=None):
+    check(_bind().jfb_stagewire_stamp_crc(ptr(crc), ptr(frame), offset, stream_ptr(stream)))
+
+
+def stagewire_check_crc(crc, frame, offset: int, mismatch, stream=None):
+    check(_bind().jfb_stagewire_check_crc(ptr(crc), ptr(frame), offset, ptr(mismatch), stream_ptr(stream)))
 
 
 def attention_scratch_bytes(n, heads, head_dim, max_keys) -> int:

@@ -74,7 +74,7 @@ class Stage(Protocol):
 
     def forward(self, m: int, prefill: bool, inputs): ...
 
-    def encode(self, activations): ...  # f32 -> F16 codec payload to send
+    def encode(self, activations, out=None): ...  # f32 -> F16 codec payload to send (into `out` if given)
 
     def decode(self, payload): ...  # F16 codec payload -> f32 stage input
 
@@ -86,6 +86,10 @@ class Stage(Protocol):
 
 
 class Link(Protocol):
+    def send_activation(self, stage, activations) -> None: ...  # encode and send to the next stage
+
+    def recv_activation(self, stage, rows: int): ...  # the next F16 payload from the previous stage
+
     def send_next(self, payload) -> None: ...
 
     def recv_prev(self, payload) -> None: ...
@@ -122,6 +126,14 @@ class TorchLink:
     def _drop_completed(self) -> None:
         # never blocks: a send that has not completed stays pending
         self.pending = [(w, buf) for w, buf in self.pending if not w.is_completed()]
+
+    def send_activation(self, stage, activations) -> None:
+        self.send_next(stage.encode(activations))
+
+    def recv_activation(self, stage, rows: int):
+        payload = stage.empty_payload(rows)
+        self.recv_prev(payload)
+        return payload
 
     def send_next(self, payload) -> None:
         self._drop_completed()
@@ -205,9 +217,7 @@ def run_schedule(rank: int, world: int, batches: Sequence[Sequence[int]], prompt
                     inputs = stage.empty_tokens(len(mb))
                     link.recv_tokens(inputs)
             else:
-                payload = stage.empty_payload(rows)
-                link.recv_prev(payload)
-                inputs = stage.decode(payload)
+                inputs = stage.decode(link.recv_activation(stage, rows))
             out = stage.forward(m, prefill, inputs)
             if last:
                 if on_output is not None:
@@ -220,7 +230,7 @@ def run_schedule(rank: int, world: int, batches: Sequence[Sequence[int]], prompt
                 for i, s in enumerate(mb):
                     results[s].append((results_tokens, i))
             else:
-                link.send_next(stage.encode(out))
+                link.send_activation(stage, out)
     if link is not None:
         link.flush()
     return ScheduleResult(tokens=results)
@@ -288,8 +298,9 @@ class EngineStage:
     def empty_payload(self, rows: int):
         return self.torch.empty((rows, self.hidden), dtype=self.torch.float16, device=self.device)
 
-    def encode(self, activations):
-        payload = self.torch.empty(activations.shape, dtype=self.torch.float16, device=self.device)
+    def encode(self, activations, out=None):
+        payload = out if out is not None else self.torch.empty(activations.shape, dtype=self.torch.float16,
+                                                                device=self.device)
         self.kernels.codec_f32_to_f16(activations, payload, stream=self.stream)
         return payload
 
@@ -335,8 +346,12 @@ class HostEngineStage(EngineStage):
     def empty_payload(self, rows: int):
         return self.torch.empty((rows, self.hidden), dtype=self.torch.float16)
 
-    def encode(self, activations):
-        return self.torch.from_numpy(np.ascontiguousarray(activations, dtype=np.float32).astype(np.float16))
+    def encode(self, activations, out=None):
+        payload = self.torch.from_numpy(np.ascontiguousarray(activations, dtype=np.float32).astype(np.float16))
+        if out is None:
+            return payload
+        out.copy_(payload)
+        return out
 
     def decode(self, payload):
         return payload.numpy().astype(np.float32)

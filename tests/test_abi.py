@@ -24,7 +24,8 @@ def declared_functions(header: Path) -> list[str]:
 
 def test_headers_are_all_listed():
     names = {h.name for h in HEADERS}
-    assert {"engine.h", "jfb_kernels.h", "jfb_engine.h", "jfb_model.h", "jfb_status.h", "jfb_tokenizer.h"} <= names
+    assert {"engine.h", "jfb_kernels.h", "jfb_engine.h", "jfb_model.h", "jfb_status.h", "jfb_tokenizer.h",
+            "jfb_stagewire.h"} <= names
     assert all(declared_functions(h) for h in HEADERS if h.name != "jfb_status.h")
 
 

@@ -54,8 +54,12 @@ class OracleScheduleStage:
     def empty_payload(self, rows):
         return torch.empty((rows, self.hidden), dtype=torch.float16)
 
-    def encode(self, activations):
-        return torch.from_numpy(np.ascontiguousarray(activations, dtype=np.float32).astype(np.float16))
+    def encode(self, activations, out=None):
+        payload = torch.from_numpy(np.ascontiguousarray(activations, dtype=np.float32).astype(np.float16))
+        if out is None:
+            return payload
+        out.copy_(payload)
+        return out
 
     def decode(self, payload):
         return payload.numpy().astype(np.float32)
@@ -78,26 +82,57 @@ class OracleScheduleStage:
         return np.concatenate([r["activations"] for r in outs], axis=0)
 
 
-def _rank_main(rank, world, port, package, prompts, micro, steps, out_path):
+class _CorruptingLink(pipeline.TorchLink):
+    """Flips one payload byte of the `nth` activation message it sends (a
+    wire fault planted on the host)."""
+
+    def __init__(self, rank, world, groups, nth, offset):
+        super().__init__(rank, world, groups)
+        self.nth, self.offset, self.count = nth, offset, 0
+
+    def send_next(self, payload) -> None:
+        if self.count == self.nth:
+            payload[self.offset] ^= 0x5A
+        self.count += 1
+        super().send_next(payload)
+
+
+def _rank_main(rank, world, port, package, prompts, micro, steps, out_path, framed=False, corrupt=-1):
     import torch.distributed as dist
     from oracle import binding as ob
+
+    from jetsonfabric_b200 import stagewire
 
     ob.set_threads(1)
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
     try:
         groups = pipeline.make_groups(world)
         pipeline.warm_groups(rank, world, groups)
-        link = pipeline.TorchLink(rank, world, groups)
         meta = ob.OracleStage(package)
         layers = meta.model.layer_count
+        hidden = meta.hidden
         meta.close()
-        start, end = pipeline.stage_ranges(layers, world)[rank]
-        stage = ob.OracleStage(package, start, end)
+        ranges = pipeline.stage_ranges(layers, world)
+        start, end = ranges[rank]
         batches = pipeline.split_batches(len(prompts), micro)
+        if corrupt >= 0:
+            link = _CorruptingLink(rank, world, groups, corrupt, 1024 + 3)
+        else:
+            link = pipeline.TorchLink(rank, world, groups)
+        if framed:
+            plan = stagewire.FramePlan(model_id="small-q4k", stage_layers=ranges, batches=batches,
+                                       prompt_lengths=[len(p) for p in prompts], steps=steps, hidden=hidden)
+            link = stagewire.StagewireLink(link, rank, plan)
+        stage = ob.OracleStage(package, start, end)
         capacity = max(len(p) for p in prompts) + steps
         sched = OracleScheduleStage(stage, prompts, batches, capacity)
-        res = pipeline.run_schedule(rank, world, batches, [len(p) for p in prompts], steps, sched, link)
-        if rank == world - 1:
+        try:
+            res = pipeline.run_schedule(rank, world, batches, [len(p) for p in prompts], steps, sched, link)
+        except stagewire.StagewireError as e:
+            with open(f"{out_path}.rank{rank}.err", "w") as f:
+                f.write(f"{type(e).__name__}: {e}")
+            res = None
+        if rank == world - 1 and res is not None:
             with open(out_path, "w") as f:
                 json.dump({str(k): v for k, v in pipeline.collect_tokens(res).items()}, f)
         dist.barrier()
@@ -153,3 +188,37 @@ def test_pipeline_matches_chained_stages(small_q4k_package, tmp_path, world, mic
     ref = _chained_reference(small_q4k_package, prompts, world, steps)
     assert got == ref
     assert all(len(v) == steps for v in got.values())
+
+
+@pytest.mark.parametrize("world,micro", [(2, 3), (3, 2)])
+def test_pipeline_over_stagewire_frames(small_q4k_package, tmp_path, world, micro):
+    """Every activation and returned token as a Stagewire v2 frame (host
+    checksums on gloo): same tokens as the chained reference, and every
+    received frame passes the decoder's rules at the end of the schedule."""
+    import torch.multiprocessing as mp
+
+    rng = np.random.default_rng(world * 7 + micro)
+    prompts = [rng.integers(0, 1024, n).tolist() for n in (6, 11, 4, 8)]
+    steps = 5
+    out_path = tmp_path / "tokens.json"
+    os.environ.setdefault("OMP_NUM_THREADS", "1")
+    mp.spawn(_rank_main, args=(world, _free_port(), str(small_q4k_package), prompts, micro, steps, str(out_path),
+                               True), nprocs=world, join=True)
+    assert not list(tmp_path.glob("*.err"))
+    got = {int(k): v for k, v in json.loads(out_path.read_text()).items()}
+    assert got == _chained_reference(small_q4k_package, prompts, world, steps)
+
+
+def test_stagewire_frame_corruption_is_detected(small_q4k_package, tmp_path):
+    """A payload byte flipped on the wire: the receiving stage's checksum
+    check fails the run when the schedule is verified."""
+    import torch.multiprocessing as mp
+
+    prompts = [[1, 2, 3, 4], [5, 6, 7]]
+    out_path = tmp_path / "tokens.json"
+    os.environ.setdefault("OMP_NUM_THREADS", "1")
+    mp.spawn(_rank_main, args=(2, _free_port(), str(small_q4k_package), prompts, 2, 3, str(out_path), True, 2),
+             nprocs=2, join=True)
+    errs = {p.name: p.read_text() for p in tmp_path.glob("*.err")}
+    assert list(errs) == ["tokens.json.rank1.err"], errs
+    assert errs["tokens.json.rank1.err"].startswith("ChecksumMismatch")
