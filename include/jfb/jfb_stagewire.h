@@ -49,6 +49,56 @@ jfb_status jfb_stagewire_stamp_crc(const uint32_t * crc, uint8_t * frame, uint32
 jfb_status jfb_stagewire_check_crc(const uint32_t * crc, const uint8_t * frame, uint32_t field_offset,
                                    int32_t * mismatch, void * stream);
 
+/* ---- in-box frame channel ----------------------------------------------------
+ *
+ * Carries Stagewire v2 frames between processes on one host through POSIX
+ * shared memory, in place of the reference's keep-alive HTTP connection
+ * (runtime/transport/http_stage_transport.cpp:481-599: one POST of the
+ * request frame answered by a status and a response frame). A stage server
+ * creates a named channel; callers open it by name. Each call writes the
+ * request frame in two pieces (the reference's EncodedStageFrameView prefix
+ * and payload) and waits for the server's status, a flag telling a reply
+ * frame from a JSON error body (the reference's non-Stagewire error
+ * responses), and the reply bytes. Frames are opaque here. Every wait is
+ * bounded by `timeout_ms` and ends with JFB_STATUS_TIMEOUT; one caller holds
+ * the channel at a time. Nothing here touches a GPU. */
+typedef struct jfb_frame_channel jfb_frame_channel;
+
+/* Server side: creates channel `name` ([A-Za-z0-9._-], up to 200 characters)
+ * with `capacity` bytes per direction (0: 513 MiB + 4 KiB, the largest
+ * frame the Stagewire v2 limits allow; the segment is sparse). Fails if the
+ * name is taken. */
+jfb_status jfb_frame_channel_create(const char * name, uint64_t capacity, jfb_frame_channel ** out);
+
+/* Caller side: opens channel `name`, waiting up to `timeout_ms` for a server
+ * to create it (JFB_STATUS_NOT_FOUND after that). */
+jfb_status jfb_frame_channel_open(const char * name, uint32_t timeout_ms, jfb_frame_channel ** out);
+
+/* Bytes per direction of an opened or created channel. */
+uint64_t jfb_frame_channel_capacity(const jfb_frame_channel * channel);
+
+/* Caller: sends head || body as one request and waits for the reply. On
+ * success *status is the server's status code (200, 400, 502, ...), *is_frame
+ * is 1 for a Stagewire reply frame and 0 for a JSON error body, and *reply /
+ * *reply_bytes stay valid until the next call or close on this handle. */
+jfb_status jfb_frame_channel_call(jfb_frame_channel * channel, const void * head, uint64_t head_bytes,
+                                  const void * body, uint64_t body_bytes, uint32_t timeout_ms, int32_t * status,
+                                  int32_t * is_frame, const uint8_t ** reply, uint64_t * reply_bytes);
+
+/* Server: waits up to `timeout_ms` for the next request; *frame stays valid
+ * until jfb_frame_channel_reply. */
+jfb_status jfb_frame_channel_receive(jfb_frame_channel * channel, uint32_t timeout_ms, const uint8_t ** frame,
+                                     uint64_t * frame_bytes);
+
+/* Server: answers the pending request with head || body. A reply larger than
+ * the channel becomes a 502 JSON error body. */
+jfb_status jfb_frame_channel_reply(jfb_frame_channel * channel, int32_t status, int32_t is_frame, const void * head,
+                                   uint64_t head_bytes, const void * body, uint64_t body_bytes);
+
+/* Unmaps the channel; a server's close also wakes its callers with an error
+ * and removes the name. */
+void jfb_frame_channel_close(jfb_frame_channel * channel);
+
 #ifdef __cplusplus
 }
 #endif

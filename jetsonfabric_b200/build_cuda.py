@@ -14,7 +14,7 @@ from pathlib import Path
 from .build import BUILD, CSRC, CUDA_HOME, INCLUDE, LIB, NVCC, ARCH, JFM_SOURCES, _run, _stale
 
 KERNELS = sorted((CSRC / "kernels").glob("*.cu"))
-ENGINE = sorted((CSRC / "engine").glob("*.cpp"))
+ENGINE = sorted((CSRC / "engine").glob("*.cpp")) + [CSRC / "transport" / "frame_channel.cpp"]
 
 NVCC_FLAGS = ARCH + ["-O3", "-lineinfo", "-std=c++20", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
                      f"-I{INCLUDE}", f"-I{CSRC}"]
