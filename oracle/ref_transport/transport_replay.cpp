@@ -21,6 +21,10 @@
 //       the same pass with synthetic StageWorkers called in-process.
 //   errors
 //       the transport's refusal paths, in-process servers on threads.
+//   golden
+//       frames from the reference's Stagewire encoder, one hex JSON line each.
+//   decode
+//       hex frames on stdin through the reference's request decoder.
 #include "activation/activation_codec_factory.hpp"
 #include "adapters/native_stage_executor.hpp"
 #include "inbox_stage_transport.hpp"
@@ -340,6 +344,173 @@ int errors() {
     return 0;
 }
 
+std::string hex(const std::string & bytes) {
+    static const char digits[] = "0123456789abcdef";
+    std::string out;
+    out.reserve(bytes.size() * 2);
+    for (const unsigned char c : bytes) {
+        out.push_back(digits[c >> 4]);
+        out.push_back(digits[c & 15]);
+    }
+    return out;
+}
+
+std::string unhex(const std::string & text) {
+    if (text.size() % 2 != 0) throw std::invalid_argument("odd hex length");
+    std::string out(text.size() / 2, '\0');
+    for (std::size_t i = 0; i < out.size(); ++i) {
+        out[i] = static_cast<char>(std::stoi(text.substr(2 * i, 2), nullptr, 16));
+    }
+    return out;
+}
+
+// Frames from the reference's own encoder (protocol/stage.cpp), one JSON line
+// each: the golden vectors of the Stagewire codec tests.
+int golden() {
+    rt::protocol::StageRequest base;
+    base.session_id = "session-7";
+    base.request_id = "request-7-stage-1";
+    base.model_id = "qwen2-7b";
+    base.stage_index = 1;
+    base.stage_count = 2;
+    base.node_name = "stage-1";
+    base.layer_start = 14;
+    base.layer_end = 28;
+    base.max_tokens = 256;
+    const auto emit = [](const std::string & name, const std::string & op, const std::string & frame) {
+        std::cout << "{\"name\":" << json_string(name) << ",\"operation\":" << json_string(op)
+                  << ",\"frame\":\"" << hex(frame) << "\"}\n";
+    };
+    {
+        auto r = base;
+        r.stage_index = 0;
+        r.layer_start = 0;
+        r.layer_end = 14;
+        r.payload_kind = "text";
+        r.encoding = "utf-8";
+        const std::string text = "151644 872 198";
+        r.payload.assign(text.begin(), text.end());
+        emit("text_prefill", "execute", rt::protocol::encode_stage_request(r, "execute"));
+    }
+    {
+        auto r = base;
+        r.payload_kind = "activation";
+        r.encoding.clear();
+        r.dtype = "f16";
+        r.shape = {3, 8};
+        r.byte_order = "little";
+        r.layout = "row_major";
+        for (int i = 0; i < 48; ++i) r.payload.push_back(static_cast<std::uint8_t>((i * 37 + 11) % 251));
+        emit("activation_prefill", "execute", rt::protocol::encode_stage_request(r, "execute"));
+        r.phase = "decode";
+        r.decode_step = 5;
+        r.shape = {1, 24};
+        r.deployment_id = "deployment-a";
+        r.deployment_epoch = 3;
+        r.model_sha256 = std::string(64, 'a');
+        emit("activation_decode_managed", "execute", rt::protocol::encode_stage_request(r, "execute"));
+    }
+    {
+        auto r = base;
+        r.stage_index = 0;
+        r.layer_start = 0;
+        r.layer_end = 14;
+        r.phase = "decode";
+        r.decode_step = 1;
+        r.payload_kind = "sampled_token";
+        r.encoding.clear();
+        r.dtype = "u32";
+        r.shape = {1};
+        r.byte_order = "little";
+        r.layout = "row_major";
+        r.payload = {0x37, 0x12, 0x02, 0x00};
+        emit("sampled_token_decode", "execute", rt::protocol::encode_stage_request(r, "execute"));
+        auto rb = r;
+        rb.payload_kind = "text";
+        rb.encoding = "utf-8";
+        rb.dtype.clear();
+        rb.shape.clear();
+        rb.byte_order.clear();
+        rb.layout.clear();
+        rb.payload.clear();
+        rb.rollback_tokens = 2;
+        emit("rollback", "rollback_session", rt::protocol::encode_stage_request(rb, "rollback_session"));
+        rb.rollback_tokens = 0;
+        emit("close", "close_session", rt::protocol::encode_stage_request(rb, "close_session"));
+    }
+    {
+        rt::protocol::StageResponse r;
+        r.operation = "execute";
+        r.session_id = "session-7";
+        r.request_id = "request-7-stage-1";
+        r.model_id = "qwen2-7b";
+        r.phase = "decode";
+        r.decode_step = 4;
+        r.stage_index = 1;
+        r.stage_count = 2;
+        r.node_name = "stage-1";
+        r.layer_start = 14;
+        r.layer_end = 28;
+        r.payload_kind = "sampled_token";
+        r.encoding.clear();
+        r.dtype = "u32";
+        r.shape = {1};
+        r.byte_order = "little";
+        r.layout = "row_major";
+        r.payload = {0x2a, 0, 0, 0};
+        r.bytes_in = 7168;
+        r.bytes_out = 4;
+        r.completion_tokens = 1;
+        r.execution_us = 812;
+        r.activation_decode_us = 9;
+        r.stage_total_us = 850;
+        r.message = "<42>";
+        r.token_eog = {0};
+        r.token_text_offsets = {0, 4};
+        emit("response_sampled_token", "execute", rt::protocol::encode_stage_response(r));
+        r.payload.clear();
+        r.payload_kind = "text";
+        r.encoding = "utf-8";
+        r.dtype.clear();
+        r.shape.clear();
+        r.byte_order.clear();
+        r.layout.clear();
+        r.message = "session closed";
+        r.token_eog.clear();
+        r.token_text_offsets.clear();
+        r.operation = "close_session";
+        emit("response_close", "close_session", rt::protocol::encode_stage_response(r));
+    }
+    return 0;
+}
+
+// Decodes hex frames (one per input line) with the reference's request
+// decoder; prints what it accepted or why it refused, one JSON line each.
+int decode() {
+    std::string line;
+    while (std::getline(std::cin, line)) {
+        if (line.empty()) continue;
+        try {
+            const std::string frame = unhex(line);
+            const std::string op = rt::protocol::decode_stage_operation(frame);
+            const rt::protocol::StageRequest r = rt::protocol::decode_stage_request(frame);
+            rt::protocol::validate_stage_operation(op, r.rollback_tokens);
+            std::cout << "{\"ok\":true,\"operation\":" << json_string(op) << ",\"session_id\":"
+                      << json_string(r.session_id) << ",\"request_id\":" << json_string(r.request_id)
+                      << ",\"phase\":" << json_string(r.phase) << ",\"decode_step\":" << r.decode_step
+                      << ",\"stage_index\":" << r.stage_index << ",\"layer_start\":" << r.layer_start
+                      << ",\"layer_end\":" << r.layer_end << ",\"payload_kind\":" << json_string(r.payload_kind)
+                      << ",\"dtype\":" << json_string(r.dtype) << ",\"shape\":[";
+            for (std::size_t i = 0; i < r.shape.size(); ++i) std::cout << (i ? "," : "") << r.shape[i];
+            std::cout << "],\"payload_bytes\":" << r.payload_bytes << ",\"payload_crc32\":" << r.payload_crc32
+                      << ",\"max_tokens\":" << r.max_tokens << "}\n";
+        } catch (const std::exception & e) {
+            std::cout << "{\"ok\":false,\"error\":" << json_string(e.what()) << "}\n";
+        }
+    }
+    return 0;
+}
+
 }  // namespace
 
 int main(int argc, char ** argv) {
@@ -350,6 +521,8 @@ int main(int argc, char ** argv) {
         if (mode == "generate") return generate(argc, argv);
         if (mode == "local") return local(argc, argv);
         if (mode == "errors") return errors();
+        if (mode == "golden") return golden();
+        if (mode == "decode") return decode();
         throw std::invalid_argument("unknown mode " + mode);
     } catch (const std::exception & e) {
         std::cerr << "transport replay: " << e.what() << std::endl;

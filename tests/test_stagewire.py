@@ -17,6 +17,7 @@ from __future__ import annotations
 import json
 import struct
 import zlib
+from pathlib import Path
 
 import numpy as np
 import pytest
@@ -307,3 +308,108 @@ def test_crc_combine_matches_zlib(n):
         a, b = data[:cut], data[cut:]
         joined = _mulmod(_raw(a), _xpow_bytes(len(b))) ^ _raw(b)
         assert ~(joined ^ _mulmod(0xFFFFFFFF, _xpow_bytes(n))) & 0xFFFFFFFF == zlib.crc32(data)
+
+
+# ---- against the reference runtime's own C++ codec ----------------------------------
+
+GOLDEN = Path(__file__).resolve().parent / "golden" / "stagewire_frames.jsonl"
+
+
+def _golden_frames():
+    return [json.loads(line) for line in GOLDEN.read_text().splitlines() if line.strip()]
+
+
+def test_reference_encoder_frames_decode():
+    """Frames written by the reference's C++ encoder (tests/golden/
+    make_stagewire_frames.py) decode here to what the reference's own decoder
+    read from them."""
+    frames = _golden_frames()
+    assert len(frames) == 8
+    for f in frames:
+        got = sw.unmarshal(bytes.fromhex(f["frame"]))
+        m = got.metadata
+        assert m.operation == f["operation"], f["name"]
+        ref = f.get("reference_decode")
+        if ref is not None:
+            assert ref["ok"]
+            for key in ("session_id", "request_id", "phase", "decode_step", "stage_index", "layer_start",
+                        "layer_end", "payload_kind", "dtype", "shape", "payload_bytes", "payload_crc32",
+                        "max_tokens"):
+                assert getattr(m, key) == ref[key], (f["name"], key)
+            assert zlib.crc32(got.payload) == ref["payload_crc32"]
+    by_name = {f["name"]: sw.unmarshal(bytes.fromhex(f["frame"])) for f in frames}
+    managed = by_name["activation_decode_managed"].metadata
+    assert (managed.deployment_id, managed.deployment_epoch, managed.model_sha256) == ("deployment-a", 3, "a" * 64)
+    resp = by_name["response_sampled_token"]
+    assert resp.payload == bytes([42, 0, 0, 0]) and resp.metadata.message == "<42>"
+    assert resp.metadata.token_text_offsets == [0, 4] and resp.metadata.execution_us == 812
+    assert by_name["rollback"].metadata.rollback_tokens == 2
+    # one flipped payload bit in a reference frame is refused here as well
+    bad = bytearray(bytes.fromhex(frames[1]["frame"]))
+    bad[-1] ^= 4
+    with pytest.raises(sw.ChecksumMismatch):
+        sw.unmarshal(bytes(bad))
+
+
+def _reference_decode(frames: list[bytes]) -> list[dict]:
+    import importlib.util
+    import subprocess
+
+    repo = Path(__file__).resolve().parent.parent
+    spec = importlib.util.spec_from_file_location("jfb_ref_transport_build",
+                                                  repo / "oracle" / "ref_transport" / "build.py")
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    from jetsonfabric_b200 import build_cuda
+    build_cuda.build()
+    binary = mod.build()
+    if binary is None:
+        pytest.skip("the reference tree is not on this machine and no prebuilt transport driver exists")
+    out = subprocess.run([str(binary), "decode"], input="\n".join(f.hex() for f in frames) + "\n",
+                         capture_output=True, text=True, timeout=60, check=True).stdout
+    return [json.loads(line) for line in out.splitlines() if line.strip()]
+
+
+def test_frames_made_here_decode_with_the_reference_decoder():
+    """marshal's frames and the device link's padded, stamped frames pass the
+    reference's C++ request decoder with the same fields; corrupted ones do
+    not."""
+    rng = np.random.default_rng(3)
+    frames, expect, offsets = [], [], [None]
+    md = Metadata(session_id="s-1", request_id="r-1", model_id="qwen2", stage_index=1, stage_count=2,
+                  node_name="stage-1", layer_start=14, layer_end=28, payload_kind="activation", dtype="f16",
+                  shape=[5, 16], max_tokens=64)
+    payload = rng.integers(0, 256, 160, dtype=np.uint8).tobytes()
+    frames.append(sw.marshal(Frame(md, payload)))
+    expect.append(dict(operation="execute", phase="prefill", shape=[5, 16], payload_crc32=zlib.crc32(payload)))
+    plan = sw.FramePlan(model_id="qwen2", stage_layers=[(0, 14), (14, 28)], batches=[[0, 1], [2]],
+                        prompt_lengths=[5, 3, 4], steps=3, hidden=16)
+    for step in range(plan.steps):
+        for m in range(2):
+            a, n = plan.activation(step, m, 1)
+            pre, off = sw.frame_prefix(a, n, 1024)
+            p = rng.integers(0, 256, n, dtype=np.uint8).tobytes()
+            frames.append(pre[:off] + f"{zlib.crc32(p):>10d}".encode() + pre[off + 10:] + p)
+            offsets.append(off)
+            expect.append(dict(operation="execute", phase="prefill" if step == 0 else "decode", decode_step=step,
+                               shape=[plan.rows(step, m), 16], payload_crc32=zlib.crc32(p)))
+    t, n = plan.tokens(0, 1)
+    pre, off = sw.frame_prefix(t, n, 1024)
+    frames.append(pre[:off] + f"{zlib.crc32(bytes(4)):>10d}".encode() + pre[off + 10:] + bytes(4))
+    expect.append(dict(operation="execute", payload_kind="sampled_tokens", stage_index=0, shape=[1]))
+    good = len(frames)
+    bad = bytearray(frames[1])
+    bad[-1] ^= 1
+    frames.append(bytes(bad))
+    bad = bytearray(frames[2])  # the stamped checksum's last digit changed
+    last = offsets[2] + 9
+    bad[last] = ord("0") + (bad[last] - ord("0") + 1) % 10
+    frames.append(bytes(bad))
+    res = _reference_decode(frames)
+    assert len(res) == len(frames)
+    for r, e in zip(res[:good], expect):
+        assert r["ok"], r
+        for k, v in e.items():
+            assert r[k] == v, (k, r)
+    assert not res[good]["ok"] and "checksum" in res[good]["error"]
+    assert not res[good + 1]["ok"] and "checksum" in res[good + 1]["error"]
