@@ -1,5 +1,6 @@
 /*
- * Stagewire v2 payload checksums on the device.
+ * Stagewire v2 frames between stages: payload checksums on the device, and
+ * an in-box frame channel between processes.
  *
  * A Stagewire v2 frame (reference internal/stagewire/frame.go:36-136) is a
  * 20-byte big-endian header, JSON metadata and the raw payload; the metadata
