@@ -48,6 +48,7 @@ scaling, a comparison only).
 from __future__ import annotations
 
 import argparse
+import gc
 import json
 import os
 import statistics
@@ -505,14 +506,15 @@ def run_pipeline(args, rank: int, world: int, local_rank: int) -> dict | None:
     # prompts from pinned host memory, and the last stage copies every sampled
     # token to pinned host memory as it is produced; wall clock, slowest rank.
     e2e = None
+    pinned: dict = {}
     if not args.skip_e2e:
         progress(rank, "e2e (pinned host prompts in, host tokens out)")
-        host_prompts = [stage.prompt_dev[m].cpu().pin_memory() for m in range(len(batches))] if rank == 0 else []
-        host_tokens = torch.empty((O, C), dtype=torch.int32).pin_memory() if last else None
+        pinned["prompts"] = [stage.prompt_dev[m].cpu().pin_memory() for m in range(len(batches))] if rank == 0 else []
+        pinned["tokens"] = torch.empty((O, C), dtype=torch.int32).pin_memory() if last else None
         offsets = [mb[0] for mb in batches]
 
         def to_host(step, m, out):
-            host_tokens[step, offsets[m]:offsets[m] + len(batches[m])].copy_(out, non_blocking=True)
+            pinned["tokens"][step, offsets[m]:offsets[m] + len(batches[m])].copy_(out, non_blocking=True)
 
         times = []
         for _ in range(max(1, args.steps)):
@@ -521,8 +523,10 @@ def run_pipeline(args, rank: int, world: int, local_rank: int) -> dict | None:
             dist.barrier()
             a = time.perf_counter()
             with torch.cuda.stream(stage.stream):
-                for m, hp in enumerate(host_prompts):
-                    stage.prompt_dev[m].copy_(hp, non_blocking=True)
+                # indexing, not a loop variable: no name outlives the loop
+                # holding a pinned buffer (see the engine close below)
+                for m in range(len(pinned["prompts"])):
+                    stage.prompt_dev[m].copy_(pinned["prompts"][m], non_blocking=True)
                 PL.run_schedule(rank, world, batches, [P] * C, O, stage, link, to_host if last else None)
             torch.cuda.synchronize()
             times.append(time.perf_counter() - a)
@@ -592,6 +596,12 @@ def run_pipeline(args, rank: int, world: int, local_rank: int) -> dict | None:
             "e2e": e2e, "roofline": roof, "cpu_baseline": None, "clocks": clocks.summary(),
             "gpu_launches": int(float(launch_total.item()) / max(1, args.steps) * args.steps),
         }
+    # A pinned host buffer that took part in a copy on the engine's stream
+    # records an event on that stream when it is freed: free them all while
+    # the stream still exists, before the engine closes it.
+    torch.cuda.synchronize()
+    pinned.clear()
+    gc.collect()
     stage.close()
     eng.close()
     dist.barrier()

@@ -390,8 +390,10 @@ __host__ __device__ inline DmmaLayout dmma_layout(uint32_t rows, uint32_t kc, ui
     return l;
 }
 
-template <int D>
-__global__ void __launch_bounds__(kDThreads, 1) dmma_attention_kernel(
+// MINB = 2 for decode-sized plans (one row per CTA): two CTAs per SM keep a
+// 64-sequence decode call in one wave and twice the warps of loads in flight.
+template <int D, int MINB>
+__global__ void __launch_bounds__(kDThreads, MINB) dmma_attention_kernel(
     const float * __restrict__ q, const int32_t * __restrict__ seq, const int32_t * __restrict__ pos, uint32_t n,
     uint32_t heads, uint32_t kv_heads, const jfb_kv_slot * __restrict__ slots, uint32_t layer, float scale,
     uint32_t keys_cap, uint32_t R, uint32_t KC, float * __restrict__ out, jfb_q8k q8, int quantize) {
@@ -715,11 +717,12 @@ DmmaPlan dmma_plan(uint32_t n, uint32_t heads, uint32_t kv_heads, uint32_t head_
     return pl;
 }
 
-template <int D>
-jfb_status launch_dmma(const DmmaPlan & pl, const float * q, uint32_t n, const int32_t * seq, const int32_t * pos,
-                       uint32_t heads, uint32_t kv_heads, const jfb_kv_slot * slots, uint32_t layer, float scale,
-                       uint32_t keys_cap, float * out, jfb_q8k q8, int quantize, cudaStream_t s) {
-    auto kernel = dmma_attention_kernel<D>;
+template <int D, int MINB>
+jfb_status launch_dmma_kernel(const DmmaPlan & pl, const float * q, uint32_t n, const int32_t * seq,
+                              const int32_t * pos, uint32_t heads, uint32_t kv_heads, const jfb_kv_slot * slots,
+                              uint32_t layer, float scale, uint32_t keys_cap, float * out, jfb_q8k q8, int quantize,
+                              cudaStream_t s) {
+    auto kernel = dmma_attention_kernel<D, MINB>;
     static std::mutex mu;
     static uint32_t attribute_bytes[64] = {};
     int dev = 0;
@@ -758,6 +761,18 @@ jfb_status launch_dmma(const DmmaPlan & pl, const float * q, uint32_t n, const i
                                              pl.rows, pl.kc, out, q8, quantize);
     if (e != cudaSuccess) return status_error(JFB_STATUS_CUDA_ERROR, "jfb_attention: %s", cudaGetErrorString(e));
     return launch_status("jfb_attention");
+}
+
+template <int D>
+jfb_status launch_dmma(const DmmaPlan & pl, const float * q, uint32_t n, const int32_t * seq, const int32_t * pos,
+                       uint32_t heads, uint32_t kv_heads, const jfb_kv_slot * slots, uint32_t layer, float scale,
+                       uint32_t keys_cap, float * out, jfb_q8k q8, int quantize, cudaStream_t s) {
+    if (pl.rows == 1) {
+        return launch_dmma_kernel<D, 2>(pl, q, n, seq, pos, heads, kv_heads, slots, layer, scale, keys_cap, out, q8,
+                                        quantize, s);
+    }
+    return launch_dmma_kernel<D, 1>(pl, q, n, seq, pos, heads, kv_heads, slots, layer, scale, keys_cap, out, q8,
+                                    quantize, s);
 }
 
 int device_sms() {
