@@ -190,7 +190,7 @@ def test_pipeline_matches_chained_stages(small_q4k_package, tmp_path, world, mic
     assert all(len(v) == steps for v in got.values())
 
 
-@pytest.mark.parametrize("world,micro", [(2, 3), (3, 2)])
+@pytest.mark.parametrize("world,micro", [(2, 3), (3, 2), (4, 4)])
 def test_pipeline_over_stagewire_frames(small_q4k_package, tmp_path, world, micro):
     """Every activation and returned token as a Stagewire v2 frame (host
     checksums on gloo): same tokens as the chained reference, and every
