@@ -390,8 +390,11 @@ __host__ __device__ inline DmmaLayout dmma_layout(uint32_t rows, uint32_t kc, ui
     return l;
 }
 
-// MINB = 2 for decode-sized plans (one row per CTA): two CTAs per SM keep a
-// 64-sequence decode call in one wave and twice the warps of loads in flight.
+// MINB = 2 for decode-sized plans (one row per CTA) with more CTAs than SMs:
+// two CTAs per SM keep, for example, a 64-sequence 7B decode call (256 CTAs)
+// in one wave with twice the warps of loads in flight. With fewer CTAs than
+// SMs the MINB = 1 kernel is faster (more registers, no spills, deeper load
+// ring).
 template <int D, int MINB>
 __global__ void __launch_bounds__(kDThreads, MINB) dmma_attention_kernel(
     const float * __restrict__ q, const int32_t * __restrict__ seq, const int32_t * __restrict__ pos, uint32_t n,
@@ -399,6 +402,9 @@ __global__ void __launch_bounds__(kDThreads, MINB) dmma_attention_kernel(
     uint32_t keys_cap, uint32_t R, uint32_t KC, float * __restrict__ out, jfb_q8k q8, int quantize) {
     constexpr int KS = D / 4;  // k-steps of a score (dimensions per lane)
     constexpr int NT = D / 8;  // n-tiles of P V (dimensions per lane)
+    // K / V loads in flight per warp: three steps with one CTA per SM, two
+    // with two (whose register budget is half)
+    constexpr int RING = MINB >= 2 ? 2 : 3;
     extern __shared__ __align__(16) uint8_t smem_raw[];
     const DmmaLayout lay = dmma_layout(R, KC, D);
     float * xs = reinterpret_cast<float *>(smem_raw);                                // [R][8][kcp]
@@ -508,15 +514,17 @@ __global__ void __launch_bounds__(kDThreads, MINB) dmma_attention_kernel(
             }
             mx = fmaxf(mx, fmaxf(x0, x1));
         };
-        // K rows of three groups in flight per warp (a ring of register buffers)
-        uint4 kb[3][KS / 8];
-        load_k(g_begin, kb[0]);
-        if (g_begin + 1 < g_end) load_k(g_begin + 1, kb[1]);
-        for (uint32_t g = g_begin; g < g_end; g += 3) {
+        // K rows of RING groups in flight per warp (a ring of register buffers)
+        uint4 kb[RING][KS / 8];
 #pragma unroll
-            for (int u = 0; u < 3; ++u) {
+        for (int u = 0; u < RING - 1; ++u) {
+            if (g_begin + u < g_end) load_k(g_begin + u, kb[u]);
+        }
+        for (uint32_t g = g_begin; g < g_end; g += RING) {
+#pragma unroll
+            for (int u = 0; u < RING; ++u) {
                 if (g + u >= g_end) break;
-                if (g + u + 2 < g_end) load_k(g + u + 2, kb[(u + 2) % 3]);
+                if (g + u + RING - 1 < g_end) load_k(g + u + RING - 1, kb[(u + RING - 1) % RING]);
                 score_group(g + u, kb[u]);
             }
         }
@@ -603,16 +611,18 @@ __global__ void __launch_bounds__(kDThreads, MINB) dmma_attention_kernel(
                 }
             }
         };
-        // V rows of three key steps in flight per warp
-        uint4 vb[3][NT / 8];
-        if (k_begin < k_end) load_v(k_begin, vb[0]);
-        if (k_begin + 4 < k_end) load_v(k_begin + 4, vb[1]);
-        for (uint32_t kk = k_begin; kk < k_end; kk += 12) {
+        // V rows of RING key steps in flight per warp
+        uint4 vb[RING][NT / 8];
 #pragma unroll
-            for (int u = 0; u < 3; ++u) {
+        for (int u = 0; u < RING - 1; ++u) {
+            if (k_begin + 4 * uint32_t(u) < k_end) load_v(k_begin + 4 * uint32_t(u), vb[u]);
+        }
+        for (uint32_t kk = k_begin; kk < k_end; kk += 4 * RING) {
+#pragma unroll
+            for (int u = 0; u < RING; ++u) {
                 const uint32_t k = kk + 4 * uint32_t(u);
                 if (k >= k_end) break;
-                if (k + 8 < k_end) load_v(k + 8, vb[(u + 2) % 3]);
+                if (k + 4 * (RING - 1) < k_end) load_v(k + 4 * (RING - 1), vb[(u + RING - 1) % RING]);
                 pv_step(k, vb[u]);
             }
         }
@@ -679,6 +689,7 @@ __global__ void __launch_bounds__(kDThreads, MINB) dmma_attention_kernel(
 
 struct DmmaPlan {
     bool ok;
+    bool two_per_sm;  // the MINB = 2 kernel: one-row CTAs that would not fit in one wave at one per SM
     uint32_t rows, kc, cluster, tiles;
     DmmaLayout layout;
 };
@@ -713,6 +724,7 @@ DmmaPlan dmma_plan(uint32_t n, uint32_t heads, uint32_t kv_heads, uint32_t head_
     if (pl.kc > kc_max) return pl;
     pl.layout = dmma_layout(pl.rows, pl.kc, head_dim);
     if (uint64_t(pl.tiles) * pl.cluster > 0x7fffffffu || kv_heads > 65535u) return pl;
+    pl.two_per_sm = pl.rows == 1 && uint64_t(pl.tiles) * pl.cluster * kv_heads > uint64_t(sms);
     pl.ok = true;
     return pl;
 }
@@ -767,7 +779,7 @@ template <int D>
 jfb_status launch_dmma(const DmmaPlan & pl, const float * q, uint32_t n, const int32_t * seq, const int32_t * pos,
                        uint32_t heads, uint32_t kv_heads, const jfb_kv_slot * slots, uint32_t layer, float scale,
                        uint32_t keys_cap, float * out, jfb_q8k q8, int quantize, cudaStream_t s) {
-    if (pl.rows == 1) {
+    if (pl.two_per_sm) {
         return launch_dmma_kernel<D, 2>(pl, q, n, seq, pos, heads, kv_heads, slots, layer, scale, keys_cap, out, q8,
                                         quantize, s);
     }

@@ -324,3 +324,13 @@ def test_long_decode_attention_matches_oracle(K, positions):
     rng = np.random.default_rng(len(positions))
     lengths = [p + 1 for p in positions]
     _attention_case(K, rng, 16, 2, 128, lengths, list(enumerate(positions)))
+
+
+@pytest.mark.parametrize("n_rows", [64, 40, 30])
+def test_wide_decode_attention_matches_oracle(K, n_rows):
+    """Decode rows at the 7B heads (7 per kv head): 64 and 40 rows give more
+    one-row CTAs than SMs (the two-per-SM kernel), 30 rows fewer."""
+    rng = np.random.default_rng(n_rows)
+    positions = rng.integers(0, 1200, n_rows).tolist()
+    lengths = [p + 1 for p in positions]
+    _attention_case(K, rng, 28, 4, 128, lengths, list(enumerate(positions)))
