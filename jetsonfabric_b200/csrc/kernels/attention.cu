@@ -455,8 +455,11 @@ __global__ void __launch_bounds__(kDThreads, MINB) dmma_attention_kernel(
         // previous kernel finishes. The newest row may still be in flight
         // from that kernel; a prefetch cannot make it stale, as L2 is the
         // point every SM's stores reach and the rows are read after the wait.
+        // With two CTAs per SM all CTAs are resident at once and their whole
+        // caches can exceed L2, so those prefetch only their first 256 keys.
         constexpr uint32_t kLines = (D * 2 + 127) / 128;
-        for (uint32_t i = threadIdx.x; i < nk * kLines; i += kDThreads) {
+        const uint32_t npre = MINB >= 2 ? min(nk, 256u) : nk;
+        for (uint32_t i = threadIdx.x; i < npre * kLines; i += kDThreads) {
             const uint64_t at = uint64_t(kc0 + i / kLines) * kvd + (i % kLines) * 64;
             asm volatile("prefetch.global.L2 [%0];" ::"l"(kbase + at));
             asm volatile("prefetch.global.L2 [%0];" ::"l"(vbase + at));
