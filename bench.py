@@ -117,6 +117,9 @@ def parse():
     p.add_argument("--skip-cpu", action="store_true")
     p.add_argument("--micro-batches", type=int, default=0, help="pipeline micro-batches (default: one per stage)")
     p.add_argument("--replicas", action="store_true", help="N > 1: full-model replicas instead of a pipeline")
+    p.add_argument("--cpu-full", action="store_true", default=None,
+                   help="--impl reference: serve the whole workload on the CPU oracle instead of the bounded sample "
+                        "(default for --preset 1.5b, the configuration the reference times end to end on CPU)")
     p.add_argument("--frames", choices=["stagewire", "raw"], default="stagewire",
                    help="N > 1 pipeline: stage traffic as Stagewire v2 frames (default) or bare payloads")
     p.add_argument("--matmul-shape", choices=MATMUL_SHAPE_NAMES, default=None,
@@ -134,6 +137,8 @@ def parse():
     a.output_tokens = ot if a.output_tokens is None else a.output_tokens
     need = a.prompt_tokens + a.output_tokens - 1
     a.capacity = max(need, cap) if a.capacity is None else max(need, a.capacity)
+    if a.cpu_full is None:
+        a.cpu_full = a.preset == "1.5b"
     return a
 
 
@@ -346,9 +351,18 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
             threads = os.cpu_count() or 1
             runner = OracleRunner(pkg, threads)
             res = runner.sample(prompt)
+            full = None
+            if args.cpu_full and not args.skip_cpu and world == 1:
+                full = reference_full_workload(args, runner)
             runner.close()
             parity = None if args.skip_parity else parity_line(gpu_tokens, res["tokens"])
             cpu = None if (args.skip_cpu or world > 1) else cpu_line(args, res, threads)
+            if full is not None:
+                cpu = {"value": round(C * O / full["seconds"], 4), "unit": UNIT, "cores": threads, "kind": "port",
+                       "ttft_ms": round(full["ttft_s"] * 1000, 1),
+                       "itl_p50_ms": round(statistics.median(full["gaps_s"]) * 1000, 2) if full["gaps_s"] else None,
+                       "sample": f"the whole {workload_name(args)} workload once (CPU oracle, OpenMP over "
+                                 f"{threads} threads); value = output tokens / wall time"}
         result = {
             "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_per_step, 3), "higher_is_better": True,
@@ -777,12 +791,57 @@ def gpu_sample_tokens(eng, prompt: list[int]) -> list[int]:
     return tokens
 
 
+def reference_full_workload(args, runner: "OracleRunner") -> dict:
+    """One pass of the whole configured workload on the CPU oracle: every
+    sequence's prompt, then output_tokens - 1 decode rounds over all
+    sequences (the reference's CPU backend serving C concurrent requests on
+    the host cores). Returns total seconds, time to the last first token, and
+    the per-round gaps."""
+    prompts = prompts_for(args, PRESETS[args.preset]["vocabulary_size"]).tolist()
+    P, O = args.prompt_tokens, args.output_tokens
+    sessions = [runner.stage.session(P + O) for _ in prompts]
+    t0 = time.perf_counter()
+    tokens = [[s.forward(True, tokens=p)["token"]] for s, p in zip(sessions, prompts)]
+    ttft = time.perf_counter() - t0
+    gaps = []
+    for _ in range(O - 1):
+        b = time.perf_counter()
+        for s, tk in zip(sessions, tokens):
+            tk.append(s.forward(False, tokens=[tk[-1]])["token"])
+        gaps.append(time.perf_counter() - b)
+    total = time.perf_counter() - t0
+    del sessions
+    return {"seconds": total, "ttft_s": ttft, "gaps_s": gaps}
+
+
 def run_reference(args, rank: int) -> dict | None:
     if rank != 0:
         return None
     pkg = ensure_package(args, 0)
     threads = os.cpu_count() or 1
     runner = OracleRunner(pkg, threads)
+    if args.cpu_full:
+        for _ in range(max(args.warmup, 0)):
+            reference_full_workload(args, runner)
+        results = [reference_full_workload(args, runner) for _ in range(args.steps)]
+        runner.close()
+        seconds = statistics.mean(r["seconds"] for r in results)
+        value = args.concurrency * args.output_tokens / seconds
+        gaps = [g for r in results for g in r["gaps_s"]]
+        return {
+            "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(seconds * 1000, 1), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": DTYPE, "impl": "reference",
+            "data": "synthetic (seeded N(0,0.02) weights, uniform-random prompt ids)",
+            "config": {"workload": workload_name(args), "model": model_name(args), "mode": "whole workload",
+                       "note": "the reference's GGML CPU backend cannot be built offline, so its C restatement "
+                               "(oracle/) serves every sequence end to end on the host cores"},
+            "ttft_p50_ms": round(statistics.median(r["ttft_s"] for r in results) * 1000, 1),
+            "itl_p50_ms": round(statistics.median(gaps) * 1000, 2) if gaps else None,
+            "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": threads, "kind": "port",
+                             "sample": f"the whole {workload_name(args)} workload, every step"},
+            "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }
     prompt = sample_prompt(args, PRESETS[args.preset]["vocabulary_size"])
     for _ in range(max(args.warmup, 0)):
         runner.sample(prompt)
