@@ -19,7 +19,9 @@
 // and returns JFB_STATUS_TIMEOUT. One caller at a time holds the channel (a
 // lock word in the header, also waited on with a bound); a caller that gave up
 // waiting leaves its request behind, and the next caller discards that
-// request's late reply by its sequence number.
+// request's late reply by its sequence number. A lock whose holder process has
+// exited is taken over, and so is the name of a server that exited without
+// closing its channel.
 #include "jfb/jfb_stagewire.h"
 
 #include <linux/futex.h>
@@ -27,6 +29,7 @@
 #include <sys/stat.h>
 #include <sys/syscall.h>
 #include <fcntl.h>
+#include <signal.h>
 #include <unistd.h>
 
 #include <atomic>
@@ -43,7 +46,7 @@
 namespace {
 
 constexpr uint32_t kMagic = 0x4A464348u;  // "JFCH"
-constexpr uint32_t kVersion = 1;
+constexpr uint32_t kVersion = 2;
 constexpr uint64_t kHeaderBytes = 4096;
 constexpr uint64_t kDefaultCapacity = (512ull << 20) + (1ull << 20) + 4096;  // max payload + max metadata + header
 
@@ -55,6 +58,7 @@ struct alignas(64) Header {
     uint64_t capacity;
     alignas(64) std::atomic<uint32_t> state;
     alignas(64) std::atomic<uint32_t> caller;  // 0 = free, else the holder's pid
+    std::atomic<uint32_t> server_pid;          // the creating process, for stale-name takeover
     alignas(64) uint64_t request_seq;
     uint64_t request_bytes;
     uint64_t reply_seq;
@@ -100,6 +104,29 @@ void futex_wait(std::atomic<uint32_t> * word, uint32_t seen, Clock::time_point d
 }
 
 std::string shm_name(const char * name) { return std::string("/jfb-stage-") + name; }
+
+// A process that no longer exists (it cannot answer or release anything).
+bool process_gone(uint32_t pid) { return pid != 0 && kill(static_cast<pid_t>(pid), 0) != 0 && errno == ESRCH; }
+
+// An existing segment named `path` whose creating server has exited without
+// closing it: removes the name so that a new server can take it.
+bool unlink_if_stale(const std::string & path) {
+    const int fd = shm_open(path.c_str(), O_RDWR, 0);
+    if (fd < 0) return errno == ENOENT;
+    struct stat st;
+    bool stale = false;
+    if (fstat(fd, &st) == 0 && static_cast<uint64_t>(st.st_size) >= kHeaderBytes) {
+        void * p = mmap(nullptr, kHeaderBytes, PROT_READ, MAP_SHARED, fd, 0);
+        if (p != MAP_FAILED) {
+            const auto * h = static_cast<const Header *>(p);
+            stale = process_gone(h->server_pid.load(std::memory_order_acquire));
+            munmap(p, kHeaderBytes);
+        }
+    }
+    close(fd);
+    if (stale) shm_unlink(path.c_str());
+    return stale;
+}
 
 bool valid_name(const char * name) {
     if (name == nullptr || name[0] == '\0' || std::strlen(name) > 200) return false;
@@ -147,10 +174,15 @@ extern "C" jfb_status jfb_frame_channel_create(const char * name, uint64_t capac
     if (capacity == 0) capacity = kDefaultCapacity;
     capacity = (capacity + 4095) / 4096 * 4096;
     const std::string path = shm_name(name);
-    const int fd = shm_open(path.c_str(), O_CREAT | O_EXCL | O_RDWR, 0600);
+    int fd = shm_open(path.c_str(), O_CREAT | O_EXCL | O_RDWR, 0600);
+    int err = fd < 0 ? errno : 0;
+    if (fd < 0 && err == EEXIST && unlink_if_stale(path)) {
+        fd = shm_open(path.c_str(), O_CREAT | O_EXCL | O_RDWR, 0600);
+        err = fd < 0 ? errno : 0;
+    }
     if (fd < 0) {
-        return fail(errno == EEXIST ? JFB_STATUS_INVALID_ARGUMENT : JFB_STATUS_IO_ERROR,
-                    "could not create stage channel %s: %s", name, std::strerror(errno));
+        return fail(err == EEXIST ? JFB_STATUS_INVALID_ARGUMENT : JFB_STATUS_IO_ERROR,
+                    "could not create stage channel %s: %s", name, std::strerror(err));
     }
     const uint64_t bytes = kHeaderBytes + 2 * capacity;
     if (ftruncate(fd, static_cast<off_t>(bytes)) != 0) {
@@ -180,6 +212,7 @@ extern "C" jfb_status jfb_frame_channel_create(const char * name, uint64_t capac
     ch->header->version = kVersion;
     ch->header->state.store(kIdle, std::memory_order_relaxed);
     ch->header->caller.store(0, std::memory_order_relaxed);
+    ch->header->server_pid.store(static_cast<uint32_t>(getpid()), std::memory_order_relaxed);
     std::atomic_thread_fence(std::memory_order_release);
     reinterpret_cast<std::atomic<uint32_t> *>(&ch->header->magic)->store(kMagic, std::memory_order_release);
     *out = ch;
@@ -253,12 +286,13 @@ extern "C" jfb_status jfb_frame_channel_call(jfb_frame_channel * ch, const void 
     }
     const auto deadline = Clock::now() + std::chrono::milliseconds(timeout_ms);
     const uint32_t me = static_cast<uint32_t>(getpid());
-    // the channel's caller lock
+    // the channel's caller lock; a holder that has exited is replaced
     for (;;) {
-        uint32_t free_word = 0;
-        if (h->caller.compare_exchange_strong(free_word, me, std::memory_order_acquire)) break;
+        uint32_t holder = 0;
+        if (h->caller.compare_exchange_strong(holder, me, std::memory_order_acquire)) break;
+        if (process_gone(holder) && h->caller.compare_exchange_strong(holder, me, std::memory_order_acquire)) break;
         if (Clock::now() >= deadline) return fail(JFB_STATUS_TIMEOUT, "stage channel %s is busy", ch->name.c_str());
-        futex_wait(&h->caller, free_word, std::min(deadline, Clock::now() + std::chrono::milliseconds(2)));
+        futex_wait(&h->caller, holder, std::min(deadline, Clock::now() + std::chrono::milliseconds(2)));
     }
     const auto release = [&] {
         h->caller.store(0, std::memory_order_release);

@@ -747,3 +747,110 @@ class StagewireLink:
                                  f"(request {md.request_id!r}, stage {md.stage_index})")
         self.verified = hi
         return hi - lo
+
+
+# ---- the in-box frame channel (include/jfb/jfb_stagewire.h) -----------------------
+
+JFB_STATUS_TIMEOUT = 9
+
+
+class ChannelTimeout(TimeoutError):
+    """A bounded wait of the frame channel gave up."""
+
+
+class FrameChannel:
+    """ctypes binding of `jfb_frame_channel_*`: Stagewire frames between
+    processes on one host through shared memory. `FrameChannel.create(name)`
+    is the server side (`receive` / `reply`), `FrameChannel.open(name)` the
+    caller side (`call`). Needs no GPU."""
+
+    _bound = None
+
+    def __init__(self, handle, server: bool):
+        self._h, self.server = handle, server
+
+    @classmethod
+    def _lib(cls):
+        if cls._bound is None:
+            import ctypes as C
+
+            from .engine import Status, lib
+
+            L = lib()
+            vp, u64, u32, i32 = C.c_void_p, C.c_uint64, C.c_uint32, C.c_int32
+            sig = {
+                "jfb_frame_channel_create": ([C.c_char_p, u64, C.POINTER(vp)], Status),
+                "jfb_frame_channel_open": ([C.c_char_p, u32, C.POINTER(vp)], Status),
+                "jfb_frame_channel_capacity": ([vp], u64),
+                "jfb_frame_channel_call": ([vp, C.c_char_p, u64, C.c_char_p, u64, u32, C.POINTER(i32), C.POINTER(i32),
+                                            C.POINTER(C.POINTER(C.c_uint8)), C.POINTER(u64)], Status),
+                "jfb_frame_channel_receive": ([vp, u32, C.POINTER(C.POINTER(C.c_uint8)), C.POINTER(u64)], Status),
+                "jfb_frame_channel_reply": ([vp, i32, i32, C.c_char_p, u64, C.c_char_p, u64], Status),
+                "jfb_frame_channel_close": ([vp], None),
+            }
+            for name, (args, res) in sig.items():
+                fn = getattr(L, name)
+                fn.argtypes, fn.restype = args, res
+            cls._bound = L
+        return cls._bound
+
+    @staticmethod
+    def _check(st) -> None:
+        from .engine import check
+
+        if st.code == JFB_STATUS_TIMEOUT:
+            raise ChannelTimeout(st.message.decode(errors="replace"))
+        check(st)
+
+    @classmethod
+    def create(cls, name: str, capacity: int = 0) -> "FrameChannel":
+        import ctypes as C
+
+        h = C.c_void_p()
+        cls._check(cls._lib().jfb_frame_channel_create(name.encode(), capacity, C.byref(h)))
+        return cls(h, True)
+
+    @classmethod
+    def open(cls, name: str, timeout_ms: int = 5000) -> "FrameChannel":
+        import ctypes as C
+
+        h = C.c_void_p()
+        cls._check(cls._lib().jfb_frame_channel_open(name.encode(), timeout_ms, C.byref(h)))
+        return cls(h, False)
+
+    @property
+    def capacity(self) -> int:
+        return int(self._lib().jfb_frame_channel_capacity(self._h))
+
+    def call(self, head: bytes, body: bytes = b"", timeout_ms: int = 5000) -> tuple[int, bool, bytes]:
+        """Sends head || body; returns (status, is_frame, reply bytes)."""
+        import ctypes as C
+
+        status, is_frame = C.c_int32(), C.c_int32()
+        reply, n = C.POINTER(C.c_uint8)(), C.c_uint64()
+        self._check(self._lib().jfb_frame_channel_call(self._h, head, len(head), body, len(body), timeout_ms,
+                                                       C.byref(status), C.byref(is_frame), C.byref(reply),
+                                                       C.byref(n)))
+        return status.value, bool(is_frame.value), C.string_at(reply, n.value) if n.value else b""
+
+    def receive(self, timeout_ms: int = 5000) -> bytes:
+        import ctypes as C
+
+        frame, n = C.POINTER(C.c_uint8)(), C.c_uint64()
+        self._check(self._lib().jfb_frame_channel_receive(self._h, timeout_ms, C.byref(frame), C.byref(n)))
+        return C.string_at(frame, n.value) if n.value else b""
+
+    def reply(self, status: int, is_frame: bool, head: bytes, body: bytes = b"") -> None:
+        self._check(self._lib().jfb_frame_channel_reply(self._h, status, 1 if is_frame else 0, head, len(head),
+                                                        body, len(body)))
+
+    def close(self) -> None:
+        if self._h:
+            self._lib().jfb_frame_channel_close(self._h)
+            self._h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
