@@ -53,7 +53,7 @@ constexpr uint64_t kDefaultCapacity = (512ull << 20) + (1ull << 20) + 4096;  // 
 enum : uint32_t { kIdle = 0, kRequest = 1, kReply = 2, kClosed = 3 };
 
 struct alignas(64) Header {
-    uint32_t magic;
+    alignas(4) uint32_t magic;  // written last by the server, through std::atomic_ref
     uint32_t version;
     uint64_t capacity;
     alignas(64) std::atomic<uint32_t> state;
@@ -214,7 +214,7 @@ extern "C" jfb_status jfb_frame_channel_create(const char * name, uint64_t capac
     ch->header->caller.store(0, std::memory_order_relaxed);
     ch->header->server_pid.store(static_cast<uint32_t>(getpid()), std::memory_order_relaxed);
     std::atomic_thread_fence(std::memory_order_release);
-    reinterpret_cast<std::atomic<uint32_t> *>(&ch->header->magic)->store(kMagic, std::memory_order_release);
+    std::atomic_ref<uint32_t>(ch->header->magic).store(kMagic, std::memory_order_release);
     *out = ch;
     return ok();
 }
@@ -238,7 +238,7 @@ extern "C" jfb_status jfb_frame_channel_open(const char * name, uint32_t timeout
                 if (p == MAP_FAILED) return fail(JFB_STATUS_IO_ERROR, "could not map stage channel %s", name);
                 auto * h = static_cast<Header *>(p);
                 const uint32_t magic =
-                    reinterpret_cast<std::atomic<uint32_t> *>(&h->magic)->load(std::memory_order_acquire);
+                    std::atomic_ref<uint32_t>(h->magic).load(std::memory_order_acquire);
                 if (magic == kMagic && h->version == kVersion &&
                     kHeaderBytes + 2 * h->capacity == static_cast<uint64_t>(st.st_size)) {
                     auto * ch = new (std::nothrow) jfb_frame_channel();
