@@ -18,6 +18,29 @@ namespace {
 constexpr int kThreads = 256;
 constexpr int kMaxRowChunks = 32;  // rows up to 8192 values
 
+__device__ __forceinline__ bool aligned16(const void * p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Eight consecutive floats at a 16-byte aligned address, as two vectors.
+__device__ __forceinline__ void load8(const float * p, float (&v)[8]) {
+    const float4 a = reinterpret_cast<const float4 *>(p)[0], b = reinterpret_cast<const float4 *>(p)[1];
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
+// row[col .. col + 8) = v, clipped to the row length; two vectors when the
+// whole group is inside a row that starts 16-byte aligned.
+__device__ __forceinline__ void store8(float * row, uint32_t col, uint32_t cols, bool vec, const float (&v)[8]) {
+    if (vec && col + 8 <= cols) {
+        reinterpret_cast<float4 *>(row + col)[0] = make_float4(v[0], v[1], v[2], v[3]);
+        reinterpret_cast<float4 *>(row + col)[1] = make_float4(v[4], v[5], v[6], v[7]);
+        return;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        if (col + j < cols) row[col + j] = v[j];
+    }
+}
+
 __device__ __forceinline__ double block_sum_double(double v, double * shared) {
     v = warp_sum(v);
     if ((threadIdx.x & 31) == 0) shared[threadIdx.x >> 5] = v;
@@ -48,12 +71,21 @@ __global__ void __launch_bounds__(kThreads) rmsnorm_quant_kernel(
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     // the norm weight is written by no earlier kernel: its loads overlap the
     // wait for the previous one
+    // whole 8-value groups move as two 16-byte vectors when every row starts
+    // 16-byte aligned (aligned buffers, a row length that is a multiple of 4);
+    // otherwise, and for ragged tails, element by element. The arithmetic and
+    // its order are the same either way.
+    const bool vec = (cols & 3u) == 0 && aligned16(x) && aligned16(w) && aligned16(out_f32);
     float wv[kRounds][8];
 #pragma unroll
     for (int c = 0; c < kRounds; ++c) {
         const uint32_t base = uint32_t(warp + 8 * c) * kQK + 8 * lane;
+        if (vec && base + 8 <= cols) {
+            load8(w + base, wv[c]);
+        } else {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) wv[c][j] = base + j < cols ? w[base + j] : 0.0f;
+            for (int j = 0; j < 8; ++j) wv[c][j] = base + j < cols ? w[base + j] : 0.0f;
+        }
     }
     pdl_wait();
     const uint32_t row = blockIdx.x;
@@ -64,11 +96,15 @@ __global__ void __launch_bounds__(kThreads) rmsnorm_quant_kernel(
 #pragma unroll
     for (int c = 0; c < kRounds; ++c) {
         const uint32_t base = uint32_t(warp + 8 * c) * kQK + 8 * lane;
+        if (vec && base + 8 <= cols) {
+            load8(xr + base, v[c]);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[c][j] = base + j < cols ? xr[base + j] : 0.0f;
+        }
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-            const uint32_t i = base + j;
-            v[c][j] = i < cols ? xr[i] : 0.0f;
-            if (i < cols) sq += double(__fmul_rn(v[c][j], v[c][j]));
+            if (base + j < cols) sq += double(__fmul_rn(v[c][j], v[c][j]));
         }
     }
     const double sum = block_sum_double(sq, red);
@@ -82,10 +118,9 @@ __global__ void __launch_bounds__(kThreads) rmsnorm_quant_kernel(
         Vals8 y;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-            const uint32_t i = base + j;
-            y.v[j] = i < cols ? __fmul_rn(__fmul_rn(v[c][j], scale), wv[c][j]) : 0.0f;
-            if (out_f32 != nullptr && i < cols) out_f32[uint64_t(row) * cols + i] = y.v[j];
+            y.v[j] = base + j < cols ? __fmul_rn(__fmul_rn(v[c][j], scale), wv[c][j]) : 0.0f;
         }
+        if (out_f32 != nullptr) store8(out_f32 + uint64_t(row) * cols, base, cols, vec, y.v);
         if (quantize) q8k_block_warp(y, q8_dest(q8, row, blk, cols / kQK));
     }
 }
@@ -124,15 +159,27 @@ __global__ void __launch_bounds__(kThreads) swiglu_quant_kernel(const float * __
     pdl_wait();
     const uint32_t blk = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (blk * kQK >= cols) return;  // warp-uniform
+    const uint32_t col = blk * kQK + 8 * lane;
+    // two 16-byte vectors per 8 values when every row starts 16-byte aligned
+    const bool vec = (cols & 3u) == 0 && aligned16(gate) && aligned16(up) && aligned16(out_f32);
     for (uint32_t row = blockIdx.y; row < n; row += gridDim.y) {
-        const uint64_t base = uint64_t(row) * cols + blk * kQK + 8 * lane;
+        const uint64_t rbase = uint64_t(row) * cols;
+        float g[8], u[8];
+        if (vec && col + 8 <= cols) {
+            load8(gate + rbase + col, g);
+            load8(up + rbase + col, u);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const bool in = col + j < cols;
+                g[j] = in ? gate[rbase + col + j] : 0.0f;
+                u[j] = in ? up[rbase + col + j] : 0.0f;
+            }
+        }
         Vals8 y;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const bool in = blk * kQK + 8 * lane + j < cols;
-            y.v[j] = in ? swiglu(gate[base + j], up[base + j]) : 0.0f;
-            if (out_f32 != nullptr && in) out_f32[base + j] = y.v[j];
-        }
+        for (int j = 0; j < 8; ++j) y.v[j] = col + j < cols ? swiglu(g[j], u[j]) : 0.0f;
+        if (out_f32 != nullptr) store8(out_f32 + rbase, col, cols, vec, y.v);
         if (quantize) q8k_block_warp(y, q8_dest(q8, row, blk, cols / kQK));
     }
 }

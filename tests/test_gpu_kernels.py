@@ -82,7 +82,7 @@ def test_quantize_q8k_bit_exact(K):
         assert np.array_equal(out.bsums[r].cpu().numpy(), bs), r
 
 
-@pytest.mark.parametrize("cols", [4, 1536, 2048, 5120])
+@pytest.mark.parametrize("cols", [4, 1536, 2048, 5120, 1540, 1538, 3])
 def test_rmsnorm_quant_bit_exact(K, cols):
     rng = np.random.default_rng(cols)
     rows = 9
@@ -334,3 +334,19 @@ def test_wide_decode_attention_matches_oracle(K, n_rows):
     positions = rng.integers(0, 1200, n_rows).tolist()
     lengths = [p + 1 for p in positions]
     _attention_case(K, rng, 28, 4, 128, lengths, list(enumerate(positions)))
+
+
+@pytest.mark.parametrize("cols", [1028, 1030, 5])
+def test_swiglu_f32_ragged_rows(K, cols):
+    """Rows whose length leaves a partial 8-value group (the element-wise tail)
+    or is not a multiple of 4 (no 16-byte vectors at all)."""
+    rng = np.random.default_rng(cols)
+    g = rng.normal(0, 4, (3, cols)).astype(np.float32)
+    u = rng.normal(0, 2, (3, cols)).astype(np.float32)
+    out = torch.empty((3, cols), dtype=torch.float32, device="cuda")
+    K.swiglu_quant(torch.from_numpy(g).cuda(), torch.from_numpy(u).cuda(), out_f32=out)
+    torch.cuda.synchronize()
+    L = ob.lib()
+    ref = np.array([[L.orc_silu_mul(float(a), float(b)) for a, b in zip(gr, ur)] for gr, ur in zip(g, u)],
+                   dtype=np.float32)
+    assert np.array_equal(out.cpu().numpy().view(np.uint32), ref.view(np.uint32))
