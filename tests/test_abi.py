@@ -141,6 +141,7 @@ CGO_SIDE = r"""
 
 #include "jfb/jfb_engine.h"
 #include "jfb/jfb_model.h"
+#include "jfb/jfb_stagewire.h"
 
 /* what the cgo stubs of the integration guide touch, written in C */
 int open_stage(const char * pkg, uint32_t start, uint32_t end, int device, jfb_engine ** eng) {
@@ -157,6 +158,15 @@ int import_gguf(const char * src, const char * dst) {
     jfb_import_report rep;
     jfb_status st = jfb_import_gguf(src, dst, &rep);
     return st.code != JFB_STATUS_OK ? (int) st.message[0] : 0;
+}
+
+int call_inbox(jfb_frame_channel * ch, const void * head, uint64_t head_len, const void * frame, uint64_t len,
+               uint32_t timeout_ms) {
+    int32_t status = 0, is_frame = 0;
+    const uint8_t * reply = NULL;
+    uint64_t n = 0;
+    jfb_status st = jfb_frame_channel_call(ch, head, head_len, frame, len, timeout_ms, &status, &is_frame, &reply, &n);
+    return st.code != JFB_STATUS_OK ? (int) st.message[0] : (int) status + is_frame + (int) n + (reply != NULL);
 }
 """
 
