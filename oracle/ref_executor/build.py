@@ -75,6 +75,7 @@ def build(force: bool = False) -> Path | None:
            str(src / "adapters" / "native_stage_executor.cpp"),
            str(ref / "runtime" / "inference" / "stage.cpp"),
            str(ref / "runtime" / "inference" / "token_payload.cpp"),
+           str(ref / "runtime" / "pipeline_parallel" / "continuous_batching_executor.cpp"),
            str(HERE / "replay.cpp"),
            f"-L{lib}", "-ljfb", "-Wl,-rpath,$ORIGIN/../../jetsonfabric_b200/lib", "-o", str(tmp)]
     subprocess.run(cmd, check=True, cwd=REPO)

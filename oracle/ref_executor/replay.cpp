@@ -11,12 +11,18 @@
 // two-stage 0-1 / 1-2 split with its activation handoff, and an oversized
 // activation shape rejected as invalid input. It then checks execute_batch:
 // three sessions decoded in one batched engine pass, with an unknown session,
-// a duplicate session and a wrong decode step rejected per input.
+// a duplicate session and a wrong decode step rejected per input. Last, the
+// reference's ContinuousBatchingExecutor coalesces three concurrent decode
+// steps into one execute_batch call.
 //
 // Test infrastructure: built by oracle/ref_executor/build.py into
 // oracle/_ref/ only when the reference sources are present.
 #include "adapters/native_stage_executor.hpp"
 #include "inference/token_payload.hpp"
+#include "pipeline_parallel/continuous_batching_executor.hpp"
+
+#include <atomic>
+#include <thread>
 
 #include <cstdint>
 #include <iostream>
@@ -190,6 +196,61 @@ void batched(const std::string & path) {
     for (const inf::ExecutionResult & r : ex.execute_batch(batch)) check(!r.ok, "capacity 2 is exhausted after one decode");
 }
 
+// Forwards to the native executor and records the batches it is handed.
+class CountingExecutor final : public inf::Executor {
+public:
+    explicit CountingExecutor(std::unique_ptr<NativeStageExecutor> inner) : inner_(std::move(inner)) {}
+    inf::ExecutionResult execute(const inf::StageInput & in) const override { return inner_->execute(in); }
+    std::vector<inf::ExecutionResult> execute_batch(const std::vector<inf::StageInput> & ins) const override {
+        std::size_t seen = largest.load();
+        while (ins.size() > seen && !largest.compare_exchange_weak(seen, ins.size())) {
+        }
+        return inner_->execute_batch(ins);
+    }
+    void close_session(const std::string & id) const override { inner_->close_session(id); }
+    void rollback_session(const std::string & id, int n) const override { inner_->rollback_session(id, n); }
+    mutable std::atomic<std::size_t> largest{0};
+
+private:
+    std::unique_ptr<NativeStageExecutor> inner_;
+};
+
+// The reference's ContinuousBatchingExecutor (continuous_batching_executor.cpp:
+// 44-127) in front of the native executor, as the worker builds it once the
+// decode_batch_size == 1 check is lifted: three sessions' decode steps sent
+// concurrently are coalesced into one execute_batch call, which the native
+// executor serves as one batched engine pass.
+void continuous_batching(const std::string & path) {
+    auto eng = engine(path);
+    const int layers = int(eng->model_info().layer_count);
+    auto native_ex = std::make_unique<NativeStageExecutor>(NativeStageConfig{
+        .engine = eng, .tokenizer = std::make_shared<FixtureTokens>(), .ctx_size = 16,
+        .position = {.index = 0, .count = 1}, .layers = {.start = 0, .end = layers}});
+    auto counting = std::make_unique<CountingExecutor>(std::move(native_ex));
+    CountingExecutor * probe = counting.get();
+    using jetsonfabric::runtime::pipeline_parallel::ContinuousBatchingConfig;
+    using jetsonfabric::runtime::pipeline_parallel::ContinuousBatchingExecutor;
+    ContinuousBatchingExecutor cb(std::move(counting),
+                                  ContinuousBatchingConfig{.max_batch_size = 3, .max_wait = std::chrono::seconds(2)});
+    const char * names[3] = {"cb0", "cb1", "cb2"};
+    std::vector<inf::StageInput> decodes;
+    for (const char * n : names) {
+        const inf::StageInput pre = prefill_request(n, layers, 0, 1);
+        check_token_seven(cb.execute(pre), std::string("batching prefill ") + n);
+        decodes.push_back(decode_request(pre, 1, inf::sampled_token_payload(7)));
+    }
+    std::vector<inf::ExecutionResult> results(decodes.size());
+    {
+        std::vector<std::jthread> callers;
+        for (std::size_t i = 0; i < decodes.size(); ++i) {
+            callers.emplace_back([&, i] { results[i] = cb.execute(decodes[i]); });
+        }
+    }
+    for (const inf::ExecutionResult & r : results) check_token_seven(r, "coalesced decode");
+    check(probe->largest.load() == decodes.size(), "the three decode steps reached the engine as one batch");
+    for (const char * n : names) cb.close_session(n);
+}
+
 }  // namespace
 
 int main(int argc, char ** argv) {
@@ -198,6 +259,7 @@ int main(int argc, char ** argv) {
         single_stage(argv[1]);
         two_stages(argv[1]);
         batched(argv[1]);
+        continuous_batching(argv[1]);
         std::cout << "replay ok\n";
         return 0;
     } catch (const std::exception & e) {

@@ -7,7 +7,8 @@ against include/jetsonfabric/native_inference.hpp and links libjfb.so. The
 GPU test runs the resulting replay of the reference's executor test
 (runtime/adapters/native_stage_executor_test.cpp:85-235) on the reference's
 2-layer fixture package, on the CUDA backend, plus a batched decode through
-execute_batch.
+execute_batch, and the reference's ContinuousBatchingExecutor coalescing
+three concurrent decode steps into one execute_batch call.
 """
 from __future__ import annotations
 
