@@ -60,6 +60,46 @@ def prepare_sources(ref: Path) -> Path:
     return src
 
 
+CONFIG_BINARIES = {"reference": OUT / "worker_config_reference", "lifted": OUT / "worker_config_lifted"}
+# the native engine's single-decode restriction in the reference worker
+# (runtime/worker/config.cpp:159-162), removed in the "lifted" build
+DECODE_BATCH_CHECK = (
+    "        if (cfg.decode_batch_size != 1) {\n"
+    "            throw std::invalid_argument(\n"
+    "                \"native serving currently requires --decode-batch-size 1\"\n"
+    "            );\n"
+    "        }\n"
+)
+
+
+def build_config_checks(force: bool = False) -> dict | None:
+    """The reference worker's config validation around config_check.cpp, as
+    it is and with the decode-batch restriction lifted."""
+    ref = reference_root()
+    if ref is None:
+        return CONFIG_BINARIES if all(p.exists() for p in CONFIG_BINARIES.values()) else None
+    inputs = [HERE / "config_check.cpp", HERE / "build.py"]
+    if not force and all(p.exists() and all(p.stat().st_mtime > i.stat().st_mtime for i in inputs)
+                         for p in CONFIG_BINARIES.values()):
+        return CONFIG_BINARIES
+    rt = ref / "runtime"
+    lifted_dir = OUT / "executor" / "worker"
+    lifted_dir.mkdir(parents=True, exist_ok=True)
+    text = (rt / "worker" / "config.cpp").read_text()
+    if text.count(DECODE_BATCH_CHECK) != 1:
+        raise RuntimeError("the reference worker's decode-batch check was not found exactly once")
+    (lifted_dir / "config.cpp").write_text(text.replace(DECODE_BATCH_CHECK, ""))
+    deps = [str(rt / "protocol" / "execution_mode.cpp"), str(rt / "pipeline_parallel" / "stage_assignment.cpp"),
+            str(rt / "tensor_parallel" / "device_mesh.cpp")]
+    for kind, config_src in (("reference", rt / "worker" / "config.cpp"), ("lifted", lifted_dir / "config.cpp")):
+        target = CONFIG_BINARIES[kind]
+        tmp = target.with_suffix(".tmp")
+        subprocess.run(["g++", "-std=c++20", "-O1", "-Wall", f"-I{rt}", str(HERE / "config_check.cpp"),
+                        str(config_src)] + deps + ["-o", str(tmp)], check=True, cwd=REPO)
+        os.replace(tmp, target)
+    return CONFIG_BINARIES
+
+
 def build(force: bool = False) -> Path | None:
     ref = reference_root()
     if ref is None:
@@ -85,3 +125,4 @@ def build(force: bool = False) -> Path | None:
 
 if __name__ == "__main__":
     print(build(force=True))
+    print(build_config_checks(force=True))

@@ -47,3 +47,23 @@ def test_reference_executor_replay_on_cuda(fixture_package):
     r = subprocess.run([str(binary), str(fixture_package)], capture_output=True, text=True, timeout=300)
     assert r.returncode == 0, r.stderr
     assert "replay ok" in r.stdout
+
+
+@pytest.mark.parametrize("args,reference,lifted", [
+    (["4", "8", "cuda"], "rejected: native serving currently requires --decode-batch-size 1", "accepted"),
+    (["1", "8", "cuda"], "accepted", "accepted"),
+    (["9", "8", "cuda"], "rejected: --decode-batch-size must be between 1 and --parallel-sessions", None),
+    (["4", "8", "rocm"], "rejected: native compute backend must be cpu or cuda", None),
+])
+def test_worker_config_lift(args, reference, lifted):
+    """The reference worker's own config validation (runtime/worker/
+    config.cpp), compiled as it is and with the native engine's
+    decode_batch_size == 1 check removed: only that restriction changes, every
+    other check stays."""
+    binaries = executor_build.build_config_checks()
+    if binaries is None:
+        pytest.skip("the reference tree is not on this machine and no prebuilt config checks exist")
+    out = {k: subprocess.run([str(p)] + args, capture_output=True, text=True, check=True).stdout.strip()
+           for k, p in binaries.items()}
+    assert out["reference"] == reference
+    assert out["lifted"] == (lifted if lifted is not None else reference)
