@@ -24,10 +24,14 @@ own default batch shapes.
                32 prompt tokens, 8 greedy tokens) against the CPU oracle
     cpu_baseline  the CPU oracle (this repository's restatement of the
                reference's GGML-CPU path) on that sample, with its prefill
-               and decode token rates
+               and decode token rates; for --preset 1.5b (the configuration
+               the reference times end to end on its CPU backend) the whole
+               workload once instead
 
 --impl reference runs the CPU oracle on the host cores instead (the
-reference's own native engine needs GGML, which cannot be built here).
+reference's own native engine needs GGML, which cannot be built here): each
+step the bounded sample, or with --cpu-full (the default for --preset 1.5b)
+the whole workload.
 
 With torchrun (N > 1) the same workload runs as an N-stage pipeline (one
 process and GPU per contiguous layer range, jetsonfabric_b200/pipeline.py):
