@@ -46,7 +46,7 @@ __host__ __device__ inline uint32_t crc_mulmod(uint32_t a, uint32_t b) {
 }
 
 // x^(8 n) mod P
-__device__ inline uint32_t crc_xpow_bytes(uint64_t n, const CrcPowers & pw) {
+__host__ __device__ inline uint32_t crc_xpow_bytes(uint64_t n, const CrcPowers & pw) {
     uint32_t r = 0x80000000u;  // x^0
     for (int j = 0; n != 0 && j < kCrcPowers; ++j, n >>= 1) {
         if (n & 1u) r = crc_mulmod(r, pw.x[j]);
@@ -95,14 +95,23 @@ __global__ void __launch_bounds__(kCrcThreads) crc_chunks_kernel(const uint8_t *
     items[item] = s;
 }
 
+// Per join level, computed on the host: x^(8 item_bytes 2^s) for the
+// tree's eight steps (every right-hand subtree but the one holding the
+// ragged last item is that long), and 0xFFFFFFFF * x^(8 total) for the finish.
+struct CrcJoinPowers {
+    uint32_t step[8];
+    uint32_t fin;
+};
+
 // Joins `count` consecutive items (each `item_bytes` long, the last one
 // `last_bytes`) 256 at a time: output item b is the register after items
-// [256 b, 256 b + 256). With `finish`, the single output becomes the CRC of the
-// `total` bytes and is written to `crc_out`.
+// [256 b, 256 b + 256). With `finish`, the single output becomes the CRC of
+// all the bytes and is written to `crc_out`.
 __global__ void __launch_bounds__(kCrcThreads) crc_join_kernel(const uint32_t * __restrict__ in, uint64_t count,
                                                              uint64_t item_bytes, uint64_t last_bytes,
-                                                             uint32_t * __restrict__ out, CrcPowers pw, int finish,
-                                                             uint64_t total, uint32_t * __restrict__ crc_out) {
+                                                             uint32_t * __restrict__ out, CrcPowers pw,
+                                                             CrcJoinPowers jp, int finish,
+                                                             uint32_t * __restrict__ crc_out) {
     __shared__ uint32_t reg[kCrcThreads];
     __shared__ uint64_t len[kCrcThreads];
     pdl_trigger();
@@ -111,18 +120,19 @@ __global__ void __launch_bounds__(kCrcThreads) crc_join_kernel(const uint32_t * 
     reg[threadIdx.x] = i < count ? in[i] : 0u;
     len[threadIdx.x] = i < count ? (i + 1 == count ? last_bytes : item_bytes) : 0u;
     __syncthreads();
-    for (int step = 1; step < kCrcThreads; step *= 2) {
+    for (int s = 0, step = 1; step < kCrcThreads; ++s, step *= 2) {
         if ((threadIdx.x % (2 * step)) == 0) {
             const uint64_t lb = len[threadIdx.x + step];
             if (lb != 0) {
-                reg[threadIdx.x] = crc_mulmod(reg[threadIdx.x], crc_xpow_bytes(lb, pw)) ^ reg[threadIdx.x + step];
+                const uint32_t xp = lb == (item_bytes << s) ? jp.step[s] : crc_xpow_bytes(lb, pw);
+                reg[threadIdx.x] = crc_mulmod(reg[threadIdx.x], xp) ^ reg[threadIdx.x + step];
                 len[threadIdx.x] += lb;
             }
         }
         __syncthreads();
     }
     if (threadIdx.x == 0) {
-        if (finish) *crc_out = ~(reg[0] ^ crc_mulmod(0xFFFFFFFFu, crc_xpow_bytes(total, pw)));
+        if (finish) *crc_out = ~(reg[0] ^ jp.fin);
         else out[blockIdx.x] = reg[0];
     }
 }
@@ -226,8 +236,11 @@ extern "C" jfb_status jfb_crc32(const void * data, uint64_t n, uint32_t * crc_ou
         const uint64_t blocks = (items + kCrcThreads - 1) / kCrcThreads;
         uint32_t * out = in + items;
         const int finish = blocks == 1 ? 1 : 0;
+        CrcJoinPowers jp;
+        for (int k = 0; k < 8; ++k) jp.step[k] = crc_xpow_bytes(item_bytes << k, pw);
+        jp.fin = finish ? crc_mulmod(0xFFFFFFFFu, crc_xpow_bytes(n, pw)) : 0u;
         e = launch_k(crc_join_kernel, dim3(uint32_t(blocks)), dim3(kCrcThreads), 0, s, static_cast<const uint32_t *>(in),
-                     items, item_bytes, last_bytes, out, pw, finish, n, crc_out);
+                     items, item_bytes, last_bytes, out, pw, jp, finish, crc_out);
         if (finish) break;
         // the joined items: full ones of 256 items, the last of the remainder
         const uint64_t full_bytes = item_bytes * kCrcThreads;
