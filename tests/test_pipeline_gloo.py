@@ -222,3 +222,27 @@ def test_stagewire_frame_corruption_is_detected(small_q4k_package, tmp_path):
     errs = {p.name: p.read_text() for p in tmp_path.glob("*.err")}
     assert list(errs) == ["tokens.json.rank1.err"], errs
     assert errs["tokens.json.rank1.err"].startswith("ChecksumMismatch")
+
+
+def test_eight_stage_framed_pipeline(tmp_path):
+    """Eight gloo ranks, one layer each, eight micro-batches, every message a
+    Stagewire frame: the schedule the 8-GPU benchmark runs, checked against the
+    chained stages."""
+    import torch.multiprocessing as mp
+
+    from jetsonfabric_b200 import jfm
+
+    package = tmp_path / "eight.jfm"
+    jfm.write_synthetic_package(package, layer_count=8, embedding_length=256, head_count=2, kv_head_count=1,
+                                feed_forward_length=512, vocabulary_size=512, context_length=128, seed=11,
+                                draw_norms=True, draw_biases=True)
+    rng = np.random.default_rng(8)
+    prompts = [rng.integers(0, 512, n).tolist() for n in (5, 3, 6, 2, 4, 7, 3, 5)]
+    steps = 4
+    out_path = tmp_path / "tokens.json"
+    os.environ.setdefault("OMP_NUM_THREADS", "1")
+    mp.spawn(_rank_main, args=(8, _free_port(), str(package), prompts, 8, steps, str(out_path), True),
+             nprocs=8, join=True)
+    assert not list(tmp_path.glob("*.err"))
+    got = {int(k): v for k, v in json.loads(out_path.read_text()).items()}
+    assert got == _chained_reference(package, prompts, 8, steps)
