@@ -736,7 +736,7 @@ class StagewireLink:
                 # the expected prefix passed every rule when it was built, and
                 # its checksum field matches the received payload
                 continue
-            # anything else: the decoder's own verdict, then the mismatch
+            # anything else: the decoder's own error first, then the mismatch
             meta_len, payload_len = parse_prefix(pre)
             if HEADER_SIZE + meta_len != self.P:
                 raise StagewireError(f"frame {k}: metadata does not fill the {self.P}-byte prefix")
