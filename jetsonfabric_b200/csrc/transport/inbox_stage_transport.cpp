@@ -261,8 +261,16 @@ bool InboxStageServer::serve_one(std::chrono::milliseconds wait) {
         const std::string body = json_error_body(code, message);
         check(jfb_frame_channel_reply(channel_, status, 0, body.data(), body.size(), nullptr, 0));
     };
+    // a response the codec refuses to encode is answered as a 502 error body,
+    // so the caller never waits for a reply that will not come
     const auto reply_frame = [&](int status, protocol::StageResponse response) {
-        protocol::EncodedStageFrame out = protocol::encode_stage_response_frame(std::move(response));
+        protocol::EncodedStageFrame out;
+        try {
+            out = protocol::encode_stage_response_frame(std::move(response));
+        } catch (const std::exception & error) {
+            reply_json(502, "invalid_stage_response", error.what());
+            return;
+        }
         check(jfb_frame_channel_reply(channel_, status, 1, out.prefix.data(), out.prefix.size(), out.payload.data(),
                                       out.payload.size()));
     };
