@@ -12,7 +12,6 @@ Every CUDA file is compiled for sm_100a only
 from __future__ import annotations
 
 import os
-import shutil
 import subprocess
 import sys
 from pathlib import Path
