@@ -61,10 +61,43 @@ __host__ inline CrcPowers crc_powers() {
     return pw;
 }
 
-// Register value after feeding each `chunk`-byte piece from register 0.
+// Per join level, computed on the host: x^(8 item_bytes 2^s) for the
+// tree's eight steps (every right-hand subtree but the one holding the
+// ragged last item is that long), and 0xFFFFFFFF * x^(8 total) for the finish.
+struct CrcJoinPowers {
+    uint32_t step[8];
+    uint32_t fin;
+};
+
+// Joins the block's 256 registers reg[] (item lengths len[], all
+// `item_bytes` but a ragged last one, 0 past the end) in a tree; reg[0] ends
+// as the register after all of them. Every thread of the block calls it.
+__device__ inline void crc_join_block(uint32_t * reg, uint64_t * len, uint64_t item_bytes, const CrcPowers & pw,
+                                      const CrcJoinPowers & jp) {
+    __syncthreads();
+    for (int s = 0, step = 1; step < kCrcThreads; ++s, step *= 2) {
+        if ((threadIdx.x % (2 * step)) == 0) {
+            const uint64_t lb = len[threadIdx.x + step];
+            if (lb != 0) {
+                const uint32_t xp = lb == (item_bytes << s) ? jp.step[s] : crc_xpow_bytes(lb, pw);
+                reg[threadIdx.x] = crc_mulmod(reg[threadIdx.x], xp) ^ reg[threadIdx.x + step];
+                len[threadIdx.x] += lb;
+            }
+        }
+        __syncthreads();
+    }
+}
+
+// Feeds each `chunk`-byte piece from register 0 (one per thread), then joins
+// the block's 256 pieces: out[b] is the register after the block's bytes, or,
+// with `finish` (a single block), the CRC of all `n` bytes in *crc_out.
 __global__ void __launch_bounds__(kCrcThreads) crc_chunks_kernel(const uint8_t * __restrict__ data, uint64_t n,
-                                                               uint64_t chunk, uint32_t * __restrict__ items) {
+                                                               uint64_t chunk, uint32_t * __restrict__ out,
+                                                               CrcPowers pw, CrcJoinPowers jp, int finish,
+                                                               uint32_t * __restrict__ crc_out) {
     __shared__ uint32_t table[256];
+    __shared__ uint32_t reg[kCrcThreads];
+    __shared__ uint64_t len[kCrcThreads];
     pdl_trigger();
     for (uint32_t i = threadIdx.x; i < 256; i += blockDim.x) {
         uint32_t c = i;
@@ -75,33 +108,34 @@ __global__ void __launch_bounds__(kCrcThreads) crc_chunks_kernel(const uint8_t *
     pdl_wait();
     const uint64_t item = uint64_t(blockIdx.x) * kCrcThreads + threadIdx.x;
     const uint64_t begin = item * chunk;
-    if (begin >= n) return;
-    const uint64_t end = begin + chunk < n ? begin + chunk : n;
     uint32_t s = 0;
-    uint64_t i = begin;
-    // 16-byte loads where the address allows (payload buffers are 256-byte aligned)
-    if ((reinterpret_cast<uintptr_t>(data + i) & 15u) == 0) {
-        for (; i + 16 <= end; i += 16) {
-            const uint4 v = *reinterpret_cast<const uint4 *>(data + i);
-            const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    uint64_t bytes = 0;
+    if (begin < n) {
+        const uint64_t end = begin + chunk < n ? begin + chunk : n;
+        bytes = end - begin;
+        uint64_t i = begin;
+        // 16-byte loads where the address allows (payload buffers are 256-byte aligned)
+        if ((reinterpret_cast<uintptr_t>(data + i) & 15u) == 0) {
+            for (; i + 16 <= end; i += 16) {
+                const uint4 v = *reinterpret_cast<const uint4 *>(data + i);
+                const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
+                for (int k = 0; k < 4; ++k) {
 #pragma unroll
-                for (int b = 0; b < 4; ++b) s = (s >> 8) ^ table[(s ^ (w[k] >> (8 * b))) & 0xffu];
+                    for (int b = 0; b < 4; ++b) s = (s >> 8) ^ table[(s ^ (w[k] >> (8 * b))) & 0xffu];
+                }
             }
         }
+        for (; i < end; ++i) s = (s >> 8) ^ table[(s ^ data[i]) & 0xffu];
     }
-    for (; i < end; ++i) s = (s >> 8) ^ table[(s ^ data[i]) & 0xffu];
-    items[item] = s;
+    reg[threadIdx.x] = s;
+    len[threadIdx.x] = bytes;
+    crc_join_block(reg, len, chunk, pw, jp);
+    if (threadIdx.x == 0) {
+        if (finish) *crc_out = ~(reg[0] ^ jp.fin);
+        else out[blockIdx.x] = reg[0];
+    }
 }
-
-// Per join level, computed on the host: x^(8 item_bytes 2^s) for the
-// tree's eight steps (every right-hand subtree but the one holding the
-// ragged last item is that long), and 0xFFFFFFFF * x^(8 total) for the finish.
-struct CrcJoinPowers {
-    uint32_t step[8];
-    uint32_t fin;
-};
 
 // Joins `count` consecutive items (each `item_bytes` long, the last one
 // `last_bytes`) 256 at a time: output item b is the register after items
@@ -119,18 +153,7 @@ __global__ void __launch_bounds__(kCrcThreads) crc_join_kernel(const uint32_t * 
     const uint64_t i = uint64_t(blockIdx.x) * kCrcThreads + threadIdx.x;
     reg[threadIdx.x] = i < count ? in[i] : 0u;
     len[threadIdx.x] = i < count ? (i + 1 == count ? last_bytes : item_bytes) : 0u;
-    __syncthreads();
-    for (int s = 0, step = 1; step < kCrcThreads; ++s, step *= 2) {
-        if ((threadIdx.x % (2 * step)) == 0) {
-            const uint64_t lb = len[threadIdx.x + step];
-            if (lb != 0) {
-                const uint32_t xp = lb == (item_bytes << s) ? jp.step[s] : crc_xpow_bytes(lb, pw);
-                reg[threadIdx.x] = crc_mulmod(reg[threadIdx.x], xp) ^ reg[threadIdx.x + step];
-                len[threadIdx.x] += lb;
-            }
-        }
-        __syncthreads();
-    }
+    crc_join_block(reg, len, item_bytes, pw, jp);
     if (threadIdx.x == 0) {
         if (finish) *crc_out = ~(reg[0] ^ jp.fin);
         else out[blockIdx.x] = reg[0];
@@ -227,20 +250,28 @@ extern "C" jfb_status jfb_crc32(const void * data, uint64_t n, uint32_t * crc_ou
     uint64_t items = (n + chunk - 1) / chunk;
     const uint64_t blocks0 = (items + kCrcThreads - 1) / kCrcThreads;
     if (blocks0 > 0x7fffffffu) return status_error(JFB_STATUS_INVALID_ARGUMENT, "crc32 input is too long");
+    auto join_powers = [&](uint64_t item_bytes, int finish) {
+        CrcJoinPowers jp;
+        for (int k = 0; k < 8; ++k) jp.step[k] = crc_xpow_bytes(item_bytes << k, pw);
+        jp.fin = finish ? crc_mulmod(0xFFFFFFFFu, crc_xpow_bytes(n, pw)) : 0u;
+        return jp;
+    };
+    // chunks and their first join in one launch; one block finishes at once
+    const int finish0 = blocks0 == 1 ? 1 : 0;
     e = launch_k(crc_chunks_kernel, dim3(uint32_t(blocks0)), dim3(kCrcThreads), 0, s, static_cast<const uint8_t *>(data),
-                 n, chunk, buf);
-    uint64_t item_bytes = chunk, last_bytes = n - (items - 1) * chunk;
+                 n, chunk, buf, pw, join_powers(chunk, finish0), finish0, crc_out);
+    if (e != cudaSuccess) return status_error(JFB_STATUS_CUDA_ERROR, "jfb_crc32: %s", cudaGetErrorString(e));
+    if (finish0) return launch_status("jfb_crc32");
+    items = blocks0;
+    uint64_t item_bytes = chunk * kCrcThreads, last_bytes = n - (blocks0 - 1) * chunk * kCrcThreads;
     uint32_t * in = buf;
     // each level joins 256 items; the last level (one block) finishes
     while (e == cudaSuccess) {
         const uint64_t blocks = (items + kCrcThreads - 1) / kCrcThreads;
         uint32_t * out = in + items;
         const int finish = blocks == 1 ? 1 : 0;
-        CrcJoinPowers jp;
-        for (int k = 0; k < 8; ++k) jp.step[k] = crc_xpow_bytes(item_bytes << k, pw);
-        jp.fin = finish ? crc_mulmod(0xFFFFFFFFu, crc_xpow_bytes(n, pw)) : 0u;
         e = launch_k(crc_join_kernel, dim3(uint32_t(blocks)), dim3(kCrcThreads), 0, s, static_cast<const uint32_t *>(in),
-                     items, item_bytes, last_bytes, out, pw, jp, finish, crc_out);
+                     items, item_bytes, last_bytes, out, pw, join_powers(item_bytes, finish), finish, crc_out);
         if (finish) break;
         // the joined items: full ones of 256 items, the last of the remainder
         const uint64_t full_bytes = item_bytes * kCrcThreads;
