@@ -413,3 +413,77 @@ def test_frames_made_here_decode_with_the_reference_decoder():
             assert r[k] == v, (k, r)
     assert not res[good]["ok"] and "checksum" in res[good]["error"]
     assert not res[good + 1]["ok"] and "checksum" in res[good + 1]["error"]
+
+
+class _HostLoopback:
+    """A base link whose sends are the next receives (CPU tensors), with an
+    optional edit applied to a sent frame's bytes."""
+
+    def __init__(self, edit=None):
+        self.q, self.edit = [], edit
+
+    def send_next(self, frame):
+        frame = frame.clone()
+        if self.edit is not None:
+            self.edit(frame)
+        self.q.append(frame)
+
+    send_tokens = send_next
+
+    def recv_prev(self, frame):
+        frame.copy_(self.q.pop(0))
+
+    recv_tokens = recv_prev
+
+    def flush(self):
+        pass
+
+
+class _HostCodec:
+    hidden = 16
+
+    def encode(self, activations, out=None):
+        import torch
+
+        out.copy_(torch.from_numpy(np.asarray(activations, dtype=np.float32).astype(np.float16)))
+        return out
+
+
+def _plan():
+    return sw.FramePlan(model_id="m", stage_layers=[(0, 1), (1, 2)], batches=[[0]], prompt_lengths=[3], steps=2,
+                        hidden=16)
+
+
+def test_host_link_round_trip_and_schedule_limits():
+    base = _HostLoopback()
+    tx, rx = sw.StagewireLink(base, 0, _plan()), sw.StagewireLink(base, 1, _plan())
+    stage = _HostCodec()
+    for step, rows in ((0, 3), (1, 1)):
+        act = np.random.default_rng(step).normal(0, 1, (rows, 16)).astype(np.float32)
+        tx.send_activation(stage, act)
+        got = rx.recv_activation(stage, rows)
+        assert np.array_equal(got.numpy(), act.astype(np.float16))
+    with pytest.raises(sw.StagewireError, match="more frames sent"):
+        tx.send_activation(stage, np.zeros((1, 16), np.float32))
+    tx.flush()
+    rx.flush()
+    # a run that stops early is reported at flush
+    tx.send_activation(stage, np.zeros((3, 16), np.float32))
+    with pytest.raises(sw.StagewireError, match="schedule ended after 1 of 2 sends"):
+        tx.flush()
+
+
+def test_host_link_rejects_metadata_that_is_not_the_schedules():
+    """A frame whose checksum holds but whose metadata names another step
+    (a digit of decode_step changed in flight) fails verification."""
+    def edit(frame):
+        raw = bytes(frame[:1024].numpy())
+        at = raw.index(b'"decode_step":0') + len(b'"decode_step":')
+        frame[at] = ord("7")
+
+    base = _HostLoopback(edit)
+    tx, rx = sw.StagewireLink(base, 0, _plan()), sw.StagewireLink(base, 1, _plan())
+    tx.send_activation(_HostCodec(), np.ones((3, 16), np.float32))
+    rx.recv_activation(_HostCodec(), 3)
+    with pytest.raises(sw.StagewireError, match="differs from the schedule"):
+        rx.verify()
